@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Vision-tower crop-batch throughput on 1..8 B200.
+
+A step = 1040 crops (80 frames x 13) through the 27-block moondream2-style tower of config 1 (patch-
+embed, 27 pre-LN blocks, post-LN), sharded evenly over the ranks, each rank working in chunks of
+130 crops, with the 729 x 1152 bf16 features all-gathered over NVLink by NCCL (async, overlapped with
+the next chunk).  Total work is fixed as N grows ("scaling": "strong").  Synthetic seeded inputs:
+pixels U[-1, 1], weights N(0, 0.02) (no checkpoints offline).
+
+value  : crops/s of the whole job with the pixels already in HBM (CUDA events, max over ranks).
+e2e    : crops/s through the public host-buffer API (strix_halo_maxx_b200.multigpu.HostPipeline):
+         pinned host pixels -> H2D -> towers -> all-gather -> D2H of this rank's features, every step.
+roofline: the tcgen05 GEMM kernel (all its launches in the timed region, CUDA events on the launching
+         stream): achieved = algorithmic GEMM FLOPs / summed launch time, against the measured sustained
+         cuBLAS bf16 peak (MEASURED_PEAKS.json).
+cpu_baseline: the CPU fp32 oracle (a port of md2fast.FastMD2._vision) on one crop, rank 0 at N=1.
+--impl reference: the same CPU oracle as the reference arm, a bounded sample per step.
+
+Run:  python bench.py [--gpus N --steps K --warmup W]   (N > 1 under torchrun, one rank per GPU)
+"""
+import argparse
+import contextlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "vision-tower crops/sec and ms per 13-crop frame at 1/2/4/8 B200; % bf16 TC peak"
+UNIT = "crops/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="vt", choices=["vt", "reference"])
+    ap.add_argument("--crops", type=int, default=1040)
+    ap.add_argument("--mb", type=int, default=130, help="crops per chunk and rank")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-frame", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops_sustained", 1400.0), d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.idx), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        self.f.flush()
+
+    def summary(self):
+        rows = []
+        for line in open(self.f.name):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) >= 9 and p[1].replace(".", "").isdigit():
+                rows.append(p)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+class OpTimer:
+    """CUDA events around every op launch of the tower (on the launching stream)."""
+
+    def __init__(self):
+        self.rec = []
+
+    @contextlib.contextmanager
+    def __call__(self, name, flops):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        self.rec.append((name, flops, s, e))
+
+    def summary(self):
+        out = {}
+        for name, flops, s, e in self.rec:
+            d = out.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0})
+            d["launches"] += 1
+            d["ms"] += s.elapsed_time(e)
+            d["flops"] += flops
+        return out
+
+
+def cpu_oracle_rate(W, cfg, n_crops, reps):
+    """Crops/s of the CPU fp32 oracle (port of FastMD2._vision's tower) on all host threads."""
+    from oracle import tower_ref
+    from strix_halo_maxx_b200.weights import crop_pixels
+    torch.set_num_threads(os.cpu_count() or 1)
+    pix = torch.from_numpy(crop_pixels(n_crops, cfg, seed=1))
+    tower_ref.tower(pix, W, cfg)             # warm-up
+    ts = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        tower_ref.tower(pix, W, cfg)
+        ts.append(time.perf_counter() - t)
+    return n_crops / statistics.median(ts), torch.get_num_threads()
+
+
+def run_reference(a):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    from strix_halo_maxx_b200.config import TOWER
+    from strix_halo_maxx_b200.weights import tower_weights, crop_pixels
+    from oracle import tower_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    W = tower_weights(TOWER, seed=0, projection=False)
+    pix = torch.from_numpy(crop_pixels(1, TOWER, seed=1))
+    for _ in range(a.warmup):
+        tower_ref.tower(pix, W, TOWER)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        tower_ref.tower(pix, W, TOWER)
+    dt = time.perf_counter() - t0
+    v = a.steps / dt
+    sample = f"1 crop per step (27 blocks + post-LN, fp32 torch CPU oracle, port of md2fast.FastMD2._vision) of the {a.crops}-crop workload"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": 1000 * dt / a.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1] pixels, N(0,0.02) weights)",
+        "config": {"workload": f"config 4 ({a.crops} crops through the 27-block tower), bounded CPU sample",
+                   "crops_per_step": 1},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def run_vt(a):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from strix_halo_maxx_b200.config import TOWER
+    from strix_halo_maxx_b200.weights import tower_weights, crop_pixels
+    from strix_halo_maxx_b200.tower import VisionTower
+    from strix_halo_maxx_b200.multigpu import local_crop_ids, encode_sharded, HostPipeline
+    from strix_halo_maxx_b200 import ops
+    from strix_halo_maxx_b200._lib import device_status
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
+                                device_id=dev)
+    cfg = TOWER
+    mb = min(a.mb, a.crops // world)
+    ids = local_crop_ids(a.crops, world, rank, mb)
+    n_local = len(ids)
+
+    W = tower_weights(cfg, seed=0, projection=not a.no_frame)
+    tower = VisionTower(W, cfg, device=dev)
+
+    # this rank's crops, chunk by chunk (ids are runs of mb consecutive crops)
+    pix_host = torch.empty(n_local, 3, cfg.img, cfg.img, dtype=torch.bfloat16).pin_memory()
+    for j in range(n_local // mb):
+        pix_host[j * mb:(j + 1) * mb] = torch.from_numpy(crop_pixels(mb, cfg, seed=1, first=ids[j * mb])).to(torch.bfloat16)
+    pix_dev = pix_host.to(dev)
+    feats_all = torch.empty(a.crops, cfg.ntok, cfg.width, dtype=torch.bfloat16, device=dev)
+    local_out = torch.empty(n_local, cfg.ntok, cfg.width, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    fwd = lambda p, out: tower.forward(p, out=out)   # noqa: E731
+
+    def step():
+        encode_sharded(fwd, pix_dev, feats_all, local_out, mb)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    device_status(clear=True)
+
+    # ---------------- timed: device-resident inputs
+    timer = OpTimer()
+    tower.op_timer = timer
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    gpu_index = phys[local] if len(phys) > local and phys[local].strip().isdigit() else str(local)
+    l0 = ops.LAUNCHES
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(gpu_index) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = ops.LAUNCHES - l0
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    tower.op_timer = None
+    ops_summary = timer.summary()
+    clocks = clk.summary()
+    status = device_status(clear=True)
+    value = a.crops * a.steps / (ms / 1000.0)
+
+    gemm_ms = sum(v["ms"] for k, v in ops_summary.items() if k.startswith("gemm_"))
+    gemm_fl = sum(v["flops"] for k, v in ops_summary.items() if k.startswith("gemm_"))
+    gemm_n = sum(v["launches"] for k, v in ops_summary.items() if k.startswith("gemm_"))
+    sustained, burst, hbm, src = peaks()
+    achieved = gemm_fl / (gemm_ms / 1000.0) / 1e12
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
+    total_ms = sum(v["ms"] for v in ops_summary.values())
+    breakdown = {k: {"launches": v["launches"], "ms_per_step": v["ms"] / a.steps,
+                     "share": v["ms"] / total_ms if total_ms else None,
+                     "tflops": (v["flops"] / (v["ms"] / 1000.0) / 1e12) if v["flops"] else None}
+                 for k, v in sorted(ops_summary.items())}
+
+    # ---------------- e2e: public host-buffer API, copies inside the timed region
+    pipe = HostPipeline(tower, n_local, mb)
+    out_host = torch.empty(n_local, cfg.ntok, cfg.width, dtype=torch.bfloat16).pin_memory()
+    pipe.run(pix_host, out_host, feats_all)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(a.steps):
+        pipe.run(pix_host, out_host, feats_all)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    e2e = {"value": a.crops * a.steps / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes(),
+           "d2h_bytes_per_step": pipe.d2h_bytes(), "api": "strix_halo_maxx_b200.multigpu.HostPipeline.run"}
+    # the e2e output must equal the device-resident path
+    e2e_ok = bool(torch.equal(out_host[:mb].to(dev), (local_out if world > 1 else feats_all)[:mb]))
+
+    # ---------------- config 2 latency: one 13-crop frame (tower + combine + projection)
+    frame_ms = None
+    if not a.no_frame:
+        crops = pix_dev[:13] if n_local >= 13 else pix_dev[:1].expand(13, -1, -1, -1).contiguous()
+        for _ in range(3):
+            tower.frame(crops)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(10):
+            tower.frame(crops)
+        g1.record()
+        torch.cuda.synchronize()
+        frame_ms = g0.elapsed_time(g1) / 10
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        v, cores = cpu_oracle_rate(W, cfg, 1, 2)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": "1 crop (27 blocks + post-LN, fp32 torch CPU oracle = port of md2fast.FastMD2._vision), median of 2 after 1 warm-up"}
+
+    if rank == 0:
+        fl = cfg.flops_per_crop()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded U[-1,1] pixels, N(0,0.02) weights; no checkpoints offline)",
+            "config": {"workload": f"config 4: {a.crops} crops (80 frames x 13) through the 27-block tower of config 1, "
+                                   f"all-gathered [{a.crops},729,1152] bf16", "crops_per_step": a.crops,
+                       "chunk_crops_per_rank": mb, "parallelism": f"dp{world} (crop sharding) + NCCL all-gather",
+                       "l2": "inputs larger than L2 (pixels %.0f MB per step, activations GBs)" % (a.crops * 3 * 378 * 378 * 2 / 1e6)},
+            "ms_per_frame_13crop_throughput": 13 * 1000.0 / value,
+            "ms_per_frame_13crop_latency": frame_ms,
+            "tflops_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12,
+            "frac_of_peak_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12 / (sustained * world),
+            "roofline": {"kernel": "gemm_bf16_tc_kernel (tcgen05, all GEMM launches of the timed region)",
+                         "bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                         "frac": achieved / sustained, "traffic": traffic,
+                         "peak_source": f"{src} bf16_tflops_sustained" + (" of measured" if src == "measured" else " of fallback"),
+                         "launches": gemm_n, "avg_launch_ms": gemm_ms / max(gemm_n, 1)},
+            "kernels": breakdown,
+            "cpu_baseline": cpu,
+            "e2e": e2e, "e2e_matches_device_path": e2e_ok,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_vt(a)
+
+
+if __name__ == "__main__":
+    main()

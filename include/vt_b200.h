@@ -1,0 +1,85 @@
+/* libvt_b200.so -- C ABI of the B200 (sm_100a) vision-tower kernels.
+ *
+ * Conventions (the reference's, moondream/gpu/hgemm.py:21-36, hattn.py:5-16):
+ *   - every function takes the CUDA stream to launch on first (torch's current stream in the Python host)
+ *     and raw device pointers; the caller owns every buffer; nothing is allocated, nothing synchronises
+ *     (except vt_device_status), so the calls can be captured in CUDA graphs;
+ *   - bf16 tensors are passed as uint16_t*; pitches / strides are in elements;
+ *   - return 0 on success, negative on error (-1 unknown variant, -2 shape or alignment, -3 CUDA launch
+ *     error, -4 layout mismatch, -5 tensor-map encode failure), the message in vt_last_error_string().
+ */
+#ifndef VT_B200_H
+#define VT_B200_H
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ABI version of this header (1). */
+int vt_abi_version(void);
+
+/* Message of the last failing call on this host thread. */
+const char* vt_last_error_string(void);
+
+/* Device status word of the current device: bit i set when a kernel's bounded wait gave up at site i
+ * (the kernel then unwinds instead of hanging).  Synchronises the device; clear != 0 resets the word. */
+int vt_device_status(int clear, unsigned int* status);
+
+/* C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias (fp32, may be NULL), optional GELU-tanh applied
+ * after rounding to bf16.  A, W bf16 K-contiguous, pitches multiples of 8, bases 16-byte aligned.
+ * tcgen05/TMEM tiles fed by TMA.
+ * Replaces: bf16gemm_launch, moondream/gpu/hip/i8gemm.hip:534 (called from HLin._run, hgemm.py:160-162);
+ * no cfg / swap / packed arguments: one persistent kernel, weights in the natural (N, K) layout. */
+int vt_gemm_bf16(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
+                 const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu);
+
+/* General GEMM epilogue: out (fp32 when out_f32, else bf16) = A.W^T + bias [+ res], res fp32 (bf16 when
+ * res_bf16) read at row (m % res_period) when res_period > 0 (positional embedding) else row m; res may
+ * alias out (in-place residual stream).  out2 (may be NULL) receives a bf16 copy of an fp32 output.
+ * GELU only with bf16 output.
+ * Replaces: bf16gemm_launch (i8gemm.hip:534) plus the unfused residual add of lin_res / mlp
+ * (moondream/gpu/md2fast.py:55-67) and the pos_emb add of md2fast.py:150. */
+int vt_gemm_ex(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+               int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+               long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2);
+
+/* Non-causal, mask-free attention O = softmax(Q K^T * scale) V for B crops x H heads of T tokens,
+ * head_dim D (multiple of 8, <= 80; zero-padded to 64 / 80 on chip).  Element (b,t,h,d) of X is at
+ * X + b*sx_b + t*sx_t + h*sx_h + d; Q/K/V read in place (no transposed V copy).
+ * Replaces: attn_fwd2, moondream/gpu/hip/attn.hip:442 (plus vtranspose, attn.hip:284), called from
+ * hattn.Attn.__call__ (moondream/gpu/hattn.py:26-37). */
+int vt_attn_fwd(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int B,
+                int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b, long long sk_t,
+                long long sk_h, long long sv_b, long long sv_t, long long sv_h, long long so_b, long long so_t,
+                long long so_h, float scale);
+
+/* y = LayerNorm(x) * gamma + beta over rows of N (N % 4 == 0, N <= 4096); x fp32 (bf16 when in_bf16),
+ * y bf16 (fp32 when out_f32); fp32 statistics.
+ * Replaces: _ln / F.layer_norm, moondream/gpu/md2fast.py:43-44 (ln1, ln2, post_ln; md2fast.py:153-158). */
+int vt_layernorm(cudaStream_t stream, const void* x, long long ldx, int in_bf16, const float* gamma,
+                 const float* beta, void* y, long long ldy, int out_f32, int M, int N, float eps);
+
+/* Patch im2col into A[B*(S/P)^2][C*P*P] (bf16, pitch ldo) with K order (c, py, px); pixel kinds:
+ * 0 fp32 NCHW, 1 bf16 NCHW, 2 uint8 NHWC normalised (u/255 - 0.5)/0.5.
+ * Replaces: the normalise + reshape/permute of moondream/gpu/md2fast.py:148-149. */
+int vt_im2col(cudaStream_t stream, const void* pix, int kind, int B, int C, int S, int P, uint16_t* out,
+              long long ldo);
+
+/* Multi-crop combine: out[t] = [ f[0][t] , mean_{i=1..n-1} f[i][t] ] (bf16).
+ * Replaces: the feature input of the projection, moondream/gpu/md2fast.py:159 (cat([x, x]) for one crop),
+ * for the 13-crop frame of the benchmark configuration (global + mean of the local crops). */
+int vt_crop_combine(cudaStream_t stream, const uint16_t* f, long long crop_stride, long long ldf, int n_crops, int T,
+                    int W, uint16_t* out, long long ldo);
+
+/* RG-LRU recurrence step over M tokens of width W: G = [gx_pre | ga_pre] fp32, state and x fp32 updated in
+ * place (state <- h, x <- x + h); first != 0 starts a sequence.
+ * Replaces: the RG-LRU forward restated in tapnext/npu/r9/cpuemu.py:33-47 (the NPU's EW SSM op). */
+int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_param, float* state, long long lds,
+             float* x, long long ldx, int M, int W, float c, int first);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VT_B200_H */

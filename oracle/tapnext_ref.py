@@ -1,0 +1,53 @@
+"""CPU fp32 restatement of the TAPNext-style per-frame step -- TEST INFRASTRUCTURE, parity unpinned.
+
+Token layout: 8x8 patch conv of a 256x256 frame (1024 tokens) + image position embedding, then the
+256 point-query tokens (tapnext/npu/step8.py:251-267).  Each of the 12 blocks is a pre-LN ViT block
+(LN -> MHA -> +, LN -> MLP GELU -> +, the vit_block part of step8.py:482-485) followed by a residual
+per-token RG-LRU whose step is tapnext/npu/r9/cpuemu.py:33-47 with exact transcendentals:
+    gx = sigmoid(Wx x + bx), ga = sigmoid(Wa x + ba), log_a = -c * ga * softplus(a_param), a = exp(log_a)
+    h = x * gx                                  (first frame, h0 is None)
+    h = a * h0 + (x * gx) * sqrt(1 - a^2)        (later frames)
+    x <- x + h, state <- h (float32)
+then the encoder LayerNorm (step8.py:488).  The BASELINE config simplifies the reference block (no
+RMSNorm / conv1d / gated MLP, dense gates), and the vendored model is not in the repository, so
+nothing pins this restatement against the reference's outputs.
+"""
+import torch
+import torch.nn.functional as F
+
+from .tower_ref import _t, im2col, layer_norm, gelu, linear
+
+
+def rglru(x, W, p, h0, c):
+    """cpuemu.py:33-47 with exact sigmoid / exp / sqrt, in float32."""
+    gx = torch.sigmoid(linear(x, W[p + "gx_w"], W[p + "gx_b"]))
+    ga = torch.sigmoid(linear(x, W[p + "ga_w"], W[p + "ga_b"]))
+    log_a = -c * ga * F.softplus(_t(W[p + "a_param"]))
+    gated = x * gx
+    if h0 is None:
+        return gated
+    a = torch.exp(log_a)
+    return a * h0 + gated * torch.sqrt(-torch.expm1(2.0 * log_a))
+
+
+def step(frame, queries, W, cfg, state=None, n_blocks=None):
+    """frame [3, 256, 256] in [-1, 1], queries [256, 768] -> (features [1280, 768], new state list)."""
+    nb = cfg.n_blocks if n_blocks is None else n_blocks
+    with torch.no_grad():
+        x = linear(im2col(_t(frame).float()[None], cfg.patch)[0], W["patch_w"], W["patch_b"]) + _t(W["pos_emb"])
+        x = torch.cat([x, _t(queries).float()], dim=0)[None]
+        T = x.shape[1]
+        new_state = []
+        for i in range(nb):
+            p = f"blocks.{i}."
+            h = layer_norm(x, W[p + "ln1_w"], W[p + "ln1_b"], cfg.eps)
+            q, k, v = [t.view(1, T, cfg.heads, -1).transpose(1, 2) for t in linear(h, W[p + "qkv_w"], W[p + "qkv_b"]).chunk(3, dim=-1)]
+            a = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(1, T, -1)
+            x = x + linear(a, W[p + "proj_w"], W[p + "proj_b"])
+            h = layer_norm(x, W[p + "ln2_w"], W[p + "ln2_b"], cfg.eps)
+            x = x + linear(gelu(linear(h, W[p + "fc1_w"], W[p + "fc1_b"])), W[p + "fc2_w"], W[p + "fc2_b"])
+            hs = rglru(x, W, p, None if state is None else state[i], cfg.lru_c)
+            new_state.append(hs)
+            x = x + hs
+        out = layer_norm(x, W["final_ln_w"], W["final_ln_b"], cfg.eps)[0]
+        return out, new_state

@@ -1,0 +1,261 @@
+// Memory-bound kernels of the tower: LayerNorm, patch im2col (+ pixel normalisation), multi-crop
+// combine and the RG-LRU recurrence.  All use 128-bit global accesses where the layout allows.
+#include "vt_common.cuh"
+#include "vt_host.h"
+
+namespace vt {
+namespace ew {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float4 load4(const void* base, long long idx, int in_bf16) {
+  if (in_bf16) {
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(base) + idx);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+  }
+  return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+}
+__device__ __forceinline__ void store4(void* base, long long idx, float4 v, int out_f32) {
+  if (out_f32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx) = v;
+  } else {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(base) + idx) = make_uint2(pack_bf2(v.x, v.y), pack_bf2(v.z, v.w));
+  }
+}
+
+// LayerNorm over rows of N (N % 4 == 0, N <= 4096): one warp per row, the row held in registers
+// (two-pass mean / variance in fp32), y = (x - mean) * rsqrt(var + eps) * gamma + beta.
+// Follows F.layer_norm as md2fast.py:43-44 calls it.
+constexpr int LN_MAXV = 32;  // float4 per lane, upper bound (N <= 4096)
+template <int MAXV>
+__global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long ldx, int in_bf16, const float* g,
+                                                        const float* bta, void* y, long long ldy, int out_f32, int M,
+                                                        int N, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + warp;
+  if (row >= M) return;
+  const int nv = N / 4;
+  float4 v[MAXV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    const int c = (i * 32 + lane);
+    if (c < nv) {
+      v[i] = load4(x, row * ldx + 4LL * c, in_bf16);
+      s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+  }
+  const float mean = warp_sum(s) / (float)N;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    const int c = (i * 32 + lane);
+    if (c < nv) {
+      const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (cc * cc + d * d);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / (float)N + eps);
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    const int c = (i * 32 + lane);
+    if (c < nv) {
+      const float4 gg = *reinterpret_cast<const float4*>(g + 4 * c);
+      const float4 bb = *reinterpret_cast<const float4*>(bta + 4 * c);
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * gg.x + bb.x;
+      o.y = (v[i].y - mean) * rstd * gg.y + bb.y;
+      o.z = (v[i].z - mean) * rstd * gg.z + bb.z;
+      o.w = (v[i].w - mean) * rstd * gg.w + bb.w;
+      store4(y, row * ldy + 4LL * c, o, out_f32);
+    }
+  }
+}
+
+// Patch im2col: pixels -> A[m, k] (bf16, pitch ldo) with m = crop*g*g + gy*g + gx and
+// k = c*P*P + py*P + px (md2fast.py:149 permutation).  kind 0: fp32 NCHW values, 1: bf16 NCHW values,
+// 2: uint8 NHWC 0..255 normalised by (u/255 - 0.5)/0.5 (md2fast.py:148).  One thread per P-pixel run.
+__global__ void __launch_bounds__(256) im2col_kernel(const void* pix, int kind, int B, int C, int S, int P,
+                                                     uint16_t* out, long long ldo) {
+  const int g = S / P;
+  const long long total = (long long)B * g * g * C * P;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i;
+    const int py = (int)(r % P); r /= P;
+    const int c = (int)(r % C); r /= C;
+    const int gx = (int)(r % g); r /= g;
+    const int gy = (int)(r % g); r /= g;
+    const long long b = r;
+    const long long m = b * g * g + (long long)gy * g + gx;
+    const int y = gy * P + py;
+    uint16_t* op = out + m * ldo + (long long)c * P * P + (long long)py * P;
+    for (int px = 0; px < P; px++) {
+      const int xx = gx * P + px;
+      float val;
+      if (kind == 0) {
+        val = reinterpret_cast<const float*>(pix)[((b * C + c) * S + y) * (long long)S + xx];
+      } else if (kind == 1) {
+        val = bf2f(reinterpret_cast<const uint16_t*>(pix)[((b * C + c) * S + y) * (long long)S + xx]);
+      } else {
+        const float u = (float)reinterpret_cast<const uint8_t*>(pix)[((b * S + y) * (long long)S + xx) * C + c];
+        val = (u / 255.0f - 0.5f) / 0.5f;
+      }
+      op[px] = f2bf(val);
+    }
+  }
+}
+
+// Multi-crop combine: out[t, :W] = f[0, t], out[t, W:2W] = mean_{i=1..n-1} f[i, t] (fp32 sum), bf16.
+__global__ void __launch_bounds__(256) combine_kernel(const uint16_t* f, long long crop_stride, long long ldf,
+                                                      int n_crops, int T, int W, uint16_t* out, long long ldo) {
+  const int nch = W / 8;
+  const long long total = (long long)T * nch;
+  const float inv = 1.0f / (float)(n_crops - 1);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / nch), c = (int)(i % nch) * 8;
+    const uint4 g0 = *reinterpret_cast<const uint4*>(f + (long long)t * ldf + c);
+    *reinterpret_cast<uint4*>(out + (long long)t * ldo + c) = g0;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 1; k < n_crops; k++) {
+      const uint4 u = *reinterpret_cast<const uint4*>(f + k * crop_stride + (long long)t * ldf + c);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        acc[2 * e] += __uint_as_float(w[e] << 16);
+        acc[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+      }
+    }
+    *reinterpret_cast<uint4*>(out + (long long)t * ldo + W + c) =
+        make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
+                   pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
+  }
+}
+
+// RG-LRU step (tapnext/npu/r9/cpuemu.py:33-47), per element (m, n < W):
+//   gx = sigmoid(G[m, n]), ga = sigmoid(G[m, W + n]), log_a = -c * ga * softplus(a_param[n])
+//   h  = x * gx                                              (first frame)
+//   h  = exp(log_a) * h0 + (x * gx) * sqrt(-expm1(2 log_a))   (later frames)
+//   state <- h, x <- x + h     (state and x fp32, updated in place)
+__device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
+__device__ __forceinline__ float softplusf_(float z) { return z > 20.f ? z : log1pf(expf(z)); }
+
+__global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param, float* state,
+                                                    long long lds, float* x, long long ldx, int M, int W, float c,
+                                                    int first) {
+  const int nv = W / 4;
+  const long long total = (long long)M * nv;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / nv;
+    const int n = (int)(i % nv) * 4;
+    const float4 gx4 = *reinterpret_cast<const float4*>(G + m * ldg + n);
+    const float4 ga4 = *reinterpret_cast<const float4*>(G + m * ldg + W + n);
+    const float4 ap4 = *reinterpret_cast<const float4*>(a_param + n);
+    float4 x4 = *reinterpret_cast<const float4*>(x + m * ldx + n);
+    float4 h4 = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(state + m * lds + n);
+    const float gx[4] = {gx4.x, gx4.y, gx4.z, gx4.w}, ga[4] = {ga4.x, ga4.y, ga4.z, ga4.w};
+    const float ap[4] = {ap4.x, ap4.y, ap4.z, ap4.w};
+    float xv[4] = {x4.x, x4.y, x4.z, x4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float gated = xv[e] * sigmoidf_(gx[e]);
+      float h;
+      if (first) {
+        h = gated;
+      } else {
+        const float log_a = -c * sigmoidf_(ga[e]) * softplusf_(ap[e]);
+        h = expf(log_a) * hv[e] + gated * sqrtf(-expm1f(2.0f * log_a));
+      }
+      hv[e] = h;
+      xv[e] += h;
+    }
+    *reinterpret_cast<float4*>(state + m * lds + n) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<float4*>(x + m * ldx + n) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+  }
+}
+
+static int grid_for(long long work, int threads) {
+  long long g = (work + threads - 1) / threads;
+  const long long cap = (long long)sm_count() * 16;
+  if (g > cap) g = cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace ew
+}  // namespace vt
+
+extern "C" {
+
+// y[M, N] = LayerNorm(x[M, N]) * gamma + beta.  x fp32 (or bf16 when in_bf16), y bf16 (or fp32 when
+// out_f32).  N % 4 == 0, N <= 4096; pitches multiples of 4 (fp32) / 4 (bf16) elements, 16-byte bases.
+int vt_layernorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma, const float* beta,
+                 void* y, long long ldy, int out_f32, int M, int N, float eps) {
+  using namespace vt;
+  if (M < 0 || N < 0) return set_error(E_SHAPE, "vt_layernorm: negative shape");
+  if (M == 0) return OK;
+  if (N == 0 || N % 4 || N > 4 * 32 * ew::LN_MAXV) return set_error(E_SHAPE, "vt_layernorm: N=%d unsupported", N);
+  if (!x || !y || !gamma || !beta) return set_error(E_SHAPE, "vt_layernorm: null pointer");
+  if (ldx < N || ldy < N || ldx % 4 || ldy % 4 || !aligned16(x) || !aligned16(y) || !aligned16(gamma) || !aligned16(beta))
+    return set_error(E_SHAPE, "vt_layernorm: pitches / alignment invalid");
+  const long long blocks = ((long long)M + 7) / 8;
+  if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "vt_layernorm: M too large");
+  const int per_lane = (N / 4 + 31) / 32;
+  if (per_lane <= 4)
+    ew::layernorm_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+  else if (per_lane <= 8)
+    ew::layernorm_kernel<8><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+  else if (per_lane <= 12)
+    ew::layernorm_kernel<12><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+  else if (per_lane <= 16)
+    ew::layernorm_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+  else
+    ew::layernorm_kernel<32><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+  return check_launch("vt_layernorm");
+}
+
+// Patch im2col of B square images (S x S, C channels, patch P) into A[B*(S/P)^2, C*P*P] bf16 with
+// row pitch ldo (>= C*P*P, a multiple of 8).  kind: 0 fp32 NCHW, 1 bf16 NCHW, 2 uint8 NHWC (0..255).
+int vt_im2col(cudaStream_t st, const void* pix, int kind, int B, int C, int S, int P, uint16_t* out, long long ldo) {
+  using namespace vt;
+  if (B < 0 || C <= 0 || P <= 0 || S <= 0 || S % P) return set_error(E_SHAPE, "vt_im2col: bad geometry");
+  if (kind < 0 || kind > 2) return set_error(E_VARIANT, "vt_im2col: unknown pixel kind %d", kind);
+  if (B == 0) return OK;
+  if (!pix || !out || ldo < (long long)C * P * P) return set_error(E_SHAPE, "vt_im2col: bad output");
+  const int g = S / P;
+  ew::im2col_kernel<<<ew::grid_for((long long)B * g * g * C * P, 256), 256, 0, st>>>(pix, kind, B, C, S, P, out, ldo);
+  return check_launch("vt_im2col");
+}
+
+// Multi-crop combine of n_crops crop features f[n][T][W] (bf16; crop n at f + n*crop_stride, row pitch
+// ldf) into out[T][2W]: global crop 0, then the mean of crops 1..n-1.
+int vt_crop_combine(cudaStream_t st, const uint16_t* f, long long crop_stride, long long ldf, int n_crops, int T, int W,
+                    uint16_t* out, long long ldo) {
+  using namespace vt;
+  if (n_crops < 2 || T < 0 || W <= 0 || W % 8) return set_error(E_SHAPE, "vt_crop_combine: bad shape");
+  if (T == 0) return OK;
+  if (!f || !out || ldf < W || ldo < 2LL * W || ldf % 8 || ldo % 8 || crop_stride % 8 || !aligned16(f) || !aligned16(out))
+    return set_error(E_SHAPE, "vt_crop_combine: pitches / alignment invalid");
+  ew::combine_kernel<<<ew::grid_for((long long)T * (W / 8), 256), 256, 0, st>>>(f, crop_stride, ldf, n_crops, T, W, out, ldo);
+  return check_launch("vt_crop_combine");
+}
+
+// RG-LRU step over M tokens of width W; G = [gx_pre | ga_pre] fp32 [M][ldg >= 2W]; state and x fp32,
+// updated in place; first != 0 starts a new sequence (state ignored and overwritten).
+int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_param, float* state, long long lds,
+             float* x, long long ldx, int M, int W, float c, int first) {
+  using namespace vt;
+  if (M < 0 || W <= 0 || W % 4) return set_error(E_SHAPE, "vt_rglru: bad shape");
+  if (M == 0) return OK;
+  if (!G || !a_param || !state || !x || ldg < 2LL * W || lds < W || ldx < W || ldg % 4 || lds % 4 || ldx % 4 ||
+      !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(a_param))
+    return set_error(E_SHAPE, "vt_rglru: pitches / alignment invalid");
+  ew::rglru_kernel<<<ew::grid_for((long long)M * (W / 4), 256), 256, 0, st>>>(G, ldg, a_param, state, lds, x, ldx, M, W,
+                                                                             c, first);
+  return check_launch("vt_rglru");
+}
+
+}  // extern "C"

@@ -1,0 +1,358 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM, operands staged by TMA):
+//     C[M, N] = epilogue( A[M, K] . W[N, K]^T )
+// the replacement of the reference's bf16gemm_kernel / bf16gemm_launch
+// (moondream/gpu/hip/i8gemm.hip:286-385, 534-552) that HLin calls (moondream/gpu/hgemm.py:139-178).
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   * tile 128 x 256 x 64, 4-stage shared-memory ring (48 KB per stage), 128-byte swizzle;
+//   * warp 0 lane 0 issues the TMA loads (no multicast), warp 1 lane 0 issues tcgen05.mma
+//     (M=128, N=256, K=16 each, fp32 accumulators in TMEM), warps 2-5 run the epilogue;
+//   * two 256-column TMEM accumulators, so the epilogue of tile i overlaps the MMAs of tile i+1;
+//   * tiles are walked N-fastest, so the CTAs resident at one time share A rows and the whole of W
+//     through L2;
+//   * epilogue: + bias, then either bf16 output (optionally GELU-tanh applied after rounding to bf16,
+//     as i8gemm.hip:378 does) or fp32 output with a residual / periodic addend (fp32 or bf16) and an
+//     optional bf16 copy.  M, N and K tails are handled by TMA zero fill and masked stores.
+#include "vt_common.cuh"
+#include "vt_host.h"
+
+namespace vt {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr long long kDrainCycles = 200000000LL;
+
+struct Epi {
+  const float* bias;  // [N] fp32 or null
+  void* out;          // [M][ldo], bf16 or fp32
+  long long ldo;
+  const void* res;    // addend [rows][ldr] or null; row = m % res_period when res_period > 0
+  long long ldr;
+  int res_period;
+  int res_bf16;
+  int out_f32;
+  int gelu;
+  uint16_t* out2;     // optional bf16 copy of an fp32 output, [M][ldo2]
+  long long ldo2;
+};
+
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+  const bool full = (n0 + 32 <= N);
+  if (ep.bias) {
+    if (full) {
+      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float4 b = __ldg(b4 + j);
+        v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n0 + j < N) v[j] += ep.bias[n0 + j];
+    }
+  }
+  if (ep.res) {
+    const long long rr = ep.res_period > 0 ? (long long)(m % ep.res_period) : (long long)m;
+    if (ep.res_bf16) {
+      const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.res) + rr * ep.ldr + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const uint4 u = *reinterpret_cast<const uint4*>(rp + 8 * j);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            v[8 * j + 2 * e] += __uint_as_float(w[e] << 16);
+            v[8 * j + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (n0 + j < N) v[j] += bf2f(rp[j]);
+      }
+    } else {
+      const float* rp = reinterpret_cast<const float*>(ep.res) + rr * ep.ldr + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float4 a = *reinterpret_cast<const float4*>(rp + 4 * j);
+          v[4 * j] += a.x; v[4 * j + 1] += a.y; v[4 * j + 2] += a.z; v[4 * j + 3] += a.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (n0 + j < N) v[j] += rp[j];
+      }
+    }
+  }
+  if (ep.out_f32) {
+    float* op = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + n0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        *reinterpret_cast<float4*>(op + 4 * j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n0 + j < N) op[j] = v[j];
+    }
+    if (ep.out2) {
+      uint16_t* o2 = ep.out2 + (long long)m * ep.ldo2 + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          *reinterpret_cast<uint4*>(o2 + 8 * j) =
+              make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
+                         pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (n0 + j < N) o2[j] = f2bf(v[j]);
+      }
+    }
+  } else {
+    if (ep.gelu) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = gelu_tanh(bfround(v[j]));
+    }
+    uint16_t* op = reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        *reinterpret_cast<uint4*>(op + 8 * j) =
+            make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
+                       pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n0 + j < N) op[j] = f2bf(v[j]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                        int K, Epi ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nN = (N + BN - 1) / BN;
+  const int ntiles = ((M + BM - 1) / BM) * nN;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int mt = t / nN, nt = t % nN;
+        for (int kb = 0; kb < nk; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, ST_GEMM_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          tma_load_2d(&tmA, &full[stage], sa, kb * BK, mt * BM);
+          tma_load_2d(&tmB, &full[stage], sa + A_BYTES, kb * BK, nt * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // unwinding: let the loads this thread issued land before the CTA exits
+        uint32_t s = stage, p = phase;
+        for (int j = 0; j < STAGES && j < issued; j++) {
+          if (s == 0) {
+            s = STAGES - 1;
+            p ^= 1;
+          } else {
+            s--;
+          }
+          mbar_wait_drain(&full[s], p, kDrainCycles);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, ST_GEMM_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; kb++) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, ST_GEMM_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // no MMA may still be writing TMEM when it is freed
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0, kDrainCycles);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, warp w reads TMEM lanes 32*(w%4) .. +31
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
+      tc_fence_after();
+      const int mt = t / nN, nt = t % nN;
+      const int m = mt * BM + row;
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        const int n0 = nt * BN + c * 32;
+        if (n0 >= N) break;  // uniform across the CTA
+        uint32_t r[32];
+        tmem_ld32(tb + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        if (m < M) epilogue_chunk(r, m, n0, N, ep);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                  int K, const Epi& ep) {
+  if (M < 0 || N < 0 || K < 0) return set_error(E_SHAPE, "vt_gemm: negative shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0 || N == 0) return OK;
+  if (K == 0) return set_error(E_SHAPE, "vt_gemm: K must be >= 1");
+  if (!A || !W || !ep.out) return set_error(E_SHAPE, "vt_gemm: null operand");
+  if (lda < K || ldw < K || lda % 8 || ldw % 8 || !aligned16(A) || !aligned16(W))
+    return set_error(E_SHAPE, "vt_gemm: A/W need 16-byte aligned bases and row pitches (lda=%lld ldw=%lld K=%d)", lda,
+                     ldw, K);
+  if (ep.ldo < N || ep.ldo % 8 || !aligned16(ep.out))
+    return set_error(E_SHAPE, "vt_gemm: output pitch %lld must be >= N=%d, a multiple of 8, 16-byte aligned", ep.ldo,
+                     N);
+  if (ep.res && (ep.ldr < N || ep.ldr % 8 || !aligned16(ep.res) || ep.res_period < 0))
+    return set_error(E_SHAPE, "vt_gemm: residual pitch %lld / period %d invalid", ep.ldr, ep.res_period);
+  if (ep.out2 && (ep.ldo2 < N || ep.ldo2 % 8 || !aligned16(ep.out2)))
+    return set_error(E_SHAPE, "vt_gemm: bf16 copy pitch %lld invalid", ep.ldo2);
+  if (ep.bias && !aligned16(ep.bias)) return set_error(E_SHAPE, "vt_gemm: bias must be 16-byte aligned");
+  if (ep.gelu && ep.out_f32) return set_error(E_VARIANT, "vt_gemm: GELU is only fused for bf16 output");
+
+  CUtensorMap ta, tb;
+  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
+  if (rc) return rc;
+  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, BN);
+  if (rc) return rc;
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_done[dev] = true;
+  }
+  const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
+  const int grid = (int)(ntiles < sm_count() ? ntiles : sm_count());
+  gemm_bf16_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  return check_launch("vt_gemm");
+}
+
+}  // namespace gemm
+}  // namespace vt
+
+extern "C" {
+
+// C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias, optionally GELU-tanh (after bf16 rounding).
+int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
+                 const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu) {
+  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0};
+  return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+// General form.  out_f32 selects fp32 output (no GELU); res (fp32, or bf16 when res_bf16) is added
+// after the bias, read at row (m % res_period) when res_period > 0; out2 receives a bf16 copy of an
+// fp32 output.  res may alias out (in-place residual update).
+int vt_gemm_ex(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N, int K,
+               const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res, long long ldr,
+               int res_period, int res_bf16, uint16_t* out2, long long ldo2) {
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2};
+  return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+}  // extern "C"

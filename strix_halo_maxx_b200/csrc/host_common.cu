@@ -1,0 +1,106 @@
+// Host helpers of libvt_b200.so: error strings, the device status word, SM count and the
+// cuTensorMapEncodeTiled entry point (fetched through the runtime, so no libcuda link is needed).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "vt_common.cuh"
+#include "vt_host.h"
+
+namespace vt {
+
+static thread_local char g_err[1024] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(E_LAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return OK;
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
+                   uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(E_TMAP, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base) || (ld_elems * 2) % 16 != 0)
+    return set_error(E_SHAPE, "tensor map: base %p / row pitch %llu elements not 16-byte aligned", base,
+                     (unsigned long long)ld_elems);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapSwizzle sw = (box_cols * 2 == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(E_TMAP, "cuTensorMapEncodeTiled failed (%d): cols %llu rows %llu ld %llu box %ux%u", (int)r,
+                     (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)ld_elems, box_cols,
+                     box_rows);
+  return OK;
+}
+
+}  // namespace vt
+
+extern "C" {
+
+const char* vt_last_error_string(void) { return vt::g_err; }
+
+// Reads (and optionally clears) the device status word of the current device.  Synchronises the
+// device.  Returns 0 when no kernel has recorded a timed-out wait.
+int vt_device_status(int clear, unsigned int* status) {
+  unsigned int s = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&s, vt::g_status, sizeof(s));
+  if (e != cudaSuccess) return vt::set_error(vt::E_LAUNCH, "vt_device_status: %s", cudaGetErrorString(e));
+  if (clear) {
+    unsigned int z = 0;
+    e = cudaMemcpyToSymbol(vt::g_status, &z, sizeof(z));
+    if (e != cudaSuccess) return vt::set_error(vt::E_LAUNCH, "vt_device_status: %s", cudaGetErrorString(e));
+  }
+  if (status) *status = s;
+  return 0;
+}
+
+int vt_abi_version(void) { return 1; }
+
+}  // extern "C"

@@ -1,0 +1,6 @@
+// Single translation unit of libvt_b200.so.  The kernels share one device status word
+// (vt::g_status), so they are compiled together rather than linked with relocatable device code.
+#include "host_common.cu"
+#include "gemm_tc.cu"
+#include "attn.cu"
+#include "elementwise.cu"

@@ -1,0 +1,24 @@
+// Host-side helpers shared by the .cu files of libvt_b200.so (not part of the public C ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vt {
+
+// Error codes, same convention as the reference's launchers (0 ok, -1 unknown variant,
+// -2 shape / alignment, -4 layout mismatch), plus -3 for a CUDA launch error and -5 for a
+// tensor-map encode failure.
+enum : int { OK = 0, E_VARIANT = -1, E_SHAPE = -2, E_LAUNCH = -3, E_LAYOUT = -4, E_TMAP = -5 };
+
+int set_error(int code, const char* fmt, ...);   // records the message for vt_last_error_string()
+int check_launch(const char* what);              // maps cudaGetLastError() to E_LAUNCH
+int sm_count();                                  // SMs of the current device (cached per device)
+bool aligned16(const void* p);
+
+// 2-D bf16 tensor map over a row-major matrix [rows][ld] (K-contiguous), box = box_cols x box_rows,
+// 128-byte swizzle when box_cols * 2 == 128, zero fill out of bounds.  Returns E_TMAP on failure.
+int make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
+                   uint32_t box_cols, uint32_t box_rows);
+
+}  // namespace vt

@@ -1,0 +1,167 @@
+"""Op-level drop-ins for the reference's plugin API, backed by libvt_b200.so.
+
+* VtLin  -- the `lin_cls` the reference's FastMD2 builds every linear with (md2fast.py:33-40, 87-103):
+  VtLin(weight, bias, dtype) -> __call__(x, gelu=False, res=None), class flags fused_gelu / fused_res
+  (hgemm.HLin, hgemm.py:139-178).
+* VtAttn -- hattn.Attn(H, T, D) -> __call__(q, k, v, out=None) -> (B, T, H*D) (hattn.py:17-37).
+* layer_norm / im2col / crop_combine / rglru -- thin wrappers of the remaining kernels.
+
+Every call launches on torch's current stream and raises VtError on a non-zero return code.
+"""
+import torch
+
+from ._lib import lib, check as _check
+
+BF16 = torch.bfloat16
+
+# Number of kernel launches made through this module (bench.py reports the count of its timed region).
+LAUNCHES = 0
+
+
+def check(rc, what):
+    global LAUNCHES
+    _check(rc, what)
+    LAUNCHES += 1
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _pad8(n):
+    return (n + 7) // 8 * 8
+
+
+def as_gemm_operand(x2):
+    """bf16 2-D view with unit column stride, a row pitch that is a multiple of 8 and a 16-B aligned base."""
+    if x2.dtype == BF16 and x2.stride(-1) == 1 and x2.stride(0) % 8 == 0 and x2.data_ptr() % 16 == 0 \
+            and x2.stride(0) >= x2.shape[1]:
+        return x2
+    M, K = x2.shape
+    buf = torch.empty(M, _pad8(K), dtype=BF16, device=x2.device)
+    buf[:, :K] = x2
+    return buf[:, :K]
+
+
+def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=None, out_f32=False, out2=None):
+    """out[M, N] = x2 . w^T + bias (+ GELU) (+ res); see vt_gemm_ex in include/vt_b200.h."""
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :N]
+    rc = lib().vt_gemm_ex(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
+                          out.data_ptr(), out.stride(0), int(out.dtype == torch.float32), int(gelu),
+                          _ptr(res), 0 if res is None else res.stride(0), int(res_period),
+                          int(res is not None and res.dtype == BF16), _ptr(out2), 0 if out2 is None else out2.stride(0))
+    check(rc, "vt_gemm_ex")
+    return out
+
+
+class VtLin:
+    """bf16 tcgen05 GEMM with fused bias, GELU-tanh and residual epilogues; weights kept (N, K)-major
+    with the row pitch padded to a multiple of 8 elements (16 B, the TMA stride rule), K=588 included."""
+    fused_gelu = True
+    fused_res = True
+
+    def __init__(self, weight, bias, dtype=BF16, device=None):
+        w = weight.detach()
+        dev = torch.device(device) if device is not None else (w.device if w.is_cuda else torch.device("cuda"))
+        self.N, self.K = w.shape
+        self.ldw = _pad8(self.K)
+        self.wbuf = torch.zeros(self.N, self.ldw, dtype=BF16, device=dev)
+        self.wbuf[:, :self.K] = w.to(dev, BF16)
+        self.w = self.wbuf[:, :self.K]
+        self.b = None if bias is None else bias.detach().to(dev, torch.float32).contiguous()
+        self.dtype = dtype
+
+    def __call__(self, x, gelu=False, res=None):
+        shp = x.shape
+        assert shp[-1] == self.K, (shp, self.K)
+        x2 = as_gemm_operand(x.reshape(-1, self.K))
+        if res is None:
+            out = gemm(x2, self.wbuf, self.ldw, self.K, self.N, self.b, gelu=gelu)
+        else:
+            if gelu:
+                raise ValueError("VtLin: gelu and res are not fused together")
+            r2 = res.reshape(-1, self.N)
+            if r2.stride(-1) != 1 or r2.stride(0) % 8 or r2.data_ptr() % 16 or r2.dtype not in (BF16, torch.float32):
+                r2 = r2.to(BF16 if r2.dtype != torch.float32 else torch.float32).contiguous()
+            out = gemm(x2, self.wbuf, self.ldw, self.K, self.N, self.b, res=r2, out_f32=(r2.dtype == torch.float32))
+        return out.reshape(*shp[:-1], self.N)
+
+
+class VtAttn:
+    """Flash attention for one (H, T, D) problem: q, k, v are (B, H, T, D) views (any strides over
+    B / H / T, contiguous D) -- e.g. the chunks of a fused QKV output -- and the result is (B, T, H*D)."""
+
+    def __init__(self, H, T, D, device="cuda"):
+        self.H, self.T, self.D = H, T, D
+        self.scale = D ** -0.5
+
+    def __call__(self, q, k, v, out=None):
+        B, H, T, D = q.shape
+        assert (H, T, D) == (self.H, self.T, self.D), (q.shape, self.H, self.T, self.D)
+        assert q.stride(3) == 1 and k.stride(3) == 1 and v.stride(3) == 1
+        if out is None:
+            out = torch.empty(B, T, H * D, dtype=BF16, device=q.device)
+        rc = lib().vt_attn_fwd(_stream(), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, T, H, D,
+                               q.stride(0), q.stride(2), q.stride(1), k.stride(0), k.stride(2), k.stride(1),
+                               v.stride(0), v.stride(2), v.stride(1), out.stride(0), out.stride(1), D, self.scale)
+        check(rc, "vt_attn_fwd")
+        return out
+
+
+def attention_qkv(qkv, B, T, H, D, out, scale=None):
+    """Attention straight from a fused QKV buffer [B*T, 3*H*D] (row pitch qkv.stride(0)) into out [B*T, H*D]."""
+    s = qkv.stride(0)
+    base = qkv.data_ptr()
+    rc = lib().vt_attn_fwd(_stream(), base, base + 2 * H * D, base + 4 * H * D, out.data_ptr(), B, T, H, D,
+                           T * s, s, D, T * s, s, D, T * s, s, D, T * out.stride(0), out.stride(0), D,
+                           D ** -0.5 if scale is None else scale)
+    check(rc, "vt_attn_fwd")
+    return out
+
+
+def layer_norm(x2, w, b, eps, out=None, out_f32=False):
+    M, N = x2.shape
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if out_f32 else BF16, device=x2.device)
+    rc = lib().vt_layernorm(_stream(), x2.data_ptr(), x2.stride(0), int(x2.dtype == BF16), w.data_ptr(), b.data_ptr(),
+                            out.data_ptr(), out.stride(0), int(out.dtype == torch.float32), M, N, float(eps))
+    check(rc, "vt_layernorm")
+    return out
+
+
+PIX_KIND = {torch.float32: 0, BF16: 1, torch.uint8: 2}
+
+
+def im2col(pix, patch, out):
+    """pix [B, C, S, S] fp32/bf16 (NCHW) or uint8 [B, S, S, C] (NHWC) -> out [B*(S/P)^2, >= C*P*P] bf16."""
+    kind = PIX_KIND[pix.dtype]
+    pix = pix.contiguous()
+    if kind == 2:
+        B, S, _, C = pix.shape
+    else:
+        B, C, S, _ = pix.shape
+    rc = lib().vt_im2col(_stream(), pix.data_ptr(), kind, B, C, S, patch, out.data_ptr(), out.stride(0))
+    check(rc, "vt_im2col")
+    return out
+
+
+def crop_combine(feats, out):
+    """feats [n, T, W] bf16 -> out [T, 2W]: global crop 0 then the mean of crops 1..n-1."""
+    n, T, W = feats.shape
+    rc = lib().vt_crop_combine(_stream(), feats.data_ptr(), feats.stride(0), feats.stride(1), n, T, W,
+                               out.data_ptr(), out.stride(0))
+    check(rc, "vt_crop_combine")
+    return out
+
+
+def rglru(G, a_param, state, x, c, first):
+    M, W = x.shape
+    rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), state.data_ptr(), state.stride(0),
+                        x.data_ptr(), x.stride(0), M, W, float(c), int(bool(first)))
+    check(rc, "vt_rglru")

@@ -1,0 +1,86 @@
+"""TAPNext-style per-frame streaming step on B200: 8x8 patch conv of a 256x256 frame
+(1024 tokens) + position embedding, 256 point-query tokens appended (token layout of
+tapnext/npu/step8.py:251-267), 12 x [pre-LN ViT block (12 heads x 64, MLP 3072 GELU) + residual RG-LRU]
+and the encoder LayerNorm.  The RG-LRU (tapnext/npu/r9/cpuemu.py:33-47) keeps one fp32 state
+[1280, 768] per block, carried across frames in device memory owned by this object; reset() starts a
+new video.
+
+Per block the kernels are the tower's (vt_layernorm, vt_gemm_ex, vt_attn_fwd with d = 64) plus:
+    xb  = bf16 copy of x, written by the fc2 residual epilogue (out2)
+    G   = xb . [Wx; Wa]^T + [bx; ba]        one vt_gemm_ex, N = 1536, fp32 out
+    vt_rglru(G, a_param, state_i, x)        gates, recurrence, state and residual update in one pass
+"""
+import torch
+
+from .config import TAPNEXT, TapNextConfig
+from . import ops
+from .ops import BF16, _pad8
+from .tower import _dev_mat, _dev_vec
+
+F32 = torch.float32
+
+
+class TapNextStep:
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda"):
+        self.cfg = cfg
+        dev = self.dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = self.dev = torch.device("cuda", torch.cuda.current_device())
+        W = weights
+        self.n_blocks = sum(1 for k in W if k.endswith(".qkv_w"))
+        self.pe_w, self.pe_ld = _dev_mat(W["patch_w"], dev)
+        self.pe_b = _dev_vec(W["patch_b"], dev)
+        self.pos = _dev_vec(W["pos_emb"], dev).reshape(cfg.n_img_tok, cfg.width)
+        self.blocks = []
+        for i in range(self.n_blocks):
+            p = f"blocks.{i}."
+            blk = {}
+            for n in ("qkv", "proj", "fc1", "fc2"):
+                blk[n + "_w"], blk[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
+                blk[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
+            g = torch.cat([torch.as_tensor(W[p + "gx_w"]), torch.as_tensor(W[p + "ga_w"])], 0)
+            blk["gate_w"], blk["gate_ld"] = _dev_mat(g, dev)
+            blk["gate_b"] = _dev_vec(torch.cat([torch.as_tensor(W[p + "gx_b"]), torch.as_tensor(W[p + "ga_b"])]), dev)
+            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "a_param"):
+                blk[n] = _dev_vec(W[p + n], dev)
+            self.blocks.append(blk)
+        self.fin_w = _dev_vec(W["final_ln_w"], dev)
+        self.fin_b = _dev_vec(W["final_ln_b"], dev)
+        T, Wd = cfg.ntok, cfg.width
+        self.a_pe = torch.zeros(cfg.n_img_tok, _pad8(cfg.patch_k), dtype=BF16, device=dev)
+        self.x = torch.empty(T, Wd, dtype=F32, device=dev)
+        self.xb = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.h = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.qkv = torch.empty(T, 3 * Wd, dtype=BF16, device=dev)
+        self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.f = torch.empty(T, _pad8(cfg.ff), dtype=BF16, device=dev)
+        self.G = torch.empty(T, 2 * Wd, dtype=F32, device=dev)
+        self.state = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
+        self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.first = True
+
+    def reset(self):
+        self.first = True
+
+    def step(self, frame, queries):
+        """frame [3, 256, 256] fp32/bf16 in [-1, 1], queries [256, 768] fp32 (device) -> [1280, 768] bf16."""
+        cfg = self.cfg
+        T, Wd, NI = cfg.ntok, cfg.width, cfg.n_img_tok
+        ops.im2col(frame.reshape(1, *frame.shape[-3:]), cfg.patch, self.a_pe)
+        ops.gemm(self.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
+                 res=self.pos, res_period=NI, out=self.x[:NI])
+        self.x[NI:].copy_(queries)
+        for i, blk in enumerate(self.blocks):
+            ops.layer_norm(self.x, blk["ln1_w"], blk["ln1_b"], cfg.eps, out=self.h)
+            ops.gemm(self.h, blk["qkv_w"], blk["qkv_ld"], Wd, 3 * Wd, blk["qkv_b"], out=self.qkv)
+            ops.attention_qkv(self.qkv, 1, T, cfg.heads, cfg.head_dim, self.a)
+            ops.gemm(self.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=self.x, out=self.x)
+            ops.layer_norm(self.x, blk["ln2_w"], blk["ln2_b"], cfg.eps, out=self.h)
+            ops.gemm(self.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True, out=self.f[:, :cfg.ff])
+            ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x,
+                     out2=self.xb)
+            ops.gemm(self.xb, blk["gate_w"], blk["gate_ld"], Wd, 2 * Wd, blk["gate_b"], out=self.G)
+            ops.rglru(self.G, blk["a_param"], self.state[i], self.x, cfg.lru_c, self.first)
+        ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+        self.first = False
+        return self.out

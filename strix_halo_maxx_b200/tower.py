@@ -1,0 +1,232 @@
+"""The moondream2 SigLIP-style vision tower on B200: the hot path FastMD2._vision computes
+(moondream/gpu/md2fast.py:147-160), re-planned for sm_100a.
+
+Per block (md2fast.py:153-157), with the residual stream x kept in fp32 in HBM:
+    h   = LN1(x)                               vt_layernorm     fp32 -> bf16
+    qkv = h . Wqkv^T + b                       vt_gemm_ex       tcgen05, bf16 out [M, 3456]
+    a   = attention(qkv)                       vt_attn_fwd      Q/K/V read in place, d 72 -> 80 on chip
+    x   = x + a . Wo^T + b                     vt_gemm_ex       residual epilogue, fp32 in place
+    h   = LN2(x)                               vt_layernorm
+    f   = gelu(h . W1^T + b)                   vt_gemm_ex       GELU-tanh epilogue, bf16 [M, 4304]
+    x   = x + f . W2^T + b                     vt_gemm_ex       residual epilogue
+Patch embed (md2fast.py:148-150): vt_im2col (normalise + (c, py, px) patch order, K 588 in a 592 pitch)
+then vt_gemm_ex with the positional embedding as a row-periodic (period 729) fp32 addend.
+post-LN (md2fast.py:158) -> bf16 features; projection (md2fast.py:159-160) -> two GEMMs.
+
+Crops are independent through every GEMM, so a batch of B crops is one M = 729*B GEMM (tiles span crop
+boundaries); attention stays per crop (grid over crops x heads).  Buffers are allocated once per batch
+size and reused, so a forward allocates nothing and can be captured in a CUDA graph.
+"""
+import torch
+
+from .config import TOWER, TowerConfig
+from . import ops
+from .ops import BF16, _pad8
+
+F32 = torch.float32
+
+
+def _dev_mat(a, dev):
+    """fp32 [N, K] -> bf16 [N, pad8(K)] on device (pad columns zero); returns (buffer, pitch)."""
+    t = torch.as_tensor(a)
+    N, K = t.shape
+    buf = torch.zeros(N, _pad8(K), dtype=BF16, device=dev)
+    buf[:, :K] = t.to(dev, BF16)
+    return buf, buf.stride(0)
+
+
+def _dev_vec(a, dev):
+    return torch.as_tensor(a).to(dev, F32).contiguous()
+
+
+class _Bufs:
+    def __init__(self, cfg: TowerConfig, B, dev):
+        M = B * cfg.ntok
+        W = cfg.width
+        self.B, self.M = B, M
+        self.a_pe = torch.zeros(M, _pad8(cfg.patch_k), dtype=BF16, device=dev)
+        self.x = torch.empty(M, W, dtype=F32, device=dev)
+        self.h = torch.empty(M, W, dtype=BF16, device=dev)
+        self.qkv = torch.empty(M, cfg.qkv_dim, dtype=BF16, device=dev)
+        self.a = torch.empty(M, W, dtype=BF16, device=dev)
+        self.f = torch.empty(M, _pad8(cfg.ff), dtype=BF16, device=dev)
+        self.feats = torch.empty(M, W, dtype=BF16, device=dev)
+
+
+class VisionTower:
+    """Patch-embed + n_blocks pre-LN blocks + post-LN (+ projection MLP) with device-resident weights.
+
+    weights: dict as produced by strix_halo_maxx_b200.weights.tower_weights (fp32 numpy or torch).
+    eps: LayerNorm eps (the benchmark configs use 1e-6; the reference's _ln uses torch's 1e-5).
+    """
+
+    def __init__(self, weights, cfg: TowerConfig = TOWER, eps=None, device="cuda", projection=True):
+        self.cfg = cfg
+        self.eps = cfg.eps if eps is None else float(eps)
+        dev = self.dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = self.dev = torch.device("cuda", torch.cuda.current_device())
+        W = weights
+        self.n_blocks = sum(1 for k in W if k.endswith(".qkv_w"))
+        self.pe_w, self.pe_ld = _dev_mat(W["patch_w"], dev)
+        self.pe_b = _dev_vec(W["patch_b"], dev)
+        self.pos = _dev_vec(W["pos_emb"], dev).reshape(cfg.ntok, cfg.width)
+        self.blocks = []
+        for i in range(self.n_blocks):
+            p = f"blocks.{i}."
+            blk = {}
+            for n in ("qkv", "proj", "fc1", "fc2"):
+                blk[n + "_w"], blk[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
+                blk[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
+            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b"):
+                blk[n] = _dev_vec(W[p + n], dev)
+            self.blocks.append(blk)
+        self.post_w = _dev_vec(W["post_ln_w"], dev)
+        self.post_b = _dev_vec(W["post_ln_b"], dev)
+        self.has_projection = projection and "proj_fc1_w" in W
+        if self.has_projection:
+            self.p1_w, self.p1_ld = _dev_mat(W["proj_fc1_w"], dev)
+            self.p1_b = _dev_vec(W["proj_fc1_b"], dev)
+            self.p2_w, self.p2_ld = _dev_mat(W["proj_fc2_w"], dev)
+            self.p2_b = _dev_vec(W["proj_fc2_b"], dev)
+        self._bufs = {}
+        self._proj_bufs = {}
+        self.op_timer = None   # optional callable(name, flops) -> context manager (bench.py times every launch)
+
+    # ------------------------------------------------------------------ buffers
+    def buffers(self, B):
+        if B not in self._bufs:
+            self._bufs[B] = _Bufs(self.cfg, B, self.dev)
+        return self._bufs[B]
+
+    def _op(self, name, flops, fn, *args, **kw):
+        if self.op_timer is None:
+            return fn(*args, **kw)
+        with self.op_timer(name, flops):
+            return fn(*args, **kw)
+
+    def _gemm(self, name, x2, w, ldw, K, N, bias, **kw):
+        return self._op("gemm_" + name, 2 * x2.shape[0] * K * N, ops.gemm, x2, w, ldw, K, N, bias, **kw)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, pix, out=None, n_blocks=None):
+        """pix: [B, 3, 378, 378] fp32 / bf16 (values in [-1, 1]) or uint8 [B, 378, 378, 3] on the device.
+        Returns post-LN features [B, 729, width] bf16 (written into `out` when given)."""
+        cfg = self.cfg
+        B = pix.shape[0]
+        nb = self.n_blocks if n_blocks is None else n_blocks
+        if B == 0:
+            return torch.empty(0, cfg.ntok, cfg.width, dtype=BF16, device=self.dev) if out is None else out
+        bf = self.buffers(B)
+        T, Wd, H, D = cfg.ntok, cfg.width, cfg.heads, cfg.head_dim
+        self._op("im2col", 0, ops.im2col, pix, cfg.patch, bf.a_pe)
+        self._gemm("patch", bf.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
+                   res=self.pos, res_period=T, out=bf.x)
+        self._blocks(bf, B, nb)
+        dst = bf.feats if out is None else out.reshape(B * T, Wd)
+        self._op("layernorm", 0, ops.layer_norm, bf.x, self.post_w, self.post_b, self.eps, out=dst)
+        return dst.reshape(B, T, Wd)
+
+    def run_blocks(self, x, n_blocks=None):
+        """Config 0: the encoder blocks alone on a residual input x [B, 729, width] fp32 (device);
+        returns the fp32 residual stream after the last block (a view of an internal buffer)."""
+        B = x.shape[0]
+        bf = self.buffers(B)
+        bf.x.copy_(x.reshape(bf.M, self.cfg.width))
+        self._blocks(bf, B, self.n_blocks if n_blocks is None else n_blocks)
+        return bf.x.reshape(B, self.cfg.ntok, self.cfg.width)
+
+    def _blocks(self, bf, B, nb):
+        cfg = self.cfg
+        T, Wd, H, D = cfg.ntok, cfg.width, cfg.heads, cfg.head_dim
+        for blk in self.blocks[:nb]:
+            self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln1_w"], blk["ln1_b"], self.eps, out=bf.h)
+            self._gemm("qkv", bf.h, blk["qkv_w"], blk["qkv_ld"], Wd, cfg.qkv_dim, blk["qkv_b"], out=bf.qkv)
+            self._op("attention", 4 * B * T * T * D * H, ops.attention_qkv, bf.qkv, B, T, H, D, bf.a)
+            self._gemm("proj", bf.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=bf.x, out=bf.x)
+            self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln2_w"], blk["ln2_b"], self.eps, out=bf.h)
+            self._gemm("fc1", bf.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True,
+                       out=bf.f[:, :cfg.ff])
+            self._gemm("fc2", bf.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=bf.x,
+                       out=bf.x)
+
+    def project(self, feats2):
+        """Projection MLP (md2fast.py:159-160): [T, 2*width] bf16 -> [T, proj_out] bf16."""
+        assert self.has_projection
+        cfg = self.cfg
+        T = feats2.shape[0]
+        if T not in self._proj_bufs:
+            self._proj_bufs[T] = (torch.empty(T, cfg.proj_hidden, dtype=BF16, device=self.dev),
+                                  torch.empty(T, cfg.proj_out, dtype=BF16, device=self.dev))
+        hid, out = self._proj_bufs[T]
+        x2 = ops.as_gemm_operand(feats2)
+        self._gemm("proj_fc1", x2, self.p1_w, self.p1_ld, 2 * cfg.width, cfg.proj_hidden, self.p1_b, gelu=True, out=hid)
+        self._gemm("proj_fc2", hid, self.p2_w, self.p2_ld, cfg.proj_hidden, cfg.proj_out, self.p2_b, out=out)
+        return out
+
+    def vision_u8(self, img_u8):
+        """The whole of FastMD2._vision: uint8 [378, 378, 3] -> [729, proj_out] bf16 (one crop: cat([x, x]))."""
+        f = self.forward(img_u8.reshape(1, *img_u8.shape[-3:]))
+        cat = torch.empty(self.cfg.ntok, 2 * self.cfg.width, dtype=BF16, device=self.dev)
+        cat[:, :self.cfg.width] = f[0]
+        cat[:, self.cfg.width:] = f[0]
+        return self.project(cat)
+
+    def frame(self, crops):
+        """Config 2: 1 global + n local crops [1+n, 3, 378, 378] -> projected frame features [729, proj_out]."""
+        f = self.forward(crops)
+        comb = torch.empty(self.cfg.ntok, 2 * self.cfg.width, dtype=BF16, device=self.dev)
+        ops.crop_combine(f, comb)
+        return self.project(comb)
+
+
+# ---------------------------------------------------------------------- drop-in for FastMD2._vision
+def _lin_weight(lin):
+    """(weight [N, K], bias [N]) of a reference `Lin` (md2fast.py:33-40) or a VtLin."""
+    if isinstance(lin, ops.VtLin):
+        return lin.w.float().cpu(), (None if lin.b is None else lin.b.float().cpu())
+    return lin.w.float().cpu(), (None if lin.b is None else lin.b.float().cpu())
+
+
+def weights_from_fastmd2(m):
+    """The vision weights of a FastMD2 instance (md2fast.py:89-103) as a tower_weights-style dict."""
+    W = {}
+
+    def put(name, lin):
+        w, b = _lin_weight(lin)
+        W[name + "_w"] = w
+        W[name + "_b"] = torch.zeros(w.shape[0]) if b is None else b
+
+    put("patch", m.patch_emb)
+    W["pos_emb"] = m.pos_emb.float().cpu().reshape(-1, m.pos_emb.shape[-1])
+    for i, b in enumerate(m.vblocks):
+        p = f"blocks.{i}."
+        for n in ("qkv", "proj", "fc1", "fc2"):
+            put(p + n, b[n])
+        W[p + "ln1_w"], W[p + "ln1_b"] = (t.float().cpu() for t in b["ln1"])
+        W[p + "ln2_w"], W[p + "ln2_b"] = (t.float().cpu() for t in b["ln2"])
+    W["post_ln_w"], W["post_ln_b"] = (t.float().cpu() for t in m.post_ln)
+    if getattr(m, "fold_proj", False):
+        raise NotImplementedError("vt_vision: fold_proj=True is not supported (use the stock two-half projection)")
+    put("proj_fc1", m.proj_fc1)
+    put("proj_fc2", m.proj_fc2)
+    return W
+
+
+def vt_vision(self, img_u8):
+    """Drop-in for FastMD2._vision (md2fast.py:147-160): uint8 [378, 378, 3] -> [729, 2048] bf16.
+    The tower is built from the instance's weights on first use and cached on it; LayerNorm eps is
+    torch's default 1e-5, the value the reference's _ln uses (md2fast.py:43-44)."""
+    t = getattr(self, "_vt_tower", None)
+    if t is None:
+        dev = img_u8.device if img_u8.is_cuda else torch.device("cuda")
+        t = self._vt_tower = VisionTower(weights_from_fastmd2(self), TOWER, eps=1e-5, device=dev)
+    return t.vision_u8(img_u8.to(t.dev))
+
+
+def enable(fastmd2_cls):
+    """Swap the B200 tower into a FastMD2 class, the way the reference's bf16emu.enable swaps its
+    emulation in (moondream/gpu/bf16emu.py:148-153).  Returns the previous _vision."""
+    prev = fastmd2_cls._vision
+    fastmd2_cls._vision = vt_vision
+    return prev

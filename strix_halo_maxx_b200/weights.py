@@ -1,0 +1,118 @@
+"""Seeded random-init weights for the two encoders (no checkpoints are available offline).
+
+Every tensor is drawn from its own numpy PCG64 stream, keyed by (seed, tensor index), so the draw
+is identical on any machine and independent of generation order; weights are N(0, 0.02), biases
+zero and LayerNorm gamma = 1, beta = 0 (the BASELINE configs).  `affine="random"` instead draws
+biases N(0, 0.02), gamma 1 + N(0, 0.1) and beta N(0, 0.05) so tests exercise every epilogue term.
+
+Names follow the reference's weight set: moondream/gpu/md2fast.py:89-103 (patch_emb, pos_emb,
+vblocks[i].{ln1,qkv,proj,ln2,fc1,fc2}, post_ln, proj_fc1, proj_fc2).
+"""
+from concurrent.futures import ThreadPoolExecutor
+import numpy as np
+
+from .config import TowerConfig, TapNextConfig
+
+
+def _draw(seed, idx, shape, kind, affine):
+    rng = np.random.default_rng(np.random.SeedSequence([int(seed), int(idx)]))
+    if kind == "w":
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+    if kind == "normal1":
+        return rng.standard_normal(shape, dtype=np.float32)
+    if affine != "random":
+        return np.ones(shape, np.float32) if kind == "gamma" else np.zeros(shape, np.float32)
+    if kind == "gamma":
+        return np.float32(1.0) + rng.standard_normal(shape, dtype=np.float32) * np.float32(0.1)
+    if kind == "beta":
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.05)
+    return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)   # bias
+
+
+def _generate(spec, seed, affine, threads=8):
+    with ThreadPoolExecutor(threads) as ex:
+        arrs = list(ex.map(lambda it: _draw(seed, it[0], it[1][1], it[1][2], affine), enumerate(spec)))
+    return {name: a for (name, _, _), a in zip(spec, arrs)}
+
+
+def tower_spec(cfg: TowerConfig, n_blocks=None, projection=True):
+    W, F = cfg.width, cfg.ff
+    nb = cfg.n_blocks if n_blocks is None else n_blocks
+    s = [("patch_w", (W, cfg.patch_k), "w"), ("patch_b", (W,), "bias"), ("pos_emb", (cfg.ntok, W), "w")]
+    for i in range(nb):
+        p = f"blocks.{i}."
+        s += [(p + "ln1_w", (W,), "gamma"), (p + "ln1_b", (W,), "beta"),
+              (p + "qkv_w", (cfg.qkv_dim, W), "w"), (p + "qkv_b", (cfg.qkv_dim,), "bias"),
+              (p + "proj_w", (W, W), "w"), (p + "proj_b", (W,), "bias"),
+              (p + "ln2_w", (W,), "gamma"), (p + "ln2_b", (W,), "beta"),
+              (p + "fc1_w", (F, W), "w"), (p + "fc1_b", (F,), "bias"),
+              (p + "fc2_w", (W, F), "w"), (p + "fc2_b", (W,), "bias")]
+    s += [("post_ln_w", (W,), "gamma"), ("post_ln_b", (W,), "beta")]
+    if projection:
+        s += [("proj_fc1_w", (cfg.proj_hidden, 2 * W), "w"), ("proj_fc1_b", (cfg.proj_hidden,), "bias"),
+              ("proj_fc2_w", (cfg.proj_out, cfg.proj_hidden), "w"), ("proj_fc2_b", (cfg.proj_out,), "bias")]
+    return s
+
+
+def tower_weights(cfg: TowerConfig, seed=0, n_blocks=None, projection=True, affine="zero"):
+    """dict name -> float32 numpy array (see module docstring for the distribution)."""
+    return _generate(tower_spec(cfg, n_blocks, projection), seed, affine)
+
+
+def tapnext_spec(cfg: TapNextConfig, n_blocks=None):
+    W, F = cfg.width, cfg.ff
+    nb = cfg.n_blocks if n_blocks is None else n_blocks
+    s = [("patch_w", (W, cfg.patch_k), "w"), ("patch_b", (W,), "bias"), ("pos_emb", (cfg.n_img_tok, W), "w")]
+    for i in range(nb):
+        p = f"blocks.{i}."
+        s += [(p + "ln1_w", (W,), "gamma"), (p + "ln1_b", (W,), "beta"),
+              (p + "qkv_w", (3 * W, W), "w"), (p + "qkv_b", (3 * W,), "bias"),
+              (p + "proj_w", (W, W), "w"), (p + "proj_b", (W,), "bias"),
+              (p + "ln2_w", (W,), "gamma"), (p + "ln2_b", (W,), "beta"),
+              (p + "fc1_w", (F, W), "w"), (p + "fc1_b", (F,), "bias"),
+              (p + "fc2_w", (W, F), "w"), (p + "fc2_b", (W,), "bias"),
+              # RG-LRU: input gate Wx, recurrence gate Wa (768 -> 768 each), a_param (softplus argument)
+              (p + "gx_w", (W, W), "w"), (p + "gx_b", (W,), "bias"),
+              (p + "ga_w", (W, W), "w"), (p + "ga_b", (W,), "bias"),
+              (p + "a_param", (W,), "normal1")]
+    s += [("final_ln_w", (W,), "gamma"), ("final_ln_b", (W,), "beta")]
+    return s
+
+
+def tapnext_weights(cfg: TapNextConfig, seed=0, n_blocks=None, affine="zero"):
+    return _generate(tapnext_spec(cfg, n_blocks), seed, affine)
+
+
+def crop_pixels(n, cfg: TowerConfig, seed=1, first=0):
+    """Crops n pixels U[-1,1] as float32 [n, 3, img, img]; crop i uses stream (seed, 1_000_000 + first + i)."""
+    out = np.empty((n, cfg.in_ch, cfg.img, cfg.img), np.float32)
+
+    def one(i):
+        rng = np.random.default_rng(np.random.SeedSequence([int(seed), 1_000_000 + first + i]))
+        out[i] = rng.random((cfg.in_ch, cfg.img, cfg.img), dtype=np.float32) * np.float32(2) - np.float32(1)
+    with ThreadPoolExecutor(8) as ex:
+        list(ex.map(one, range(n)))
+    return out
+
+
+def tapnext_inputs(cfg: TapNextConfig, n_frames, seed=2):
+    """frames U[-1,1] [F, 3, img, img] and point-query tokens N(0,1) [F, n_queries, width]."""
+    rng = np.random.default_rng(np.random.SeedSequence([int(seed), 7]))
+    frames = rng.random((n_frames, cfg.in_ch, cfg.img, cfg.img), dtype=np.float32) * np.float32(2) - np.float32(1)
+    queries = rng.standard_normal((n_frames, cfg.n_queries, cfg.width), dtype=np.float32)
+    return frames, queries
+
+
+def crop_u8(n, cfg: TowerConfig, seed=3):
+    """n uint8 HWC crops [n, img, img, 3] (the input FastMD2._vision takes, md2fast.py:147-148)."""
+    out = np.empty((n, cfg.img, cfg.img, cfg.in_ch), np.uint8)
+    for i in range(n):
+        rng = np.random.default_rng(np.random.SeedSequence([int(seed), 2_000_000 + i]))
+        out[i] = rng.integers(0, 256, (cfg.img, cfg.img, cfg.in_ch), dtype=np.uint8)
+    return out
+
+
+def block_input(cfg: TowerConfig, seed=4, batch=1):
+    """Config 0 block input: activations N(0, 1) [batch, 729, width]."""
+    rng = np.random.default_rng(np.random.SeedSequence([int(seed), 3_000_000]))
+    return rng.standard_normal((batch, cfg.ntok, cfg.width), dtype=np.float32)

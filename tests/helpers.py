@@ -1,0 +1,50 @@
+"""Shared checks: the per-token parity metrics of the north star (max relative L2 error per output
+token <= 2e-2, cosine similarity per token >= 0.999) and golden-fixture loading."""
+import json
+import os
+
+import numpy as np
+import torch
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOK_REL = 2e-2
+TOK_COS = 0.999
+
+
+def token_metrics(out, ref):
+    """(max over tokens of ||out - ref|| / ||ref||, min over tokens of cos(out, ref)); last dim = features."""
+    o = torch.as_tensor(out).double().reshape(-1, out.shape[-1])
+    r = torch.as_tensor(ref).double().reshape(-1, ref.shape[-1])
+    rel = (o - r).norm(dim=-1) / r.norm(dim=-1).clamp_min(1e-30)
+    cos = torch.nn.functional.cosine_similarity(o, r, dim=-1)
+    return float(rel.max()), float(cos.min())
+
+
+def assert_tokens_close(out, ref, rel=TOK_REL, cos=TOK_COS, what=""):
+    r, c = token_metrics(out, ref)
+    assert r <= rel and c >= cos, f"{what}: max per-token rel {r:.3e} (<= {rel}), min cos {c:.6f} (>= {cos})"
+    return r, c
+
+
+def load_golden(name):
+    d = np.load(os.path.join(GOLDEN, name + ".npz"))
+    out = {k: d[k] for k in d.files if k != "meta"}
+    out["meta"] = json.loads(str(d["meta"]))
+    return out
+
+
+def token_probe(dim):
+    """Same fixed directions as tests/golden/make_golden.py."""
+    return np.random.default_rng(np.random.SeedSequence([9, dim])).standard_normal((dim, 8))
+
+
+def golden_rel(out, g):
+    """Compare a full output [T, D] against a golden fixture: (max rel over the stored rows,
+    max rel of the per-token probes, max rel of per-token sums scaled by the token norm)."""
+    out = np.asarray(torch.as_tensor(out).double().cpu())
+    rows = g["rows"]
+    rr = np.linalg.norm(out[rows] - g["out_rows"], axis=-1) / np.linalg.norm(g["out_rows"], axis=-1)
+    proj = out @ token_probe(out.shape[-1])
+    pr = np.linalg.norm(proj - g["tok_proj"], axis=-1) / np.linalg.norm(g["tok_proj"], axis=-1)
+    sr = np.abs(out.sum(-1) - g["tok_sum"]) / g["tok_norm"]
+    return float(rr.max()), float(pr.max()), float(sr.max())

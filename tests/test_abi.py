@@ -1,0 +1,54 @@
+"""The C-ABI library loads and exports exactly what include/vt_b200.h declares (no compute calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from strix_halo_maxx_b200 import build
+from strix_halo_maxx_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "vt_b200.h")
+
+
+def header_decls():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = {}
+    for m in re.finditer(r"^\s*(?:const\s+)?\w+\**\s+\**(vt_\w+)\s*\(([^;]*?)\)\s*;", src, flags=re.M | re.S):
+        args = m.group(2).strip()
+        n = 0 if args in ("", "void") else len(args.split(","))
+        decls[m.group(1)] = n
+    return decls
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return ctypes.CDLL(_lib.LIB_PATH)
+
+
+def test_header_matches_binding_table():
+    decls = header_decls()
+    assert set(decls) == set(_lib.SIGNATURES), (set(decls) ^ set(_lib.SIGNATURES))
+    for name, n in decls.items():
+        assert len(_lib.SIGNATURES[name][1]) == n, (name, n, len(_lib.SIGNATURES[name][1]))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in header_decls():
+        assert hasattr(lib, name), name
+
+
+def test_binding_loads_and_reports_version():
+    assert _lib.lib().vt_abi_version() == 1
+
+
+def test_errors_are_reported_without_a_gpu():
+    # shape validation happens on the host before any CUDA call
+    L = _lib.lib()
+    rc = L.vt_gemm_bf16(None, 16, 588, 16, 588, None, 16, 8, 4, 8, 588, 0)
+    assert rc == -2 and b"16-byte" in L.vt_last_error_string()
+    rc = L.vt_attn_fwd(None, 16, 16, 16, 16, 1, 10, 2, 72 + 4, *([8] * 12), 1.0)
+    assert rc == -1

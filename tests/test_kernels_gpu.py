@@ -1,0 +1,220 @@
+"""Kernel parity on the GPU, through the C ABI (ctypes), against plain PyTorch fp32 on the same
+bf16-rounded operands.  GEMM shapes: the reference's vision shapes (moondream/gpu/test_hgemm.py:16) plus
+tails and edge cases; tolerance rel < 5e-3 as test_hgemm.py:45.  Attention: the reference's
+(16, 729, 72) strided QKV layout (hattn.py:48-51) and the TAPNext (12, 1280, 64) case."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+from strix_halo_maxx_b200 import ops
+from strix_halo_maxx_b200._lib import lib, device_status, VtError
+
+DEV = "cuda"
+BF = torch.bfloat16
+
+
+def rel(a, b):
+    return float((a.float() - b.float()).norm() / b.float().norm())
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    device_status(clear=True)
+    yield
+    assert device_status(clear=True) == 0, "a kernel recorded a timed-out wait"
+
+
+def _operands(M, K, N, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(M, K, device=DEV, generator=g).to(BF)
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.02).to(BF)
+    b = torch.randn(N, device=DEV, generator=g)
+    return x, w, b
+
+
+VIS = [(729, 1152, 3456), (729, 1152, 1152), (729, 1152, 4304), (729, 4304, 1152), (729, 2304, 8192),
+       (729, 8192, 2048), (729, 588, 1152)]
+EDGE = [(1, 64, 8), (7, 72, 24), (128, 64, 256), (129, 1152, 264), (300, 8, 40), (9477, 1152, 3456), (2048, 4304, 1152)]
+
+
+@pytest.mark.parametrize("M,K,N", VIS + EDGE)
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_bf16(M, K, N, gelu):
+    x, w, b = _operands(M, K, N)
+    lin = ops.VtLin(w, b)
+    out = lin(x, gelu=gelu)
+    ref = F.linear(x.float(), w.float(), b)
+    if gelu:
+        ref = F.gelu(ref.to(BF).float(), approximate="tanh")
+    assert out.shape == (M, N) and out.dtype == BF
+    assert rel(out, ref) < 5e-3
+
+
+@pytest.mark.parametrize("M,K,N", [(729, 1152, 1152), (1458, 4304, 1152), (77, 200, 96)])
+@pytest.mark.parametrize("res_dtype", [torch.float32, BF])
+def test_gemm_residual(M, K, N, res_dtype):
+    x, w, b = _operands(M, K, N, 1)
+    res = torch.randn(M, N, device=DEV).to(res_dtype)
+    out = ops.VtLin(w, b)(x, res=res)
+    ref = F.linear(x.float(), w.float(), b) + res.float()
+    assert out.dtype == res_dtype
+    assert rel(out, ref) < 5e-3
+
+
+def test_gemm_inplace_residual_periodic_addend_and_bf16_copy():
+    M, K, N, P = 3 * 729, 592, 1152, 729
+    x, w, b = _operands(M, K, N, 2)
+    pos = torch.randn(P, N, device=DEV)
+    out = torch.empty(M, N, device=DEV)
+    ops.gemm(x, w, K, K, N, b, res=pos, res_period=P, out=out)
+    ref = F.linear(x.float(), w.float(), b) + pos.repeat(3, 1)
+    assert rel(out, ref) < 5e-3
+    x2 = out.clone()
+    copy = torch.empty(M, N, device=DEV, dtype=BF)
+    ops.gemm(x, w, K, K, N, b, res=x2, out=x2, out2=copy)       # in place: x2 += x . w^T + b
+    ref2 = ref + F.linear(x.float(), w.float(), b)
+    assert rel(x2, ref2) < 5e-3
+    assert torch.equal(copy, x2.to(BF))
+
+
+def test_gemm_k588_in_padded_pitch_matches_contiguous():
+    M, K, N = 729, 588, 1152
+    x, w, b = _operands(M, K, N, 3)
+    buf = torch.zeros(M, 592, device=DEV, dtype=BF)
+    buf[:, :K] = x
+    a = ops.VtLin(w, b)(buf[:, :K])
+    c = ops.VtLin(w, b)(x)      # copied into a padded operand by the wrapper
+    assert torch.equal(a, c)
+
+
+def test_gemm_empty_and_errors():
+    x, w, b = _operands(8, 64, 16)
+    out = torch.empty(0, 16, device=DEV, dtype=BF)
+    assert lib().vt_gemm_bf16(0, x.data_ptr(), 64, w.data_ptr(), 64, None, out.data_ptr(), 16, 0, 16, 64, 0) == 0
+    with pytest.raises(VtError):
+        ops.gemm(x, w, 64, 64, 16, b, gelu=True, out_f32=True)
+    bad = torch.empty(8, 70, device=DEV, dtype=BF)
+    assert lib().vt_gemm_bf16(0, bad.data_ptr(), 70, w.data_ptr(), 64, None, out.data_ptr(), 16, 8, 16, 64, 0) == -2
+
+
+def test_gemm_graph_replay_bit_exact():
+    """test_hgemm.py:51-67: a captured launch replays bit-exactly like eager."""
+    M, K, N = 729, 1152, 4304
+    x, w, b = _operands(M, K, N, 4)
+    lin = ops.VtLin(w, b)
+    xin = x.clone()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        lin(xin, gelu=True)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = lin(xin, gelu=True)
+    x2 = torch.randn_like(x.float()).to(BF)
+    xin.copy_(x2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, lin(x2, gelu=True))
+
+
+def test_gemm_rows_are_batch_invariant():
+    """A row's result does not depend on which M tile it lands in (fixed K order): crops batched into
+    one GEMM give bit-identical features to crops run alone."""
+    K, N = 1152, 3456
+    x, w, b = _operands(3 * 729, K, N, 5)
+    lin = ops.VtLin(w, b)
+    full = lin(x)
+    one = lin(x[729:1458].contiguous())
+    assert torch.equal(full[729:1458], one)
+
+
+def _attn_ref(q, k, v):
+    return F.scaled_dot_product_attention(q.float(), k.float(), v.float())
+
+
+@pytest.mark.parametrize("B,H,T,D", [(1, 16, 729, 72), (3, 16, 729, 72), (1, 12, 1280, 64), (2, 2, 1, 72),
+                                     (1, 3, 7, 16), (2, 4, 65, 64), (1, 1, 200, 80)])
+def test_attention_strided_qkv(B, H, T, D):
+    qkv = torch.randn(B, T, 3 * H * D, device=DEV).to(BF)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    out = ops.VtAttn(H, T, D)(q, k, v)
+    ref = _attn_ref(q, k, v).transpose(1, 2).reshape(B, T, H * D)
+    assert rel(out, ref) < 1e-2
+    sdpa_bf16 = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, T, H * D)
+    assert rel(out, ref) < 3 * max(rel(sdpa_bf16, ref), 2e-3)
+
+
+def test_attention_qkv_buffer_path_matches_views():
+    B, H, T, D = 2, 16, 729, 72
+    qkv = torch.randn(B * T, 3 * H * D, device=DEV).to(BF)
+    out = torch.empty(B * T, H * D, device=DEV, dtype=BF)
+    ops.attention_qkv(qkv, B, T, H, D, out)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.view(B, T, -1).chunk(3, dim=-1)]
+    assert torch.equal(out.view(B, T, -1), ops.VtAttn(H, T, D)(q, k, v))
+
+
+def test_attention_large_logits_stay_finite():
+    B, H, T, D = 1, 2, 300, 72
+    qkv = (torch.randn(B, T, 3 * H * D, device=DEV) * 8).to(BF)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    out = ops.VtAttn(H, T, D)(q, k, v)
+    assert torch.isfinite(out.float()).all()
+    assert rel(out, _attn_ref(q, k, v).transpose(1, 2).reshape(B, T, -1)) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,in_bf16,out_f32", [(729, 1152, False, False), (1280, 768, False, True),
+                                                 (5, 1152, True, False), (33, 2048, False, False), (3, 4096, True, True)])
+def test_layernorm(M, N, in_bf16, out_f32):
+    x = (torch.randn(M, N, device=DEV) * 3 + 0.5)
+    if in_bf16:
+        x = x.to(BF)
+    w = torch.randn(N, device=DEV)
+    b = torch.randn(N, device=DEV)
+    out = ops.layer_norm(x, w, b, 1e-6, out_f32=out_f32)
+    ref = F.layer_norm(x.float(), (N,), w, b, 1e-6)
+    assert rel(out, ref) < (1e-5 if out_f32 else 4e-3)
+
+
+@pytest.mark.parametrize("kind", [torch.float32, BF, torch.uint8])
+def test_im2col(kind):
+    from oracle.tower_ref import im2col, normalize_u8
+    B = 2
+    if kind == torch.uint8:
+        pix = torch.randint(0, 256, (B, 378, 378, 3), dtype=torch.uint8, device=DEV)
+        ref = im2col(normalize_u8(pix.cpu()))
+    else:
+        pix = (torch.rand(B, 3, 378, 378, device=DEV) * 2 - 1).to(kind)
+        ref = im2col(pix.float().cpu())
+    out = torch.zeros(B * 729, 592, device=DEV, dtype=BF)
+    ops.im2col(pix, 14, out)
+    assert torch.equal(out[:, :588].cpu(), ref.reshape(-1, 588).to(BF))
+    assert not out[:, 588:].any()
+
+
+def test_crop_combine():
+    f = torch.randn(13, 729, 1152, device=DEV).to(BF)
+    out = torch.empty(729, 2304, device=DEV, dtype=BF)
+    ops.crop_combine(f, out)
+    assert torch.equal(out[:, :1152], f[0])
+    assert rel(out[:, 1152:], f[1:].float().mean(0)) < 4e-3
+
+
+@pytest.mark.parametrize("first", [True, False])
+def test_rglru(first):
+    from oracle.tapnext_ref import rglru as rglru_ref
+    M, W = 1280, 768
+    x = torch.randn(M, W, device=DEV)
+    h0 = torch.randn(M, W, device=DEV)
+    Wd = {"blocks.0.gx_w": torch.randn(W, W) * 0.02, "blocks.0.gx_b": torch.randn(W) * 0.1,
+          "blocks.0.ga_w": torch.randn(W, W) * 0.02, "blocks.0.ga_b": torch.randn(W) * 0.1,
+          "blocks.0.a_param": torch.randn(W)}
+    G = torch.cat([F.linear(x.cpu(), Wd["blocks.0.gx_w"], Wd["blocks.0.gx_b"]),
+                   F.linear(x.cpu(), Wd["blocks.0.ga_w"], Wd["blocks.0.ga_b"])], 1).to(DEV)
+    ref = rglru_ref(x.cpu(), Wd, "blocks.0.", None if first else h0.cpu(), 8.0)
+    state, xx = h0.clone(), x.clone()
+    ops.rglru(G, Wd["blocks.0.a_param"].to(DEV), state, xx, 8.0, first)
+    assert rel(state, ref) < 1e-5
+    assert rel(xx, x + ref.to(DEV)) < 1e-5

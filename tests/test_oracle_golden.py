@@ -1,0 +1,71 @@
+"""Pin the CPU oracle (oracle/tower_ref.py) to the reference: the fixtures in tests/golden were produced
+by the reference's own FastMD2._vision (moondream/gpu/md2fast.py:147-160) on the same seeded weights
+and inputs (tests/golden/make_golden.py)."""
+import numpy as np
+import pytest
+import torch
+
+from strix_halo_maxx_b200.config import TowerConfig
+from strix_halo_maxx_b200 import weights as wg
+from oracle import tower_ref
+from helpers import load_golden, golden_rel
+
+CFG = TowerConfig()
+TOL = 2e-4   # fp32 vs fp32 (same algorithm, possibly different summation order)
+
+
+def _weights(meta):
+    W = wg.tower_weights(CFG, seed=meta["wseed"], n_blocks=meta["n_blocks"], affine=meta["affine"])
+    return W
+
+
+@pytest.mark.parametrize("name", ["vision_u8_27_zero", "vision_u8_2_random"])
+def test_vision_u8(name):
+    g = load_golden(name)
+    m = g["meta"]
+    W = _weights(m)
+    assert np.allclose(g["wsum"], [np.abs(W["patch_w"]).sum(), np.abs(W["blocks.0.qkv_w"]).sum(),
+                                   np.abs(W["pos_emb"]).sum()], rtol=1e-6), "weight generator drifted"
+    img = wg.crop_u8(1, CFG, seed=m["img_seed"])[0]
+    out = tower_ref.vision_u8(img, W, CFG, eps=m["eps"], n_blocks=m["n_blocks"])
+    assert max(golden_rel(out, g)) < TOL
+
+
+@pytest.mark.parametrize("name", ["tower_u8_27_zero", "tower_u8_2_random"])
+def test_tower_u8(name):
+    g = load_golden(name)
+    m = g["meta"]
+    W = _weights(m)
+    img = wg.crop_u8(1, CFG, seed=m["img_seed"])[0]
+    out = tower_ref.tower(tower_ref.normalize_u8(img), W, CFG, eps=m["eps"], n_blocks=m["n_blocks"])[0]
+    assert max(golden_rel(out, g)) < TOL
+
+
+def test_tower_pixels():
+    g = load_golden("tower_pix_27_zero")
+    m = g["meta"]
+    W = _weights(m)
+    pix = wg.crop_pixels(1, CFG, seed=m["pix_seed"])
+    out = tower_ref.tower(torch.from_numpy(pix), W, CFG, eps=m["eps"], n_blocks=27)[0]
+    assert max(golden_rel(out, g)) < TOL
+
+
+def test_block():
+    g = load_golden("block_1_random")
+    m = g["meta"]
+    W = _weights(m)
+    x = torch.from_numpy(wg.block_input(CFG, seed=m["x_seed"]))
+    out = tower_ref.block(x, W, 0, CFG.heads, m["eps"])[0]
+    assert max(golden_rel(out, g)) < TOL
+
+
+def test_golden_detects_a_planted_error():
+    """The comparison is not vacuous: an oracle with a wrong eps (1e-6 instead of the reference's 1e-5) on
+    the 2-block affine case, or a transposed im2col, fails it."""
+    g = load_golden("tower_u8_2_random")
+    m = g["meta"]
+    W = _weights(m)
+    img = wg.crop_u8(1, CFG, seed=m["img_seed"])[0]
+    pix = tower_ref.normalize_u8(img)
+    bad = tower_ref.tower(pix.transpose(2, 3), W, CFG, eps=m["eps"], n_blocks=2)[0]
+    assert max(golden_rel(bad, g)) > 1e-2
