@@ -61,6 +61,12 @@ int vt_attn_fwd(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const
 int vt_layernorm(cudaStream_t stream, const void* x, long long ldx, int in_bf16, const float* gamma,
                  const float* beta, void* y, long long ldy, int out_f32, int M, int N, float eps);
 
+/* y = x * rsqrt(mean(x^2) + eps) * gamma (RMSNorm) over rows of N, layout rules of vt_layernorm.
+ * Replaces: the temporal pre-norm (RMSNorm) of the TAPNext recurrent block, tapnext/npu/step8.py:474
+ * (the NPU's "rms" EW op, tapnext/npu/pack8.py:115-121). */
+int vt_rmsnorm(cudaStream_t stream, const void* x, long long ldx, int in_bf16, const float* gamma, void* y,
+               long long ldy, int out_f32, int M, int N, float eps);
+
 /* Patch im2col into A[B*(S/P)^2][C*P*P] (bf16, pitch ldo) with K order (c, py, px); pixel kinds:
  * 0 fp32 NCHW, 1 bf16 NCHW, 2 uint8 NHWC normalised (u/255 - 0.5)/0.5.
  * Replaces: the normalise + reshape/permute of moondream/gpu/md2fast.py:148-149. */
@@ -73,11 +79,12 @@ int vt_im2col(cudaStream_t stream, const void* pix, int kind, int B, int C, int 
 int vt_crop_combine(cudaStream_t stream, const uint16_t* f, long long crop_stride, long long ldf, int n_crops, int T,
                     int W, uint16_t* out, long long ldo);
 
-/* RG-LRU recurrence step over M tokens of width W: G = [gx_pre | ga_pre] fp32, state and x fp32 updated in
- * place (state <- h, x <- x + h); first != 0 starts a sequence.
+/* RG-LRU recurrence step over M tokens of width W on the bf16 input u (the normalised stream):
+ * G = [gx_pre | ga_pre] fp32; state and the residual stream x fp32, updated in place (state <- h,
+ * x <- x + h); first != 0 starts a sequence.
  * Replaces: the RG-LRU forward restated in tapnext/npu/r9/cpuemu.py:33-47 (the NPU's EW SSM op). */
-int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_param, float* state, long long lds,
-             float* x, long long ldx, int M, int W, float c, int first);
+int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_param, const uint16_t* u,
+             long long ldu, float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first);
 
 #ifdef __cplusplus
 }

@@ -3,10 +3,12 @@
 Token layout: 8x8 patch conv of a 256x256 frame (1024 tokens) + image position embedding, then the
 256 point-query tokens (tapnext/npu/step8.py:251-267).  Each of the 12 blocks is a pre-LN ViT block
 (LN -> MHA -> +, LN -> MLP GELU -> +, the vit_block part of step8.py:482-485) followed by a residual
-per-token RG-LRU whose step is tapnext/npu/r9/cpuemu.py:33-47 with exact transcendentals:
-    gx = sigmoid(Wx x + bx), ga = sigmoid(Wa x + ba), log_a = -c * ga * softplus(a_param), a = exp(log_a)
-    h = x * gx                                  (first frame, h0 is None)
-    h = a * h0 + (x * gx) * sqrt(1 - a^2)        (later frames)
+temporal block in the reference's shape (step8.py:474-480: pre-norm, recurrence, + x): t = RMSNorm(x)
+(gamma folded, eps 1e-6), then the per-token RG-LRU of tapnext/npu/r9/cpuemu.py:33-47 on t with exact
+transcendentals:
+    gx = sigmoid(Wx t + bx), ga = sigmoid(Wa t + ba), log_a = -c * ga * softplus(a_param), a = exp(log_a)
+    h = t * gx                                  (first frame, h0 is None)
+    h = a * h0 + (t * gx) * sqrt(1 - a^2)        (later frames)
     x <- x + h, state <- h (float32)
 then the encoder LayerNorm (step8.py:488).  The BASELINE config simplifies the reference block (no
 RMSNorm / conv1d / gated MLP, dense gates), and the vendored model is not in the repository, so
@@ -30,6 +32,11 @@ def rglru(x, W, p, h0, c):
     return a * h0 + gated * torch.sqrt(-torch.expm1(2.0 * log_a))
 
 
+def rms_norm(x, w, eps):
+    """x * rsqrt(mean(x^2) + eps) * w (the temporal pre-norm, step8.py:474)."""
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * _t(w)
+
+
 def step(frame, queries, W, cfg, state=None, n_blocks=None):
     """frame [3, 256, 256] in [-1, 1], queries [256, 768] -> (features [1280, 768], new state list)."""
     nb = cfg.n_blocks if n_blocks is None else n_blocks
@@ -46,7 +53,8 @@ def step(frame, queries, W, cfg, state=None, n_blocks=None):
             x = x + linear(a, W[p + "proj_w"], W[p + "proj_b"])
             h = layer_norm(x, W[p + "ln2_w"], W[p + "ln2_b"], cfg.eps)
             x = x + linear(gelu(linear(h, W[p + "fc1_w"], W[p + "fc1_b"])), W[p + "fc2_w"], W[p + "fc2_b"])
-            hs = rglru(x, W, p, None if state is None else state[i], cfg.lru_c)
+            t = rms_norm(x, W[p + "rms_w"], cfg.eps)
+            hs = rglru(t, W, p, None if state is None else state[i], cfg.lru_c)
             new_state.append(hs)
             x = x + hs
         out = layer_norm(x, W["final_ln_w"], W["final_ln_b"], cfg.eps)[0]

@@ -20,9 +20,10 @@ SIGNATURES = {
     "vt_gemm_ex": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL]),
     "vt_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, F]),
     "vt_layernorm": (I, [P, P, LL, I, P, P, P, LL, I, I, I, F]),
+    "vt_rmsnorm": (I, [P, P, LL, I, P, P, LL, I, I, I, F]),
     "vt_im2col": (I, [P, P, I, I, I, I, I, P, LL]),
     "vt_crop_combine": (I, [P, P, LL, LL, I, I, I, P, LL]),
-    "vt_rglru": (I, [P, P, LL, P, P, LL, P, LL, I, I, F, I]),
+    "vt_rglru": (I, [P, P, LL, P, P, LL, P, LL, P, LL, I, I, F, I]),
 }
 
 

@@ -31,8 +31,9 @@ __device__ __forceinline__ void store4(void* base, long long idx, float4 v, int 
 // LayerNorm over rows of N (N % 4 == 0, N <= 4096): one warp per row, the row held in registers
 // (two-pass mean / variance in fp32), y = (x - mean) * rsqrt(var + eps) * gamma + beta.
 // Follows F.layer_norm as md2fast.py:43-44 calls it.
+// RMS = true gives RMSNorm instead: y = x * rsqrt(mean(x^2) + eps) * gamma (+ beta when given).
 constexpr int LN_MAXV = 32;  // float4 per lane, upper bound (N <= 4096)
-template <int MAXV>
+template <int MAXV, bool RMS>
 __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long ldx, int in_bf16, const float* g,
                                                         const float* bta, void* y, long long ldy, int out_f32, int M,
                                                         int N, float eps) {
@@ -50,7 +51,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
       s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
     }
   }
-  const float mean = warp_sum(s) / (float)N;
+  const float mean = RMS ? 0.f : warp_sum(s) / (float)N;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXV; i++) {
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
     const int c = (i * 32 + lane);
     if (c < nv) {
       const float4 gg = *reinterpret_cast<const float4*>(g + 4 * c);
-      const float4 bb = *reinterpret_cast<const float4*>(bta + 4 * c);
+      const float4 bb = bta ? *reinterpret_cast<const float4*>(bta + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 o;
       o.x = (v[i].x - mean) * rstd * gg.x + bb.x;
       o.y = (v[i].y - mean) * rstd * gg.y + bb.y;
@@ -136,17 +137,17 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* f, long lo
   }
 }
 
-// RG-LRU step (tapnext/npu/r9/cpuemu.py:33-47), per element (m, n < W):
+// RG-LRU step (tapnext/npu/r9/cpuemu.py:33-47) on the normalised input u, per element (m, n < W):
 //   gx = sigmoid(G[m, n]), ga = sigmoid(G[m, W + n]), log_a = -c * ga * softplus(a_param[n])
-//   h  = x * gx                                              (first frame)
-//   h  = exp(log_a) * h0 + (x * gx) * sqrt(-expm1(2 log_a))   (later frames)
-//   state <- h, x <- x + h     (state and x fp32, updated in place)
+//   h  = u * gx                                              (first frame)
+//   h  = exp(log_a) * h0 + (u * gx) * sqrt(-expm1(2 log_a))   (later frames)
+//   state <- h, x <- x + h     (u bf16; state and the residual stream x fp32, updated in place)
 __device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
 __device__ __forceinline__ float softplusf_(float z) { return z > 20.f ? z : log1pf(expf(z)); }
 
-__global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param, float* state,
-                                                    long long lds, float* x, long long ldx, int M, int W, float c,
-                                                    int first) {
+__global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param,
+                                                    const uint16_t* u, long long ldu, float* state, long long lds,
+                                                    float* x, long long ldx, int M, int W, float c, int first) {
   const int nv = W / 4;
   const long long total = (long long)M * nv;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -156,13 +157,16 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
     const float4 ga4 = *reinterpret_cast<const float4*>(G + m * ldg + W + n);
     const float4 ap4 = *reinterpret_cast<const float4*>(a_param + n);
     float4 x4 = *reinterpret_cast<const float4*>(x + m * ldx + n);
+    const uint2 u2 = *reinterpret_cast<const uint2*>(u + m * ldu + n);
+    const float uv[4] = {__uint_as_float(u2.x << 16), __uint_as_float(u2.x & 0xffff0000u), __uint_as_float(u2.y << 16),
+                         __uint_as_float(u2.y & 0xffff0000u)};
     float4 h4 = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(state + m * lds + n);
     const float gx[4] = {gx4.x, gx4.y, gx4.z, gx4.w}, ga[4] = {ga4.x, ga4.y, ga4.z, ga4.w};
     const float ap[4] = {ap4.x, ap4.y, ap4.z, ap4.w};
     float xv[4] = {x4.x, x4.y, x4.z, x4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
     for (int e = 0; e < 4; e++) {
-      const float gated = xv[e] * sigmoidf_(gx[e]);
+      const float gated = uv[e] * sigmoidf_(gx[e]);
       float h;
       if (first) {
         h = gated;
@@ -185,36 +189,44 @@ static int grid_for(long long work, int threads) {
   return (int)(g < 1 ? 1 : g);
 }
 
+template <bool RMS>
+static int norm_launch(const char* what, cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma,
+                       const float* beta, void* y, long long ldy, int out_f32, int M, int N, float eps) {
+  if (M < 0 || N < 0) return set_error(E_SHAPE, "%s: negative shape", what);
+  if (M == 0) return OK;
+  if (N == 0 || N % 4 || N > 4 * 32 * LN_MAXV) return set_error(E_SHAPE, "%s: N=%d unsupported", what, N);
+  if (!x || !y || !gamma || (!RMS && !beta)) return set_error(E_SHAPE, "%s: null pointer", what);
+  if (ldx < N || ldy < N || ldx % 4 || ldy % 4 || !aligned16(x) || !aligned16(y) || !aligned16(gamma) ||
+      (beta && !aligned16(beta)))
+    return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
+  const long long blocks = ((long long)M + 7) / 8;
+  if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
+  const int per_lane = (N / 4 + 31) / 32;
+#define VT_LN(V) layernorm_kernel<V, RMS><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps)
+  if (per_lane <= 4) VT_LN(4);
+  else if (per_lane <= 8) VT_LN(8);
+  else if (per_lane <= 12) VT_LN(12);
+  else if (per_lane <= 16) VT_LN(16);
+  else VT_LN(32);
+#undef VT_LN
+  return check_launch(what);
+}
 }  // namespace ew
 }  // namespace vt
 
 extern "C" {
 
 // y[M, N] = LayerNorm(x[M, N]) * gamma + beta.  x fp32 (or bf16 when in_bf16), y bf16 (or fp32 when
-// out_f32).  N % 4 == 0, N <= 4096; pitches multiples of 4 (fp32) / 4 (bf16) elements, 16-byte bases.
+// out_f32).  N % 4 == 0, N <= 4096; pitches multiples of 4 elements, 16-byte bases.
 int vt_layernorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma, const float* beta,
                  void* y, long long ldy, int out_f32, int M, int N, float eps) {
-  using namespace vt;
-  if (M < 0 || N < 0) return set_error(E_SHAPE, "vt_layernorm: negative shape");
-  if (M == 0) return OK;
-  if (N == 0 || N % 4 || N > 4 * 32 * ew::LN_MAXV) return set_error(E_SHAPE, "vt_layernorm: N=%d unsupported", N);
-  if (!x || !y || !gamma || !beta) return set_error(E_SHAPE, "vt_layernorm: null pointer");
-  if (ldx < N || ldy < N || ldx % 4 || ldy % 4 || !aligned16(x) || !aligned16(y) || !aligned16(gamma) || !aligned16(beta))
-    return set_error(E_SHAPE, "vt_layernorm: pitches / alignment invalid");
-  const long long blocks = ((long long)M + 7) / 8;
-  if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "vt_layernorm: M too large");
-  const int per_lane = (N / 4 + 31) / 32;
-  if (per_lane <= 4)
-    ew::layernorm_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
-  else if (per_lane <= 8)
-    ew::layernorm_kernel<8><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
-  else if (per_lane <= 12)
-    ew::layernorm_kernel<12><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
-  else if (per_lane <= 16)
-    ew::layernorm_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
-  else
-    ew::layernorm_kernel<32><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
-  return check_launch("vt_layernorm");
+  return vt::ew::norm_launch<false>("vt_layernorm", st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+}
+
+// y = x * rsqrt(mean(x^2) + eps) * gamma (RMSNorm), same layout rules as vt_layernorm.
+int vt_rmsnorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma, void* y, long long ldy,
+               int out_f32, int M, int N, float eps) {
+  return vt::ew::norm_launch<true>("vt_rmsnorm", st, x, ldx, in_bf16, gamma, nullptr, y, ldy, out_f32, M, N, eps);
 }
 
 // Patch im2col of B square images (S x S, C channels, patch P) into A[B*(S/P)^2, C*P*P] bf16 with
@@ -243,18 +255,19 @@ int vt_crop_combine(cudaStream_t st, const uint16_t* f, long long crop_stride, l
   return check_launch("vt_crop_combine");
 }
 
-// RG-LRU step over M tokens of width W; G = [gx_pre | ga_pre] fp32 [M][ldg >= 2W]; state and x fp32,
-// updated in place; first != 0 starts a new sequence (state ignored and overwritten).
-int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_param, float* state, long long lds,
-             float* x, long long ldx, int M, int W, float c, int first) {
+// RG-LRU step over M tokens of width W on the bf16 input u; G = [gx_pre | ga_pre] fp32 [M][ldg >= 2W];
+// state and x fp32, updated in place; first != 0 starts a new sequence (state ignored and overwritten).
+int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_param, const uint16_t* u, long long ldu,
+             float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first) {
   using namespace vt;
   if (M < 0 || W <= 0 || W % 4) return set_error(E_SHAPE, "vt_rglru: bad shape");
   if (M == 0) return OK;
-  if (!G || !a_param || !state || !x || ldg < 2LL * W || lds < W || ldx < W || ldg % 4 || lds % 4 || ldx % 4 ||
-      !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(a_param))
+  if (!G || !a_param || !u || !state || !x || ldg < 2LL * W || ldu < W || lds < W || ldx < W || ldg % 4 || ldu % 4 ||
+      lds % 4 || ldx % 4 || !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(a_param) ||
+      (reinterpret_cast<uintptr_t>(u) & 7))
     return set_error(E_SHAPE, "vt_rglru: pitches / alignment invalid");
-  ew::rglru_kernel<<<ew::grid_for((long long)M * (W / 4), 256), 256, 0, st>>>(G, ldg, a_param, state, lds, x, ldx, M, W,
-                                                                             c, first);
+  ew::rglru_kernel<<<ew::grid_for((long long)M * (W / 4), 256), 256, 0, st>>>(G, ldg, a_param, u, ldu, state, lds, x,
+                                                                             ldx, M, W, c, first);
   return check_launch("vt_rglru");
 }
 

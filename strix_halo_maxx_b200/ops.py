@@ -135,6 +135,16 @@ def layer_norm(x2, w, b, eps, out=None, out_f32=False):
     return out
 
 
+def rms_norm(x2, w, eps, out=None, out_f32=False):
+    M, N = x2.shape
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if out_f32 else BF16, device=x2.device)
+    rc = lib().vt_rmsnorm(_stream(), x2.data_ptr(), x2.stride(0), int(x2.dtype == BF16), w.data_ptr(),
+                          out.data_ptr(), out.stride(0), int(out.dtype == torch.float32), M, N, float(eps))
+    check(rc, "vt_rmsnorm")
+    return out
+
+
 PIX_KIND = {torch.float32: 0, BF16: 1, torch.uint8: 2}
 
 
@@ -160,8 +170,9 @@ def crop_combine(feats, out):
     return out
 
 
-def rglru(G, a_param, state, x, c, first):
+def rglru(G, a_param, u, state, x, c, first):
+    """RG-LRU step on the bf16 input u [M, W]: state [M, W] and x [M, W] fp32 updated in place."""
     M, W = x.shape
-    rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), state.data_ptr(), state.stride(0),
-                        x.data_ptr(), x.stride(0), M, W, float(c), int(bool(first)))
+    rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), u.data_ptr(), u.stride(0),
+                        state.data_ptr(), state.stride(0), x.data_ptr(), x.stride(0), M, W, float(c), int(bool(first)))
     check(rc, "vt_rglru")

@@ -1,14 +1,15 @@
 """TAPNext-style per-frame streaming step on B200: 8x8 patch conv of a 256x256 frame
 (1024 tokens) + position embedding, 256 point-query tokens appended (token layout of
-tapnext/npu/step8.py:251-267), 12 x [pre-LN ViT block (12 heads x 64, MLP 3072 GELU) + residual RG-LRU]
+tapnext/npu/step8.py:251-267), 12 x [pre-LN ViT block (12 heads x 64, MLP 3072 GELU) + residual temporal block (RMSNorm pre-norm, RG-LRU,
++ x; the shape of the reference's recurrent block, step8.py:474-480)]
 and the encoder LayerNorm.  The RG-LRU (tapnext/npu/r9/cpuemu.py:33-47) keeps one fp32 state
 [1280, 768] per block, carried across frames in device memory owned by this object; reset() starts a
 new video.
 
 Per block the kernels are the tower's (vt_layernorm, vt_gemm_ex, vt_attn_fwd with d = 64) plus:
-    xb  = bf16 copy of x, written by the fc2 residual epilogue (out2)
-    G   = xb . [Wx; Wa]^T + [bx; ba]        one vt_gemm_ex, N = 1536, fp32 out
-    vt_rglru(G, a_param, state_i, x)        gates, recurrence, state and residual update in one pass
+    t   = RMSNorm(x)                        vt_rmsnorm, bf16 out
+    G   = t . [Wx; Wa]^T + [bx; ba]         one vt_gemm_ex, N = 1536, fp32 out
+    vt_rglru(G, a_param, t, state_i, x)     gates, recurrence, state and residual update in one pass
 """
 import torch
 
@@ -41,7 +42,7 @@ class TapNextStep:
             g = torch.cat([torch.as_tensor(W[p + "gx_w"]), torch.as_tensor(W[p + "ga_w"])], 0)
             blk["gate_w"], blk["gate_ld"] = _dev_mat(g, dev)
             blk["gate_b"] = _dev_vec(torch.cat([torch.as_tensor(W[p + "gx_b"]), torch.as_tensor(W[p + "ga_b"])]), dev)
-            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "a_param"):
+            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "rms_w", "a_param"):
                 blk[n] = _dev_vec(W[p + n], dev)
             self.blocks.append(blk)
         self.fin_w = _dev_vec(W["final_ln_w"], dev)
@@ -49,7 +50,7 @@ class TapNextStep:
         T, Wd = cfg.ntok, cfg.width
         self.a_pe = torch.zeros(cfg.n_img_tok, _pad8(cfg.patch_k), dtype=BF16, device=dev)
         self.x = torch.empty(T, Wd, dtype=F32, device=dev)
-        self.xb = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.t = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.h = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.qkv = torch.empty(T, 3 * Wd, dtype=BF16, device=dev)
         self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
@@ -77,10 +78,10 @@ class TapNextStep:
             ops.gemm(self.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=self.x, out=self.x)
             ops.layer_norm(self.x, blk["ln2_w"], blk["ln2_b"], cfg.eps, out=self.h)
             ops.gemm(self.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True, out=self.f[:, :cfg.ff])
-            ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x,
-                     out2=self.xb)
-            ops.gemm(self.xb, blk["gate_w"], blk["gate_ld"], Wd, 2 * Wd, blk["gate_b"], out=self.G)
-            ops.rglru(self.G, blk["a_param"], self.state[i], self.x, cfg.lru_c, self.first)
+            ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x)
+            ops.rms_norm(self.x, blk["rms_w"], cfg.eps, out=self.t)
+            ops.gemm(self.t, blk["gate_w"], blk["gate_ld"], Wd, 2 * Wd, blk["gate_b"], out=self.G)
+            ops.rglru(self.G, blk["a_param"], self.t, self.state[i], self.x, cfg.lru_c, self.first)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
         self.first = False
         return self.out

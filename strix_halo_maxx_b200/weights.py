@@ -71,7 +71,9 @@ def tapnext_spec(cfg: TapNextConfig, n_blocks=None):
               (p + "ln2_w", (W,), "gamma"), (p + "ln2_b", (W,), "beta"),
               (p + "fc1_w", (F, W), "w"), (p + "fc1_b", (F,), "bias"),
               (p + "fc2_w", (W, F), "w"), (p + "fc2_b", (W,), "bias"),
-              # RG-LRU: input gate Wx, recurrence gate Wa (768 -> 768 each), a_param (softplus argument)
+              # temporal pre-norm (RMSNorm gamma), RG-LRU input gate Wx, recurrence gate Wa (768 -> 768
+              # each) and a_param (softplus argument)
+              (p + "rms_w", (W,), "gamma"),
               (p + "gx_w", (W, W), "w"), (p + "gx_b", (W,), "bias"),
               (p + "ga_w", (W, W), "w"), (p + "ga_b", (W,), "bias"),
               (p + "a_param", (W,), "normal1")]

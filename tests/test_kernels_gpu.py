@@ -16,7 +16,8 @@ BF = torch.bfloat16
 
 
 def rel(a, b):
-    return float((a.float() - b.float()).norm() / b.float().norm())
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).norm() / b.norm())
 
 
 @pytest.fixture(autouse=True)
@@ -194,6 +195,15 @@ def test_im2col(kind):
     assert not out[:, 588:].any()
 
 
+@pytest.mark.parametrize("M,N", [(1280, 768), (7, 1152)])
+def test_rmsnorm(M, N):
+    from oracle.tapnext_ref import rms_norm
+    x = torch.randn(M, N, device=DEV) * 4
+    w = torch.randn(N, device=DEV)
+    out = ops.rms_norm(x, w, 1e-6, out_f32=True)
+    assert rel(out, rms_norm(x.cpu(), w.cpu(), 1e-6)) < 1e-5
+
+
 def test_crop_combine():
     f = torch.randn(13, 729, 1152, device=DEV).to(BF)
     out = torch.empty(729, 2304, device=DEV, dtype=BF)
@@ -207,14 +217,16 @@ def test_rglru(first):
     from oracle.tapnext_ref import rglru as rglru_ref
     M, W = 1280, 768
     x = torch.randn(M, W, device=DEV)
+    u = torch.randn(M, W, device=DEV).to(BF)
     h0 = torch.randn(M, W, device=DEV)
     Wd = {"blocks.0.gx_w": torch.randn(W, W) * 0.02, "blocks.0.gx_b": torch.randn(W) * 0.1,
           "blocks.0.ga_w": torch.randn(W, W) * 0.02, "blocks.0.ga_b": torch.randn(W) * 0.1,
           "blocks.0.a_param": torch.randn(W)}
-    G = torch.cat([F.linear(x.cpu(), Wd["blocks.0.gx_w"], Wd["blocks.0.gx_b"]),
-                   F.linear(x.cpu(), Wd["blocks.0.ga_w"], Wd["blocks.0.ga_b"])], 1).to(DEV)
-    ref = rglru_ref(x.cpu(), Wd, "blocks.0.", None if first else h0.cpu(), 8.0)
+    uf = u.float().cpu()
+    G = torch.cat([F.linear(uf, Wd["blocks.0.gx_w"], Wd["blocks.0.gx_b"]),
+                   F.linear(uf, Wd["blocks.0.ga_w"], Wd["blocks.0.ga_b"])], 1).to(DEV)
+    ref = rglru_ref(uf, Wd, "blocks.0.", None if first else h0.cpu(), 8.0)
     state, xx = h0.clone(), x.clone()
-    ops.rglru(G, Wd["blocks.0.a_param"].to(DEV), state, xx, 8.0, first)
+    ops.rglru(G, Wd["blocks.0.a_param"].to(DEV), u, state, xx, 8.0, first)
     assert rel(state, ref) < 1e-5
     assert rel(xx, x + ref.to(DEV)) < 1e-5
