@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--mb", type=int, default=130, help="crops per chunk and rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-frame", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     return ap.parse_args()
 
 
@@ -175,6 +176,32 @@ def run_reference(a):
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
+def run_e2e(a, tower, n_local, mb, pix_host, feats_all, local_out, dev, world, barrier, max_over_ranks):
+    """Crops/s through HostPipeline.run: pinned host pixels in, pinned host features out, every step."""
+    from strix_halo_maxx_b200.multigpu import HostPipeline
+    cfg = tower.cfg
+    pipe = HostPipeline(tower, n_local, mb)
+    out_host = torch.empty(n_local, cfg.ntok, cfg.width, dtype=torch.bfloat16).pin_memory()
+    pipe.run(pix_host, out_host, feats_all)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(a.steps):
+        pipe.run(pix_host, out_host, feats_all)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    e2e = {"value": a.crops * a.steps / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes(),
+           "d2h_bytes_per_step": pipe.d2h_bytes(), "api": "strix_halo_maxx_b200.multigpu.HostPipeline.run"}
+    # the e2e output must equal the device-resident path
+    e2e_ok = bool(torch.equal(out_host[:mb].to(dev), (local_out if world > 1 else feats_all)[:mb]))
+
+    return e2e, e2e_ok
+
+
 def run_vt(a):
     import torch.distributed as dist
     from datetime import timedelta
@@ -267,25 +294,10 @@ def run_vt(a):
                  for k, v in sorted(ops_summary.items())}
 
     # ---------------- e2e: public host-buffer API, copies inside the timed region
-    pipe = HostPipeline(tower, n_local, mb)
-    out_host = torch.empty(n_local, cfg.ntok, cfg.width, dtype=torch.bfloat16).pin_memory()
-    pipe.run(pix_host, out_host, feats_all)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(a.steps):
-        pipe.run(pix_host, out_host, feats_all)
-    f1.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
-    e2e = {"value": a.crops * a.steps / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes(),
-           "d2h_bytes_per_step": pipe.d2h_bytes(), "api": "strix_halo_maxx_b200.multigpu.HostPipeline.run"}
-    # the e2e output must equal the device-resident path
-    e2e_ok = bool(torch.equal(out_host[:mb].to(dev), (local_out if world > 1 else feats_all)[:mb]))
-
+    e2e, e2e_ok = None, None
+    if not a.no_e2e:
+        e2e, e2e_ok = run_e2e(a, tower, n_local, mb, pix_host, feats_all, local_out, dev, world, barrier,
+                              max_over_ranks)
     # ---------------- config 2 latency: one 13-crop frame (tower + combine + projection)
     frame_ms = None
     if not a.no_frame:

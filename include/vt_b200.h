@@ -55,6 +55,31 @@ int vt_attn_fwd(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const
                 long long sk_h, long long sv_b, long long sv_t, long long sv_h, long long so_b, long long so_t,
                 long long so_h, float scale);
 
+/* Fused QKV projection for attention: A[M = crops*T, K] . W[3*H*D, K]^T + bias, bf16, written straight into
+ * the attention-tile layout vt_attn_tiles_fwd reads (tiles: vt_attn_tiles_bytes(M/T, T, H, D) bytes,
+ * zero-filled once at allocation).
+ * Replaces: the qkv HLin call + chunk/view/transpose of md2fast.py:154 feeding hattn.Attn, whose V^T copy
+ * (vtranspose, attn.hip:284) this layout makes unnecessary. */
+int vt_gemm_qkv_tiles(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
+                      const float* bias, uint16_t* tiles, int M, int K, int T, int H, int D);
+
+/* Size in bytes of the attention-tile buffer for B crops x H heads x T tokens of head_dim D:
+ * layout [B][q|k|v][H][ceil(T/128)][DP/8][128][8] bf16, DP = 64 (D <= 64) or 80.  0 if unsupported. */
+long long vt_attn_tiles_bytes(int B, int T, int H, int D);
+
+/* Strided Q/K/V (element (b,t,h,d) at X + b*sx_b + t*sx_t + h*sx_h + d) -> attention tiles (zero-filled
+ * once at allocation; pads are never written).
+ * Replaces: vtranspose, moondream/gpu/hip/attn.hip:284 (the reference's pre-pass of hattn.Attn). */
+int vt_attn_pack(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* tiles,
+                 int B, int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b,
+                 long long sk_t, long long sk_h, long long sv_b, long long sv_t, long long sv_h);
+
+/* tcgen05 flash attention from attention tiles: O[b,t,h,:D] = softmax(Q K^T * scale) V, S and O in TMEM,
+ * P through shared memory; O element (b,t,h,d) at O + b*so_b + t*so_t + h*so_h + d (strides multiples of 8).
+ * Replaces: attn_fwd2, moondream/gpu/hip/attn.hip:442 (hattn.Attn.__call__, hattn.py:26-37). */
+int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
+                      long long so_b, long long so_t, long long so_h, float scale);
+
 /* y = LayerNorm(x) * gamma + beta over rows of N (N % 4 == 0, N <= 4096); x fp32 (bf16 when in_bf16),
  * y bf16 (fp32 when out_f32); fp32 statistics.
  * Replaces: _ln / F.layer_norm, moondream/gpu/md2fast.py:43-44 (ln1, ln2, post_ln; md2fast.py:153-158). */

@@ -1,0 +1,348 @@
+// Flash attention on the 5th-generation tensor cores (tcgen05 / TMEM), the B200 replacement of the
+// reference's attn_fwd2 (moondream/gpu/hip/attn.hip:142-272, 442) and its V^T copy (vtranspose,
+// attn.hip:275-288) behind hattn.Attn (moondream/gpu/hattn.py:17-37).
+//
+// Operand layout ("attention tiles"): for crop b, operand w (0 q, 1 k, 2 v), head h, 128-token tile tt,
+// 8-element d chunk c, row r:   tiles[((((b*3 + w)*H + h)*Tt + tt)*NC + c)*1024 + r*8 + e]
+// with Tt = ceil(T/128), NC = DP/8, DP = 64 or 80 (head_dim padded to the tensor-core K granularity).
+// One 128-token tile of one operand is NC*2 KB contiguous, in exactly the canonical no-swizzle layout
+// tcgen05 reads (8-row x 16-byte core matrices), so it arrives with one cp.async.bulk.  Rows t >= T and
+// lanes d >= D are zero (the buffer is zeroed once at allocation and never written there).  The tower's
+// QKV GEMM writes this layout from its epilogue; vt_attn_pack builds it from any strided Q/K/V.
+//
+// CTA = one 128-query tile of one (crop, head); 6 warps:
+//   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 128-key tile);
+//   warp 5 lane 0: tcgen05.mma  S = Q K_j^T (M 128, N 128, K DP) into TMEM, then O += P_j V_j (M 128,
+//                  N DP, K 128; V is an MN-major B operand) into a TMEM accumulator;
+//   warps 0-3: softmax, thread i owns query row i (TMEM lane i): row max, P = 2^(s*scale*log2e - m),
+//              bf16 P written to shared memory in the K-major canonical layout, row sums in fp32.
+// O is rescaled only when a row max grows by more than 2^8 (P <= 256 otherwise, exact in fp32
+// accumulation), so TMEM round trips of O are rare.  tcgen05 ops of one thread complete in issue order,
+// so the commit after S_j also means PV_{j-1} is done when softmax sees S_j.
+#include "vt_common.cuh"
+#include "vt_host.h"
+
+namespace vt {
+namespace attn_tc {
+
+constexpr int BQ = 128, BKV = 128, THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;  // S: columns [0, 128), O: [128, 128 + DP)
+constexpr long long kDrainCycles = 200000000LL;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int NC>
+struct Smem {
+  static constexpr int TILE = NC * 2048;  // bytes of one 128-row operand tile
+  static constexpr int Q = 0, K = TILE, V = 2 * TILE, P = 3 * TILE;
+  static constexpr int BAR = P + 16 * 2048;  // P: 16 chunks of 128 rows x 16 B
+  static constexpr int BYTES = BAR + 128;
+};
+
+struct Args {
+  const uint16_t* tiles;
+  uint16_t* o;
+  int T, H, D, Tt;
+  long long so_b, so_t, so_h;
+  float scale_log2;
+  int b0;
+};
+
+template <int NC>
+__global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
+  using L = Smem<NC>;
+  constexpr int DP = NC * 8;
+  constexpr uint32_t TB = L::TILE;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* k_full = bar + 1;
+  uint64_t* k_empty = bar + 2;
+  uint64_t* v_full = bar + 3;
+  uint64_t* v_empty = bar + 4;
+  uint64_t* s_full = bar + 5;
+  uint64_t* p_full = bar + 6;
+  uint64_t* o_full = bar + 7;
+  uint64_t* drain = bar + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tt = blockIdx.x, h = blockIdx.y, b = a.b0 + blockIdx.z;
+  const int T = a.T, H = a.H, Tt = a.Tt;
+  const int nkv = (T + BKV - 1) / BKV;
+  const size_t tile_elems = (size_t)NC * 1024;
+  const uint16_t* q_src = a.tiles + ((((size_t)b * 3 + 0) * H + h) * Tt + tt) * tile_elems;
+  const uint16_t* k_base = a.tiles + ((((size_t)b * 3 + 1) * H + h) * Tt) * tile_elems;
+  const uint16_t* v_base = a.tiles + ((((size_t)b * 3 + 2) * H + h) * Tt) * tile_elems;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 9; i++) mbar_init(&bar[i], 1);
+    mbar_init(p_full, 128);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---------------- bulk loads
+      bool ok = true;
+      int pending_k = -1, pending_v = -1;  // phase of the last armed, not yet observed load
+      mbar_arrive_expect_tx(q_full, TB);
+      bulk_load(sm + L::Q, q_src, TB, q_full);
+      for (int j = 0; j < nkv && ok; j++) {
+        if (j > 0 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(k_full, TB);
+        bulk_load(sm + L::K, k_base + (size_t)j * tile_elems, TB, k_full);
+        pending_k = j & 1;
+        if (j > 0 && !mbar_wait(v_empty, (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(v_full, TB);
+        bulk_load(sm + L::V, v_base + (size_t)j * tile_elems, TB, v_full);
+        pending_v = j & 1;
+      }
+      if (!ok) {  // unwinding: let every copy this thread issued land before the CTA exits
+        mbar_wait_drain(q_full, 0, kDrainCycles);
+        if (pending_k >= 0) mbar_wait_drain(k_full, (uint32_t)pending_k, kDrainCycles);
+        if (pending_v >= 0) mbar_wait_drain(v_full, (uint32_t)pending_v, kDrainCycles);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV);
+      constexpr uint32_t IDESC_O = idesc_bf16(BQ, DP) | (1u << 16);  // B (= V) MN-major
+      const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V),
+                     sp = smem_u32(sm + L::P);
+      bool ok = mbar_wait(q_full, 0, abort_flag, ST_ATTN_MMA);
+      for (int j = 0; j < nkv && ok; j++) {
+        if (!mbar_wait(k_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA = two 8-element chunks, 2048 B apart
+          umma_f16(t_s, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(sk + k * 4096, 2048, 128), IDESC_S,
+                   k > 0 ? 1u : 0u);
+        umma_commit(k_empty);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        if (!mbar_wait(v_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < BKV / 16; k++)  // 16 keys per MMA: P chunks 2k, 2k+1; V rows 16k..16k+15
+          umma_f16(t_o, sdesc_noswz(sp + k * 4096, 2048, 128), sdesc_noswz(sv + k * 256, 128, 2048), IDESC_O,
+                   (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(v_empty);
+      }
+      if (ok) umma_commit(o_full);
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0, kDrainCycles);
+    }
+  } else {
+    // ---------------- softmax warps 0-3: thread = query row
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint8_t* P = sm + L::P;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; j++) {
+      if (!mbar_wait(s_full, j & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
+      tc_fence_after();
+      const int kbase = j * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        uint32_t r[32];
+        tmem_ld32(t_s + lane_off + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e++)
+          if (kbase + c * 32 + e < T) mx = fmaxf(mx, __uint_as_float(r[e]));
+      }
+      mx *= a.scale_log2;
+      if (j == 0) {
+        m_used = mx;
+      } else {
+        const bool need = mx > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {  // O round trip through registers (warp-collective)
+          const float m_new = need ? mx : m_used;
+          const float alpha = exp2f(m_used - m_new);
+          m_used = m_new;
+          l *= alpha;
+#pragma unroll
+          for (int c = 0; c < DP / 16; c++) {
+            uint32_t r[16];
+            tmem_ld16(t_o + lane_off + c * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; e++) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st16(t_o + lane_off + c * 16, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        uint32_t r[32];
+        tmem_ld32(t_s + lane_off + c * 32, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const int k0 = kbase + c * 32 + 2 * e;
+          const float p0 = k0 < T ? exp2f(__uint_as_float(r[2 * e]) * a.scale_log2 - m_used) : 0.f;
+          const float p1 = k0 + 1 < T ? exp2f(__uint_as_float(r[2 * e + 1]) * a.scale_log2 - m_used) : 0.f;
+          sum += p0 + p1;
+          pk[e] = pack_bf2(p0, p1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          *reinterpret_cast<uint4*>(P + (c * 4 + q) * 2048 + row * 16) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+      }
+      l += sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
+      tc_fence_after();
+      const int t = tt * BQ + row;
+      const float inv = 1.f / l;
+      uint16_t* orow = a.o + (size_t)b * a.so_b + (size_t)t * a.so_t + (size_t)h * a.so_h;
+#pragma unroll
+      for (int c = 0; c < DP / 16; c++) {
+        uint32_t r[16];
+        tmem_ld16(t_o + lane_off + c * 16, r);
+        tmem_ld_wait();
+        if (t < T) {
+#pragma unroll
+          for (int half = 0; half < 2; half++) {
+            const int d0 = c * 16 + half * 8;
+            if (d0 < a.D)
+              *reinterpret_cast<uint4*>(orow + d0) =
+                  make_uint4(pack_bf2(__uint_as_float(r[8 * half]) * inv, __uint_as_float(r[8 * half + 1]) * inv),
+                             pack_bf2(__uint_as_float(r[8 * half + 2]) * inv, __uint_as_float(r[8 * half + 3]) * inv),
+                             pack_bf2(__uint_as_float(r[8 * half + 4]) * inv, __uint_as_float(r[8 * half + 5]) * inv),
+                             pack_bf2(__uint_as_float(r[8 * half + 6]) * inv, __uint_as_float(r[8 * half + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Strided Q/K/V -> attention tiles.  One thread per 16-byte chunk (8 elements of d); rows t < T and
+// chunks c < D/8 only (the pads keep their zeros).
+__global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                                                   const uint16_t* __restrict__ v, uint16_t* __restrict__ tiles, int B,
+                                                   int T, int H, int D, int NC, int Tt, long long sq_b, long long sq_t,
+                                                   long long sq_h, long long sk_b, long long sk_t, long long sk_h,
+                                                   long long sv_b, long long sv_t, long long sv_h) {
+  const int dch = D / 8;
+  const long long per_tok = 3LL * H * dch;
+  const long long total = (long long)B * T * per_tok;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i;
+    const int c = (int)(r % dch); r /= dch;
+    const int hh = (int)(r % H); r /= H;
+    const int w = (int)(r % 3); r /= 3;
+    const int t = (int)(r % T);
+    const long long bb = r / T;
+    const uint16_t* src = w == 0 ? q + bb * sq_b + t * sq_t + hh * sq_h
+                        : w == 1 ? k + bb * sk_b + t * sk_t + hh * sk_h
+                                 : v + bb * sv_b + t * sv_t + hh * sv_h;
+    const size_t dst = ((((size_t)bb * 3 + w) * H + hh) * Tt + t / 128) * ((size_t)NC * 1024) + (size_t)c * 1024 +
+                       (size_t)(t % 128) * 8;
+    *reinterpret_cast<uint4*>(tiles + dst) = *reinterpret_cast<const uint4*>(src + c * 8);
+  }
+}
+
+template <int NC>
+static int launch_nc(cudaStream_t st, Args a, int B) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(attn_tc_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<NC>::BYTES);
+    attr_done[dev] = true;
+  }
+  for (int b0 = 0; b0 < B; b0 += 65535) {
+    a.b0 = b0;
+    const int nb = (B - b0) < 65535 ? (B - b0) : 65535;
+    attn_tc_kernel<NC><<<dim3(a.Tt, a.H, nb), THREADS, Smem<NC>::BYTES, st>>>(a);
+    int rc = check_launch("vt_attn_tiles_fwd");
+    if (rc) return rc;
+  }
+  return OK;
+}
+
+static int dp_chunks(int D) { return D <= 64 ? 8 : 10; }
+
+}  // namespace attn_tc
+}  // namespace vt
+
+extern "C" {
+
+// Bytes of the attention-tile buffer for B crops x H heads x T tokens, head_dim D (0 if unsupported).
+long long vt_attn_tiles_bytes(int B, int T, int H, int D) {
+  if (B < 0 || T < 0 || H < 0 || D <= 0 || D % 8 || D > 80) return 0;
+  const long long Tt = (T + 127) / 128;
+  return (long long)B * 3 * H * Tt * vt::attn_tc::dp_chunks(D) * 1024 * 2;
+}
+
+// Strided Q/K/V (element (b,t,h,d) at X + b*sx_b + t*sx_t + h*sx_h + d) -> attention tiles.  `tiles`
+// must hold vt_attn_tiles_bytes(B, T, H, D) bytes and be zero-filled once when allocated.
+int vt_attn_pack(cudaStream_t st, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* tiles, int B,
+                 int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b, long long sk_t,
+                 long long sk_h, long long sv_b, long long sv_t, long long sv_h) {
+  using namespace vt;
+  if (B < 0 || T < 0 || H < 0) return set_error(E_SHAPE, "vt_attn_pack: negative shape");
+  if (B == 0 || T == 0 || H == 0) return OK;
+  if (D <= 0 || D % 8 || D > 80) return set_error(E_VARIANT, "vt_attn_pack: head_dim %d unsupported", D);
+  const long long s16[] = {sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, sv_b, sv_t, sv_h};
+  for (long long s : s16)
+    if (s % 8) return set_error(E_SHAPE, "vt_attn_pack: strides must be multiples of 8 elements");
+  if (!Q || !K || !V || !tiles || !aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(tiles))
+    return set_error(E_SHAPE, "vt_attn_pack: pointers must be 16-byte aligned");
+  const int NC = attn_tc::dp_chunks(D), Tt = (T + 127) / 128;
+  const long long total = (long long)B * T * 3 * H * (D / 8);
+  long long g = (total + 255) / 256;
+  const long long cap = (long long)sm_count() * 16;
+  attn_tc::pack_kernel<<<(int)(g < cap ? (g < 1 ? 1 : g) : cap), 256, 0, st>>>(Q, K, V, tiles, B, T, H, D, NC, Tt, sq_b,
+                                                                               sq_t, sq_h, sk_b, sk_t, sk_h, sv_b,
+                                                                               sv_t, sv_h);
+  return check_launch("vt_attn_pack");
+}
+
+// O[b, t, h, :D] = softmax(Q K^T * scale) V from attention tiles (tcgen05).  O element (b,t,h,d) at
+// O + b*so_b + t*so_t + h*so_h + d; so_* multiples of 8, O 16-byte aligned.
+int vt_attn_tiles_fwd(cudaStream_t st, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D, long long so_b,
+                      long long so_t, long long so_h, float scale) {
+  using namespace vt;
+  if (B < 0 || T < 0 || H < 0) return set_error(E_SHAPE, "vt_attn_tiles_fwd: negative shape");
+  if (B == 0 || T == 0 || H == 0) return OK;
+  if (H > 65535) return set_error(E_SHAPE, "vt_attn_tiles_fwd: H=%d too large", H);
+  if (D <= 0 || D % 8 || D > 80) return set_error(E_VARIANT, "vt_attn_tiles_fwd: head_dim %d unsupported", D);
+  if (!tiles || !O || !aligned16(tiles) || !aligned16(O) || (so_b | so_t | so_h) % 8)
+    return set_error(E_SHAPE, "vt_attn_tiles_fwd: pointers / strides not 16-byte aligned");
+  attn_tc::Args a{tiles, O, T, H, D, (T + 127) / 128, so_b, so_t, so_h, scale * 1.4426950408889634f, 0};
+  if (attn_tc::dp_chunks(D) == 8) return attn_tc::launch_nc<8>(st, a, B);
+  return attn_tc::launch_nc<10>(st, a, B);
+}
+
+}  // extern "C"

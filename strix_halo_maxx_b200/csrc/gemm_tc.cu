@@ -40,6 +40,9 @@ struct Epi {
   int gelu;
   uint16_t* out2;     // optional bf16 copy of an fp32 output, [M][ldo2]
   long long ldo2;
+  // attention-tile output (pk_T > 0): the bf16 result [M = crops*T][3*H*D] is scattered into the tile
+  // layout vt_attn_tiles_fwd reads, ((((b*3 + w)*H + h)*Tt + t/128)*NC + d/8)*1024 + (t%128)*8 + d%8
+  int pk_T, pk_H, pk_D, pk_NC, pk_Tt;
 };
 
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep) {
@@ -119,6 +122,24 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
 #pragma unroll
         for (int j = 0; j < 32; j++)
           if (n0 + j < N) o2[j] = f2bf(v[j]);
+      }
+    }
+  } else if (ep.pk_T > 0) {
+    const int HD = ep.pk_H * ep.pk_D;
+    const long long crop = m / ep.pk_T;
+    const int t = m % ep.pk_T;
+    const size_t tile_elems = (size_t)ep.pk_NC * 1024;
+    uint16_t* base = reinterpret_cast<uint16_t*>(ep.out);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int n = n0 + 8 * j;
+      if (n < N) {
+        const int w = n / HD, rem = n % HD, hh = rem / ep.pk_D, d = rem % ep.pk_D;
+        const size_t off = ((((size_t)crop * 3 + w) * ep.pk_H + hh) * ep.pk_Tt + t / 128) * tile_elems +
+                           (size_t)(d / 8) * 1024 + (size_t)(t % 128) * 8;
+        *reinterpret_cast<uint4*>(base + off) =
+            make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
+                       pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
       }
     }
   } else {
@@ -303,7 +324,7 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
   if (lda < K || ldw < K || lda % 8 || ldw % 8 || !aligned16(A) || !aligned16(W))
     return set_error(E_SHAPE, "vt_gemm: A/W need 16-byte aligned bases and row pitches (lda=%lld ldw=%lld K=%d)", lda,
                      ldw, K);
-  if (ep.ldo < N || ep.ldo % 8 || !aligned16(ep.out))
+  if (ep.pk_T <= 0 && (ep.ldo < N || ep.ldo % 8 || !aligned16(ep.out)))
     return set_error(E_SHAPE, "vt_gemm: output pitch %lld must be >= N=%d, a multiple of 8, 16-byte aligned", ep.ldo,
                      N);
   if (ep.res && (ep.ldr < N || ep.ldr % 8 || !aligned16(ep.res) || ep.res_period < 0))
@@ -341,7 +362,7 @@ extern "C" {
 // C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias, optionally GELU-tanh (after bf16 rounding).
 int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
                  const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu) {
-  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0};
+  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0, 0, 0, 0, 0, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -351,8 +372,23 @@ int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16
 int vt_gemm_ex(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N, int K,
                const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res, long long ldr,
                int res_period, int res_bf16, uint16_t* out2, long long ldo2) {
-  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2};
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
+                   0, 0, 0, 0, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+// Fused QKV projection for attention: A[M = crops*T, K] . W[3*H*D, K]^T + bias, written as bf16 straight
+// into the attention-tile layout of vt_attn_tiles_fwd (`tiles` holds vt_attn_tiles_bytes(M/T, T, H, D)
+// bytes, zero-filled once when allocated; its pad rows and lanes are never written).
+int vt_gemm_qkv_tiles(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
+                      const float* bias, uint16_t* tiles, int M, int K, int T, int H, int D) {
+  using namespace vt;
+  if (T <= 0 || H <= 0 || D <= 0 || D % 8 || D > 80 || M < 0 || M % T)
+    return set_error(E_SHAPE, "vt_gemm_qkv_tiles: M=%d T=%d H=%d D=%d invalid (M a multiple of T, D%%8 == 0, D <= 80)", M,
+                     T, H, D);
+  if (!aligned16(tiles)) return set_error(E_SHAPE, "vt_gemm_qkv_tiles: tiles must be 16-byte aligned");
+  vt::gemm::Epi ep{bias, tiles, 0, nullptr, 0, 0, 0, 0, 0, nullptr, 0, T, H, D, D <= 64 ? 8 : 10, (T + 127) / 128};
+  return vt::gemm::launch(st, A, lda, W, ldw, M, 3 * H * D, K, ep);
 }
 
 }  // extern "C"

@@ -3,4 +3,5 @@
 #include "host_common.cu"
 #include "gemm_tc.cu"
 #include "attn.cu"
+#include "attn_tc.cu"
 #include "elementwise.cu"

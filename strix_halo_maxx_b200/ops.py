@@ -93,13 +93,41 @@ class VtLin:
         return out.reshape(*shp[:-1], self.N)
 
 
+def attn_tiles(B, T, H, D, device):
+    """Zero-filled attention-tile buffer (see vt_attn_tiles_bytes in include/vt_b200.h)."""
+    n = lib().vt_attn_tiles_bytes(B, T, H, D)
+    if n <= 0:
+        raise ValueError(f"attention tiles: unsupported shape B={B} T={T} H={H} D={D}")
+    return torch.zeros(n // 2, dtype=BF16, device=device)
+
+
+def attention_tiles(tiles, B, T, H, D, out, scale=None):
+    """tcgen05 attention from an attention-tile buffer into out [B*T, >= H*D] (row pitch out.stride(0))."""
+    rc = lib().vt_attn_tiles_fwd(_stream(), tiles.data_ptr(), out.data_ptr(), B, T, H, D, T * out.stride(0),
+                                 out.stride(0), D, D ** -0.5 if scale is None else scale)
+    check(rc, "vt_attn_tiles_fwd")
+    return out
+
+
+def gemm_qkv_tiles(x2, w, ldw, K, bias, tiles, T, H, D):
+    """QKV projection written straight into attention tiles (the tower's fused path)."""
+    rc = lib().vt_gemm_qkv_tiles(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, _ptr(bias),
+                                 tiles.data_ptr(), x2.shape[0], K, T, H, D)
+    check(rc, "vt_gemm_qkv_tiles")
+    return tiles
+
+
 class VtAttn:
-    """Flash attention for one (H, T, D) problem: q, k, v are (B, H, T, D) views (any strides over
-    B / H / T, contiguous D) -- e.g. the chunks of a fused QKV output -- and the result is (B, T, H*D)."""
+    """Flash attention for one (H, T, D) problem, the contract of hattn.Attn (hattn.py:17-37): q, k, v are
+    (B, H, T, D) views (any strides over B / H / T, contiguous D) -- e.g. the chunks of a fused QKV
+    output -- and the result is (B, T, H*D).  Like hattn.Attn holds its V^T buffer, this object holds
+    the attention-tile buffer the pack kernel fills (one per batch size)."""
 
     def __init__(self, H, T, D, device="cuda"):
         self.H, self.T, self.D = H, T, D
         self.scale = D ** -0.5
+        self.device = device
+        self._tiles = {}
 
     def __call__(self, q, k, v, out=None):
         B, H, T, D = q.shape
@@ -107,20 +135,28 @@ class VtAttn:
         assert q.stride(3) == 1 and k.stride(3) == 1 and v.stride(3) == 1
         if out is None:
             out = torch.empty(B, T, H * D, dtype=BF16, device=q.device)
-        rc = lib().vt_attn_fwd(_stream(), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, T, H, D,
-                               q.stride(0), q.stride(2), q.stride(1), k.stride(0), k.stride(2), k.stride(1),
-                               v.stride(0), v.stride(2), v.stride(1), out.stride(0), out.stride(1), D, self.scale)
-        check(rc, "vt_attn_fwd")
+        tiles = self._tiles.get(B)
+        if tiles is None:
+            tiles = self._tiles[B] = attn_tiles(B, T, H, D, q.device)
+        rc = lib().vt_attn_pack(_stream(), q.data_ptr(), k.data_ptr(), v.data_ptr(), tiles.data_ptr(), B, T, H, D,
+                                q.stride(0), q.stride(2), q.stride(1), k.stride(0), k.stride(2), k.stride(1),
+                                v.stride(0), v.stride(2), v.stride(1))
+        check(rc, "vt_attn_pack")
+        rc = lib().vt_attn_tiles_fwd(_stream(), tiles.data_ptr(), out.data_ptr(), B, T, H, D, out.stride(0),
+                                     out.stride(1), D, self.scale)
+        check(rc, "vt_attn_tiles_fwd")
         return out
 
 
-def attention_qkv(qkv, B, T, H, D, out, scale=None):
-    """Attention straight from a fused QKV buffer [B*T, 3*H*D] (row pitch qkv.stride(0)) into out [B*T, H*D]."""
-    s = qkv.stride(0)
-    base = qkv.data_ptr()
-    rc = lib().vt_attn_fwd(_stream(), base, base + 2 * H * D, base + 4 * H * D, out.data_ptr(), B, T, H, D,
-                           T * s, s, D, T * s, s, D, T * s, s, D, T * out.stride(0), out.stride(0), D,
-                           D ** -0.5 if scale is None else scale)
+def attention_mma_sync(q, k, v, out=None):
+    """The first-generation mma.sync attention kernel (vt_attn_fwd), kept as an independent GPU cross-check
+    of the tcgen05 kernel in the tests; no product path calls it."""
+    B, H, T, D = q.shape
+    if out is None:
+        out = torch.empty(B, T, H * D, dtype=BF16, device=q.device)
+    rc = lib().vt_attn_fwd(_stream(), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, T, H, D,
+                           q.stride(0), q.stride(2), q.stride(1), k.stride(0), k.stride(2), k.stride(1),
+                           v.stride(0), v.stride(2), v.stride(1), out.stride(0), out.stride(1), D, D ** -0.5)
     check(rc, "vt_attn_fwd")
     return out
 

@@ -6,7 +6,8 @@ and the encoder LayerNorm.  The RG-LRU (tapnext/npu/r9/cpuemu.py:33-47) keeps on
 [1280, 768] per block, carried across frames in device memory owned by this object; reset() starts a
 new video.
 
-Per block the kernels are the tower's (vt_layernorm, vt_gemm_ex, vt_attn_fwd with d = 64) plus:
+Per block the kernels are the tower's (vt_layernorm, vt_gemm_ex, vt_gemm_qkv_tiles + vt_attn_tiles_fwd
+with d = 64) plus:
     t   = RMSNorm(x)                        vt_rmsnorm, bf16 out
     G   = t . [Wx; Wa]^T + [bx; ba]         one vt_gemm_ex, N = 1536, fp32 out
     vt_rglru(G, a_param, t, state_i, x)     gates, recurrence, state and residual update in one pass
@@ -52,7 +53,7 @@ class TapNextStep:
         self.x = torch.empty(T, Wd, dtype=F32, device=dev)
         self.t = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.h = torch.empty(T, Wd, dtype=BF16, device=dev)
-        self.qkv = torch.empty(T, 3 * Wd, dtype=BF16, device=dev)
+        self.tiles = ops.attn_tiles(1, T, cfg.heads, cfg.head_dim, dev)
         self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.f = torch.empty(T, _pad8(cfg.ff), dtype=BF16, device=dev)
         self.G = torch.empty(T, 2 * Wd, dtype=F32, device=dev)
@@ -73,8 +74,9 @@ class TapNextStep:
         self.x[NI:].copy_(queries)
         for i, blk in enumerate(self.blocks):
             ops.layer_norm(self.x, blk["ln1_w"], blk["ln1_b"], cfg.eps, out=self.h)
-            ops.gemm(self.h, blk["qkv_w"], blk["qkv_ld"], Wd, 3 * Wd, blk["qkv_b"], out=self.qkv)
-            ops.attention_qkv(self.qkv, 1, T, cfg.heads, cfg.head_dim, self.a)
+            ops.gemm_qkv_tiles(self.h, blk["qkv_w"], blk["qkv_ld"], Wd, blk["qkv_b"], self.tiles, T, cfg.heads,
+                               cfg.head_dim)
+            ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
             ops.gemm(self.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=self.x, out=self.x)
             ops.layer_norm(self.x, blk["ln2_w"], blk["ln2_b"], cfg.eps, out=self.h)
             ops.gemm(self.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True, out=self.f[:, :cfg.ff])

@@ -3,8 +3,8 @@
 
 Per block (md2fast.py:153-157), with the residual stream x kept in fp32 in HBM:
     h   = LN1(x)                               vt_layernorm     fp32 -> bf16
-    qkv = h . Wqkv^T + b                       vt_gemm_ex       tcgen05, bf16 out [M, 3456]
-    a   = attention(qkv)                       vt_attn_fwd      Q/K/V read in place, d 72 -> 80 on chip
+    qkv = h . Wqkv^T + b                       vt_gemm_qkv_tiles  tcgen05, epilogue writes attention tiles
+    a   = attention(qkv)                       vt_attn_tiles_fwd  tcgen05, S / O in TMEM, d 72 -> 80
     x   = x + a . Wo^T + b                     vt_gemm_ex       residual epilogue, fp32 in place
     h   = LN2(x)                               vt_layernorm
     f   = gelu(h . W1^T + b)                   vt_gemm_ex       GELU-tanh epilogue, bf16 [M, 4304]
@@ -47,7 +47,7 @@ class _Bufs:
         self.a_pe = torch.zeros(M, _pad8(cfg.patch_k), dtype=BF16, device=dev)
         self.x = torch.empty(M, W, dtype=F32, device=dev)
         self.h = torch.empty(M, W, dtype=BF16, device=dev)
-        self.qkv = torch.empty(M, cfg.qkv_dim, dtype=BF16, device=dev)
+        self.tiles = ops.attn_tiles(B, cfg.ntok, cfg.heads, cfg.head_dim, dev)
         self.a = torch.empty(M, W, dtype=BF16, device=dev)
         self.f = torch.empty(M, _pad8(cfg.ff), dtype=BF16, device=dev)
         self.feats = torch.empty(M, W, dtype=BF16, device=dev)
@@ -141,8 +141,9 @@ class VisionTower:
         T, Wd, H, D = cfg.ntok, cfg.width, cfg.heads, cfg.head_dim
         for blk in self.blocks[:nb]:
             self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln1_w"], blk["ln1_b"], self.eps, out=bf.h)
-            self._gemm("qkv", bf.h, blk["qkv_w"], blk["qkv_ld"], Wd, cfg.qkv_dim, blk["qkv_b"], out=bf.qkv)
-            self._op("attention", 4 * B * T * T * D * H, ops.attention_qkv, bf.qkv, B, T, H, D, bf.a)
+            self._op("gemm_qkv", 2 * bf.M * Wd * cfg.qkv_dim, ops.gemm_qkv_tiles, bf.h, blk["qkv_w"], blk["qkv_ld"], Wd,
+                     blk["qkv_b"], bf.tiles, T, H, D)
+            self._op("attention", 4 * B * T * T * D * H, ops.attention_tiles, bf.tiles, B, T, H, D, bf.a)
             self._gemm("proj", bf.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=bf.x, out=bf.x)
             self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln2_w"], blk["ln2_b"], self.eps, out=bf.h)
             self._gemm("fc1", bf.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True,

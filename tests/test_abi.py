@@ -16,7 +16,7 @@ def header_decls():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     decls = {}
-    for m in re.finditer(r"^\s*(?:const\s+)?\w+\**\s+\**(vt_\w+)\s*\(([^;]*?)\)\s*;", src, flags=re.M | re.S):
+    for m in re.finditer(r"^\s*(?:const\s+)?(?:(?:unsigned|long)\s+)*\w+\**\s+\**(vt_\w+)\s*\(([^;]*?)\)\s*;", src, flags=re.M | re.S):
         args = m.group(2).strip()
         n = 0 if args in ("", "void") else len(args.split(","))
         decls[m.group(1)] = n

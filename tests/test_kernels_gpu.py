@@ -136,8 +136,11 @@ def _attn_ref(q, k, v):
     return F.scaled_dot_product_attention(q.float(), k.float(), v.float())
 
 
-@pytest.mark.parametrize("B,H,T,D", [(1, 16, 729, 72), (3, 16, 729, 72), (1, 12, 1280, 64), (2, 2, 1, 72),
-                                     (1, 3, 7, 16), (2, 4, 65, 64), (1, 1, 200, 80)])
+ATTN_CASES = [(1, 16, 729, 72), (3, 16, 729, 72), (1, 12, 1280, 64), (2, 2, 1, 72), (1, 3, 7, 16), (2, 4, 65, 64),
+              (1, 1, 200, 80), (1, 2, 129, 72), (1, 1, 256, 64)]
+
+
+@pytest.mark.parametrize("B,H,T,D", ATTN_CASES)
 def test_attention_strided_qkv(B, H, T, D):
     qkv = torch.randn(B, T, 3 * H * D, device=DEV).to(BF)
     q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
@@ -148,13 +151,29 @@ def test_attention_strided_qkv(B, H, T, D):
     assert rel(out, ref) < 3 * max(rel(sdpa_bf16, ref), 2e-3)
 
 
-def test_attention_qkv_buffer_path_matches_views():
-    B, H, T, D = 2, 16, 729, 72
-    qkv = torch.randn(B * T, 3 * H * D, device=DEV).to(BF)
+@pytest.mark.parametrize("B,H,T,D", ATTN_CASES[:3])
+def test_attention_tcgen05_matches_mma_sync_kernel(B, H, T, D):
+    qkv = torch.randn(B, T, 3 * H * D, device=DEV).to(BF)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    a = ops.VtAttn(H, T, D)(q, k, v)
+    b = ops.attention_mma_sync(q, k, v)
+    assert rel(a, b) < 6e-3
+
+
+def test_attention_fused_qkv_tiles_match_pack_path():
+    """QKV GEMM writing attention tiles == separate GEMM + pack (bit-exact: same GEMM rows)."""
+    B, H, T, D, K = 2, 16, 729, 72, 1152
+    x, w, b = _operands(B * T, K, 3 * H * D, 6)
+    tiles = ops.attn_tiles(B, T, H, D, DEV)
+    ops.gemm_qkv_tiles(x, w, K, K, b, tiles, T, H, D)
     out = torch.empty(B * T, H * D, device=DEV, dtype=BF)
-    ops.attention_qkv(qkv, B, T, H, D, out)
-    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.view(B, T, -1).chunk(3, dim=-1)]
-    assert torch.equal(out.view(B, T, -1), ops.VtAttn(H, T, D)(q, k, v))
+    ops.attention_tiles(tiles, B, T, H, D, out)
+    qkv = ops.VtLin(w, b)(x).view(B, T, -1)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    att = ops.VtAttn(H, T, D)
+    ref = att(q, k, v)
+    assert torch.equal(att._tiles[B], tiles)
+    assert torch.equal(out.view(B, T, -1), ref)
 
 
 def test_attention_large_logits_stay_finite():
