@@ -80,6 +80,20 @@ int vt_attn_pack(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, cons
 int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
                       long long so_b, long long so_t, long long so_h, float scale);
 
+/* Attention without any device allocation, for callers that cannot allocate device memory where they
+ * need attention: code running during CUDA-graph stream capture (cudaMalloc is not allowed there), hosts
+ * with a device-memory budget fixed at start-up, and plain C / FFI callers with no device allocator.
+ * Same result as vt_attn_pack + vt_attn_tiles_fwd (same strides and scale); the attention tiles live in a
+ * fixed 16 MiB array inside the library (held by every GPU that loads it until exit), so problems needing
+ * more than 16 MiB of tiles (vt_attn_tiles_bytes) return -2.  Each call zeroes the part it uses; calls that
+ * overlap on the GPU race on the shared array.  The first call on a device looks up the array's address
+ * with that device current: make it before any stream capture.
+ * No counterpart in the reference (its attention always takes a caller-allocated V^T buffer). */
+int vt_attn_fwd_noalloc(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+                        int B, int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b,
+                        long long sk_t, long long sk_h, long long sv_b, long long sv_t, long long sv_h,
+                        long long so_b, long long so_t, long long so_h, float scale);
+
 /* y = LayerNorm(x) * gamma + beta over rows of N (N % 4 == 0, N <= 4096); x fp32 (bf16 when in_bf16),
  * y bf16 (fp32 when out_f32); fp32 statistics.
  * Replaces: _ln / F.layer_norm, moondream/gpu/md2fast.py:43-44 (ln1, ln2, post_ln; md2fast.py:153-158). */

@@ -23,6 +23,7 @@ SIGNATURES = {
     "vt_attn_tiles_bytes": (LL, [I, I, I, I]),
     "vt_attn_pack": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL]),
     "vt_attn_tiles_fwd": (I, [P, P, P, I, I, I, I, LL, LL, LL, F]),
+    "vt_attn_fwd_noalloc": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, F]),
     "vt_layernorm": (I, [P, P, LL, I, P, P, P, LL, I, I, I, F]),
     "vt_rmsnorm": (I, [P, P, LL, I, P, P, LL, I, I, I, F]),
     "vt_im2col": (I, [P, P, I, I, I, I, I, P, LL]),

@@ -4,4 +4,5 @@
 #include "gemm_tc.cu"
 #include "attn.cu"
 #include "attn_tc.cu"
+#include "attn_noalloc.cu"
 #include "elementwise.cu"
