@@ -155,15 +155,21 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       if (!mbar_wait(s_full, j & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
       const int kbase = j * BKV;
+      const bool tail = kbase + BKV > T;  // only the last key tile has keys past T (zero rows, masked)
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         uint32_t r[32];
         tmem_ld32(t_s + lane_off + c * 32, r);
         tmem_ld_wait();
+        if (!tail) {
 #pragma unroll
-        for (int e = 0; e < 32; e++)
-          if (kbase + c * 32 + e < T) mx = fmaxf(mx, __uint_as_float(r[e]));
+          for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(r[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            if (kbase + c * 32 + e < T) mx = fmaxf(mx, __uint_as_float(r[e]));
+        }
       }
       mx *= a.scale_log2;
       if (j == 0) {
@@ -187,20 +193,26 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           tmem_st_wait();
         }
       }
+      const float neg_m = -m_used, sl2 = a.scale_log2;
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         uint32_t r[32];
         tmem_ld32(t_s + lane_off + c * 32, r);
         tmem_ld_wait();
+        float p[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) p[e] = ex2_approx(fmaf(__uint_as_float(r[e]), sl2, neg_m));
+        if (tail) {
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            if (kbase + c * 32 + e >= T) p[e] = 0.f;
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-          const int k0 = kbase + c * 32 + 2 * e;
-          const float p0 = k0 < T ? exp2f(__uint_as_float(r[2 * e]) * a.scale_log2 - m_used) : 0.f;
-          const float p1 = k0 + 1 < T ? exp2f(__uint_as_float(r[2 * e + 1]) * a.scale_log2 - m_used) : 0.f;
-          sum += p0 + p1;
-          pk[e] = pack_bf2(p0, p1);
+          sum += p[2 * e] + p[2 * e + 1];
+          pk[e] = pack_bf2(p[2 * e], p[2 * e + 1]);
         }
 #pragma unroll
         for (int q = 0; q < 4; q++)

@@ -26,21 +26,36 @@ enum : unsigned int {
 constexpr long long kSpinCycles = 4000000000LL;
 
 // ---------------------------------------------------------------- bf16
-__device__ __forceinline__ uint16_t f2bf(float f) {  // round to nearest even (inputs are finite)
-  uint32_t u = __float_as_uint(f);
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
+// fp32 -> bf16 with round-to-nearest-even (the cvt instruction; one instruction per pair for pack_bf2).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
+  return r;
 }
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
 __device__ __forceinline__ float bfround(float f) { return bf2f(f2bf(f)); }
-__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {  // lo -> bits 0..15, hi -> bits 16..31
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Hardware approximations (single MUFU instructions): 2^x and tanh(x).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// GELU, tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+// GELU, tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), with the hardware tanh
+// (max relative error about 2^-11, below the bf16 rounding the GEMM epilogue applies next).
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(u));
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.0f + tanh_approx(u));
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
