@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-frame", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
+    ap.add_argument("--no-fold", action="store_true", help="LayerNorm as separate passes instead of folded into GEMMs")
     return ap.parse_args()
 
 
@@ -224,7 +225,7 @@ def run_vt(a):
     n_local = len(ids)
 
     W = tower_weights(cfg, seed=0, projection=not a.no_frame)
-    tower = VisionTower(W, cfg, device=dev)
+    tower = VisionTower(W, cfg, device=dev, fold_ln=not a.no_fold)
 
     # this rank's crops, chunk by chunk (ids are runs of mb consecutive crops)
     pix_host = torch.empty(n_local, 3, cfg.img, cfg.img, dtype=torch.bfloat16).pin_memory()

@@ -55,6 +55,33 @@ int vt_attn_fwd(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const
                 long long sk_h, long long sv_b, long long sv_t, long long sv_h, long long so_b, long long so_t,
                 long long so_h, float scale);
 
+/* Superset of vt_gemm_ex with the tower's LayerNorm fusions (NULL / 0 disables each):
+ *   stats_out (fp32 output, N % 32 == 0): stats_out[m][j] = (mean, sum of squared deviations) of output row
+ *     m over columns 32j..32j+31, float pairs [M][N/32] -- the row statistics of the new residual stream;
+ *   ln_moments / ln_c: LayerNorm of the A rows folded into this GEMM: A holds x (bf16), W holds
+ *     W * diag(gamma), ln_c[n] = sum_k W[n][k] (of the bf16 W), bias holds b + W beta, and the epilogue
+ *     computes rstd * (acc - mean * ln_c[n]) + bias with (mean, rstd) = ln_moments[m] (vt_row_moments);
+ *   tiles_T / tiles_H / tiles_D > 0: bf16 output scattered into the attention-tile layout (N = 3*H*D).
+ * Replaces: the pre-LN + linear pairs of md2fast.py:153-154 and 157 (_ln then qkv / fc1) plus the residual
+ * epilogues of md2fast.py:156-157, with the LayerNorm's row statistics produced by the GEMM that writes
+ * the residual stream instead of a separate F.layer_norm pass. */
+int vt_gemm_fused(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M,
+                  int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+                  long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
+                  const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D);
+
+/* Row statistics of x[M, N] fp32 (N % 32 == 0) in the stats_out format of vt_gemm_fused, and optionally the
+ * bf16 copy xb: the LayerNorm inputs for a residual stream that no vt_gemm_fused epilogue produced.
+ * Replaces: the statistics half of _ln, md2fast.py:43-44. */
+int vt_rowstats(cudaStream_t stream, const float* x, long long ldx, uint16_t* xb, long long ldxb, float* stats, int M,
+                int N);
+
+/* moments[m] = (mean, rsqrt(var + eps)) of row m of a residual stream with N = 32*nchunk columns, from its
+ * chunk statistics (float pairs [M][nchunk], as vt_rowstats / vt_gemm_fused stats_out write them), merged
+ * with Chan's parallel formula; the ln_moments input of vt_gemm_fused.
+ * Replaces: the statistics half of _ln, md2fast.py:43-44. */
+int vt_row_moments(cudaStream_t stream, const float* stats, int M, int nchunk, float eps, float* moments);
+
 /* Fused QKV projection for attention: A[M = crops*T, K] . W[3*H*D, K]^T + bias, bf16, written straight into
  * the attention-tile layout vt_attn_tiles_fwd reads (tiles: vt_attn_tiles_bytes(M/T, T, H, D) bytes,
  * zero-filled once at allocation).

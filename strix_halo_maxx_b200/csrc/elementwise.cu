@@ -78,6 +78,61 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
   }
 }
 
+// Row statistics for a folded LayerNorm: one warp per row of x (fp32, N % 32 == 0); lane l handles the
+// 32-column chunks l, l+32, ...: stats[row][j] = (chunk mean, chunk sum of squared deviations), and xb
+// (optional) receives the bf16 copy of x the folded GEMM reads.
+__global__ void __launch_bounds__(256) rowstats_kernel(const float* __restrict__ x, long long ldx,
+                                                       uint16_t* __restrict__ xb, long long ldxb,
+                                                       float2* __restrict__ stats, int M, int N) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + warp;
+  if (row >= M) return;
+  const int nch = N / 32;
+  for (int j = lane; j < nch; j += 32) {
+    const float4* p = reinterpret_cast<const float4*>(x + row * ldx + 32LL * j);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 a = p[i];
+      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    }
+    float sm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) sm += v[i];
+    const float mean = sm * (1.f / 32.f);
+    float m2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) m2 = fmaf(v[i] - mean, v[i] - mean, m2);
+    stats[row * nch + j] = make_float2(mean, m2);
+    if (xb) {
+      uint4* q = reinterpret_cast<uint4*>(xb + row * ldxb + 32LL * j);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        q[i] = make_uint4(pack_bf2(v[8 * i], v[8 * i + 1]), pack_bf2(v[8 * i + 2], v[8 * i + 3]),
+                          pack_bf2(v[8 * i + 4], v[8 * i + 5]), pack_bf2(v[8 * i + 6], v[8 * i + 7]));
+    }
+  }
+}
+
+// (mean, 1/sqrt(var + eps)) of every row from its nchunk per-32-column (mean, M2) pairs, merged with
+// Chan's parallel formula (equal chunk counts): one thread per row.
+__global__ void __launch_bounds__(256) row_moments_kernel(const float2* __restrict__ stats, int nchunk, int M,
+                                                          float eps, float2* __restrict__ out) {
+  for (long long m = (long long)blockIdx.x * blockDim.x + threadIdx.x; m < M; m += (long long)gridDim.x * blockDim.x) {
+    const float2* st = stats + m * nchunk;
+    float s = 0.f;
+    for (int j = 0; j < nchunk; j++) s += st[j].x;
+    const float mu = s / (float)nchunk;
+    float m2 = 0.f;
+    for (int j = 0; j < nchunk; j++) {
+      const float2 v = st[j];
+      const float d = v.x - mu;
+      m2 += v.y + 32.f * d * d;
+    }
+    out[m] = make_float2(mu, rsqrtf(m2 / (32.f * (float)nchunk) + eps));
+  }
+}
+
 // Patch im2col: pixels -> A[m, k] (bf16, pitch ldo) with m = crop*g*g + gy*g + gx and
 // k = c*P*P + py*P + px (md2fast.py:149 permutation).  kind 0: fp32 NCHW values, 1: bf16 NCHW values,
 // 2: uint8 NHWC 0..255 normalised by (u/255 - 0.5)/0.5 (md2fast.py:148).  One thread per P-pixel run.
@@ -227,6 +282,35 @@ int vt_layernorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, con
 int vt_rmsnorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma, void* y, long long ldy,
                int out_f32, int M, int N, float eps) {
   return vt::ew::norm_launch<true>("vt_rmsnorm", st, x, ldx, in_bf16, gamma, nullptr, y, ldy, out_f32, M, N, eps);
+}
+
+// Per-32-column chunk (mean, M2) of every row of x[M, N] (fp32, N % 32 == 0) into stats[M][N/32] (float
+// pairs), and optionally the bf16 copy xb: the inputs of a LayerNorm folded into vt_gemm_fused.
+int vt_rowstats(cudaStream_t st, const float* x, long long ldx, uint16_t* xb, long long ldxb, float* stats, int M,
+                int N) {
+  using namespace vt;
+  if (M < 0 || N <= 0 || N % 32) return set_error(E_SHAPE, "vt_rowstats: N=%d must be a positive multiple of 32", N);
+  if (M == 0) return OK;
+  if (!x || !stats || ldx < N || ldx % 4 || !aligned16(x) || (reinterpret_cast<uintptr_t>(stats) & 7) ||
+      (xb && (ldxb < N || ldxb % 8 || !aligned16(xb))))
+    return set_error(E_SHAPE, "vt_rowstats: pitches / alignment invalid");
+  const long long blocks = ((long long)M + 7) / 8;
+  if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "vt_rowstats: M too large");
+  ew::rowstats_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, ldx, xb, ldxb, reinterpret_cast<float2*>(stats), M, N);
+  return check_launch("vt_rowstats");
+}
+
+// Row moments for a folded LayerNorm: moments[m] = (mean, rsqrt(var + eps)) of row m (N = 32 * nchunk
+// columns) from the chunk statistics vt_rowstats / vt_gemm_fused(stats_out) wrote.
+int vt_row_moments(cudaStream_t st, const float* stats, int M, int nchunk, float eps, float* moments) {
+  using namespace vt;
+  if (M < 0 || nchunk <= 0) return set_error(E_SHAPE, "vt_row_moments: bad shape");
+  if (M == 0) return OK;
+  if (!stats || !moments || (reinterpret_cast<uintptr_t>(stats) & 7) || (reinterpret_cast<uintptr_t>(moments) & 7))
+    return set_error(E_SHAPE, "vt_row_moments: pointers must be 8-byte aligned");
+  ew::row_moments_kernel<<<ew::grid_for(M, 256), 256, 0, st>>>(reinterpret_cast<const float2*>(stats), nchunk, M, eps,
+                                                               reinterpret_cast<float2*>(moments));
+  return check_launch("vt_row_moments");
 }
 
 // Patch im2col of B square images (S x S, C channels, patch P) into A[B*(S/P)^2, C*P*P] bf16 with

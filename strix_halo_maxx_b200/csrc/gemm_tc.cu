@@ -6,27 +6,36 @@
 // Design (one CTA per SM, persistent over output tiles):
 //   * tile 128 x 256 x 64, 4-stage shared-memory ring (48 KB per stage), 128-byte swizzle;
 //   * warp 0 lane 0 issues the TMA loads (no multicast), warp 1 lane 0 issues tcgen05.mma
-//     (M=128, N=256, K=16 each, fp32 accumulators in TMEM), warps 2-5 run the epilogue;
+//     (M=128, N=256, K=16 each, fp32 accumulators in TMEM), warps 2-9 run the epilogue (two warps per
+//     TMEM lane quarter, each on half of the tile's columns, so one warp's loads hide behind the other's);
 //   * two 256-column TMEM accumulators, so the epilogue of tile i overlaps the MMAs of tile i+1;
 //   * tiles are walked N-fastest, so the CTAs resident at one time share A rows and the whole of W
 //     through L2;
 //   * epilogue: + bias, then either bf16 output (optionally GELU-tanh applied after rounding to bf16,
 //     as i8gemm.hip:378 does) or fp32 output with a residual / periodic addend (fp32 or bf16) and an
 //     optional bf16 copy.  M, N and K tails are handled by TMA zero fill and masked stores.
+#include <cstdlib>
+
 #include "vt_common.cuh"
 #include "vt_host.h"
 
 namespace vt {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
-constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+// Tile shape: BM x BN x BK with BN 256 (default) or 192.
+constexpr int BM = 128, BK = 64;
+constexpr int EPI_WARPS = 8;                 // two warps per TMEM lane quarter, each owning half the columns
+constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr long long kDrainCycles = 200000000LL;
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 5;
+  static constexpr uint32_t TMEM_COLS = 512;  // two BN-column accumulators, rounded to a power of two
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
 
 struct Epi {
   const float* bias;  // [N] fp32 or null
@@ -43,13 +52,39 @@ struct Epi {
   // attention-tile output (pk_T > 0): the bf16 result [M = crops*T][3*H*D] is scattered into the tile
   // layout vt_attn_tiles_fwd reads, ((((b*3 + w)*H + h)*Tt + t/128)*NC + d/8)*1024 + (t%128)*8 + d%8
   int pk_T, pk_H, pk_D, pk_NC, pk_Tt;
+  // row statistics of an fp32 output (stats_out != null, N % 32 == 0): for every 32-column chunk j of
+  // row m, stats_out[m * N/32 + j] = (chunk mean, chunk sum of squared deviations)
+  float2* stats_out;
+  // LayerNorm folded into this GEMM (ln_moments != null): A holds bf16 x, W holds W * diag(gamma), and
+  // the accumulator becomes rstd * (acc - mean * ln_c[n]) (+ bias = b + W beta), with (mean, rstd) of
+  // row m read from ln_moments[m] (written by vt_row_moments from the chunk statistics)
+  const float2* ln_moments;
+  const float* ln_c;
 };
 
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep) {
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
+                                               float rstd) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
   const bool full = (n0 + 32 <= N);
+  if (ep.ln_moments) {
+    if (full) {
+      const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float4 c = __ldg(c4 + j);
+        v[4 * j] = rstd * fmaf(-mu, c.x, v[4 * j]);
+        v[4 * j + 1] = rstd * fmaf(-mu, c.y, v[4 * j + 1]);
+        v[4 * j + 2] = rstd * fmaf(-mu, c.z, v[4 * j + 2]);
+        v[4 * j + 3] = rstd * fmaf(-mu, c.w, v[4 * j + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n0 + j < N) v[j] = rstd * fmaf(-mu, ep.ln_c[n0 + j], v[j]);
+    }
+  }
   if (ep.bias) {
     if (full) {
       const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
@@ -100,6 +135,16 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     }
   }
   if (ep.out_f32) {
+    if (ep.stats_out) {  // N % 32 == 0, so the chunk is full
+      float sm = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; j++) sm += v[j];
+      const float mean = sm * (1.f / 32.f);
+      float m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; j++) m2 = fmaf(v[j] - mean, v[j] - mean, m2);
+      ep.stats_out[(long long)m * (N / 32) + n0 / 32] = make_float2(mean, m2);
+    }
     float* op = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + n0;
     if (full) {
 #pragma unroll
@@ -162,9 +207,13 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                         int K, Epi ep) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES, STAGE_BYTES = C::STAGE_BYTES, A_BYTES = C::A_BYTES;
+  constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -189,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -281,26 +330,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_wait_drain(drain, 0, kDrainCycles);
     }
   } else {
-    // ---------------- epilogue: warps 2..5, warp w reads TMEM lanes 32*(w%4) .. +31
+    // ---------------- epilogue: warps 2..9; warp w reads TMEM lanes 32*(w%4) .. +31 (the hardware's
+    // lane-quarter rule) and the chunks [half * BN/64, (half + 1) * BN/64) of the tile's columns
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int CH = BN / 64;  // 32-column chunks per warp
     const int row = q * 32 + lane;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
-      tc_fence_after();
       const int mt = t / nN, nt = t % nN;
       const int m = mt * BM + row;
+      float mu = 0.f, rstd = 1.f;
+      if (ep.ln_moments && m < M) {  // issued before the wait: the load overlaps the tile's MMAs
+        const float2 mr = ep.ln_moments[m];
+        mu = mr.x;
+        rstd = mr.y;
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
+      tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = half * CH; c < (half + 1) * CH; c++) {
         const int n0 = nt * BN + c * 32;
         if (n0 >= N) break;  // uniform across the CTA
         uint32_t r[32];
         tmem_ld32(tb + (uint32_t)(c * 32), r);
         tmem_ld_wait();
-        if (m < M) epilogue_chunk(r, m, n0, N, ep);
+        if (m < M) epilogue_chunk(r, m, n0, N, ep, mu, rstd);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -313,6 +371,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+template <int BN>
+static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                     int K, const Epi& ep) {
+  CUtensorMap ta, tb;
+  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
+  if (rc) return rc;
+  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, BN);
+  if (rc) return rc;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
+    attr_done[dev] = true;
+  }
+  const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
+  const int grid = (int)(ntiles < sm_count() ? ntiles : sm_count());
+  gemm_bf16_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  return check_launch("vt_gemm");
 }
 
 static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
@@ -333,25 +413,20 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
     return set_error(E_SHAPE, "vt_gemm: bf16 copy pitch %lld invalid", ep.ldo2);
   if (ep.bias && !aligned16(ep.bias)) return set_error(E_SHAPE, "vt_gemm: bias must be 16-byte aligned");
   if (ep.gelu && ep.out_f32) return set_error(E_VARIANT, "vt_gemm: GELU is only fused for bf16 output");
+  if (ep.stats_out && (!ep.out_f32 || N % 32 || (reinterpret_cast<uintptr_t>(ep.stats_out) & 7)))
+    return set_error(E_VARIANT, "vt_gemm: row statistics need an fp32 output with N %% 32 == 0");
+  if (ep.ln_moments && (!ep.ln_c || !aligned16(ep.ln_c) || (reinterpret_cast<uintptr_t>(ep.ln_moments) & 7)))
+    return set_error(E_VARIANT, "vt_gemm: folded LayerNorm needs ln_c (16-byte aligned) and 8-byte aligned moments");
 
-  CUtensorMap ta, tb;
-  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
-  if (rc) return rc;
-  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, BN);
-  if (rc) return rc;
-
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_done[dev] = true;
-  }
-  const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
-  const int grid = (int)(ntiles < sm_count() ? ntiles : sm_count());
-  gemm_bf16_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
-  return check_launch("vt_gemm");
+  // 256-wide tiles by default: measured on B200 they beat 192-wide ones on every tower shape, even where
+  // 192 divides N exactly (N = 1152, 3456).  VT_GEMM_BN=192 selects the 192-wide tile (tuning switch,
+  // like the reference's HGEMM_* variables, hgemm.py:56, 85-86).
+  static const int forced = [] {
+    const char* e = getenv("VT_GEMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 192) return launch_bn<192>(st, A, lda, W, ldw, M, N, K, ep);
+  return launch_bn<256>(st, A, lda, W, ldw, M, N, K, ep);
 }
 
 }  // namespace gemm
@@ -362,7 +437,7 @@ extern "C" {
 // C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias, optionally GELU-tanh (after bf16 rounding).
 int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
                  const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu) {
-  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0, 0, 0, 0, 0, 0};
+  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0, 0, 0, 0, 0, 0, nullptr, nullptr, nullptr};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -373,7 +448,28 @@ int vt_gemm_ex(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t
                const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res, long long ldr,
                int res_period, int res_bf16, uint16_t* out2, long long ldo2) {
   vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
-                   0, 0, 0, 0, 0};
+                   0, 0, 0, 0, 0, nullptr, nullptr, nullptr};
+  return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+// Superset of vt_gemm_ex with the LayerNorm fusions of the tower (see include/vt_b200.h):
+//   stats_out  (fp32 output only): per-32-column chunk (mean, M2) of every output row;
+//   ln_moments / ln_c: LayerNorm of the A rows folded into the epilogue;
+//   tiles_T > 0: bf16 output scattered into the attention-tile layout (N = 3*tiles_H*tiles_D).
+int vt_gemm_fused(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                  int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+                  long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
+                  const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D) {
+  using namespace vt;
+  if (tiles_T > 0) {
+    if (tiles_H <= 0 || tiles_D <= 0 || tiles_D % 8 || tiles_D > 80 || M % tiles_T || N != 3 * tiles_H * tiles_D ||
+        out_f32 || gelu || res || out2 || stats_out || !aligned16(out))
+      return set_error(E_SHAPE, "vt_gemm_fused: attention-tile output needs bf16, N = 3*H*D, M a multiple of T");
+  }
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
+                   tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
+                   tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
+                   reinterpret_cast<const float2*>(ln_moments), ln_c};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -387,7 +483,8 @@ int vt_gemm_qkv_tiles(cudaStream_t st, const uint16_t* A, long long lda, const u
     return set_error(E_SHAPE, "vt_gemm_qkv_tiles: M=%d T=%d H=%d D=%d invalid (M a multiple of T, D%%8 == 0, D <= 80)", M,
                      T, H, D);
   if (!aligned16(tiles)) return set_error(E_SHAPE, "vt_gemm_qkv_tiles: tiles must be 16-byte aligned");
-  vt::gemm::Epi ep{bias, tiles, 0, nullptr, 0, 0, 0, 0, 0, nullptr, 0, T, H, D, D <= 64 ? 8 : 10, (T + 127) / 128};
+  vt::gemm::Epi ep{bias, tiles, 0, nullptr, 0, 0, 0, 0, 0, nullptr, 0, T, H, D, D <= 64 ? 8 : 10, (T + 127) / 128,
+                   nullptr, nullptr, nullptr};
   return vt::gemm::launch(st, A, lda, W, ldw, M, 3 * H * D, K, ep);
 }
 

@@ -47,17 +47,52 @@ def as_gemm_operand(x2):
     return buf[:, :K]
 
 
-def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=None, out_f32=False, out2=None):
-    """out[M, N] = x2 . w^T + bias (+ GELU) (+ res); see vt_gemm_ex in include/vt_b200.h."""
+def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=None, out_f32=False, out2=None,
+         stats_out=None, ln=None, tiles=None):
+    """out[M, N] = x2 . w^T + bias (+ GELU) (+ res), see vt_gemm_fused in include/vt_b200.h.
+    stats_out: [M, N/32, 2] fp32 row-chunk statistics of the (fp32) output; ln: (moments [M, 2], c) of a
+    LayerNorm folded into this GEMM; tiles: (T, H, D) to scatter into the attention-tile buffer `out`."""
     M = x2.shape[0]
     if out is None:
         out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :N]
-    rc = lib().vt_gemm_ex(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
-                          out.data_ptr(), out.stride(0), int(out.dtype == torch.float32), int(gelu),
-                          _ptr(res), 0 if res is None else res.stride(0), int(res_period),
-                          int(res is not None and res.dtype == BF16), _ptr(out2), 0 if out2 is None else out2.stride(0))
-    check(rc, "vt_gemm_ex")
+    ln_mom, ln_c = ln if ln is not None else (None, None)
+    tT, tH, tD = tiles if tiles is not None else (0, 0, 0)
+    rc = lib().vt_gemm_fused(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
+                             out.data_ptr(), out.stride(0) if tiles is None else 0,
+                             int(tiles is None and out.dtype == torch.float32), int(gelu), _ptr(res),
+                             0 if res is None else res.stride(0), int(res_period),
+                             int(res is not None and res.dtype == BF16), _ptr(out2),
+                             0 if out2 is None else out2.stride(0), _ptr(stats_out), _ptr(ln_mom), _ptr(ln_c),
+                             tT, tH, tD)
+    check(rc, "vt_gemm_fused")
     return out
+
+
+def row_stats(x2, stats, xb=None):
+    """Chunk statistics (and the bf16 copy xb) of an fp32 residual stream x2 [M, N] for a folded LayerNorm."""
+    M, N = x2.shape
+    rc = lib().vt_rowstats(_stream(), x2.data_ptr(), x2.stride(0), _ptr(xb), 0 if xb is None else xb.stride(0),
+                           stats.data_ptr(), M, N)
+    check(rc, "vt_rowstats")
+    return stats
+
+
+def row_moments(stats, eps, out):
+    """(mean, rstd) per row [M, 2] from chunk statistics [M, nchunk, 2] (the ln input of gemm)."""
+    M, nchunk = stats.shape[0], stats.shape[1]
+    rc = lib().vt_row_moments(_stream(), stats.data_ptr(), M, nchunk, float(eps), out.data_ptr())
+    check(rc, "vt_row_moments")
+    return out
+
+
+def fold_layernorm(w, b, gamma, beta):
+    """Weights of a linear with the preceding LayerNorm's affine folded in: (bf16 W * diag(gamma),
+    fp32 c = row sums of that bf16 matrix, fp32 b + W beta).  w [N, K], b [N], gamma / beta [K] (fp32)."""
+    w = torch.as_tensor(w).float()
+    wf = (w * torch.as_tensor(gamma).float()[None, :]).to(BF16)
+    c = wf.float().sum(dim=1)
+    bf = torch.as_tensor(b).float() + w @ torch.as_tensor(beta).float()
+    return wf, c, bf
 
 
 class VtLin:

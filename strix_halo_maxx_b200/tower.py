@@ -1,14 +1,18 @@
 """The moondream2 SigLIP-style vision tower on B200: the hot path FastMD2._vision computes
 (moondream/gpu/md2fast.py:147-160), re-planned for sm_100a.
 
-Per block (md2fast.py:153-157), with the residual stream x kept in fp32 in HBM:
-    h   = LN1(x)                               vt_layernorm     fp32 -> bf16
-    qkv = h . Wqkv^T + b                       vt_gemm_qkv_tiles  tcgen05, epilogue writes attention tiles
-    a   = attention(qkv)                       vt_attn_tiles_fwd  tcgen05, S / O in TMEM, d 72 -> 80
-    x   = x + a . Wo^T + b                     vt_gemm_ex       residual epilogue, fp32 in place
-    h   = LN2(x)                               vt_layernorm
-    f   = gelu(h . W1^T + b)                   vt_gemm_ex       GELU-tanh epilogue, bf16 [M, 4304]
-    x   = x + f . W2^T + b                     vt_gemm_ex       residual epilogue
+Per block (md2fast.py:153-157), with the residual stream x kept in fp32 in HBM and each LayerNorm folded
+into the GEMM that follows it (default, fold_ln=True):
+    mom = (mean, rstd) of x rows   vt_row_moments  from the chunk statistics the last residual GEMM wrote
+    qkv = LN1(x) . Wqkv^T + b      vt_gemm_fused  A = bf16 x, W * gamma1; epilogue applies
+                                                  rstd * (acc - mean * rowsum(W')) + b + W beta1 and
+                                                  writes attention tiles
+    a   = attention(qkv)           vt_attn_tiles_fwd  tcgen05, S / O in TMEM, d 72 -> 80
+    x   = x + a . Wo^T + b         vt_gemm_fused  residual epilogue, fp32 in place, also writes the bf16
+                                                  copy of x and its per-32-column (mean, M2) statistics
+    f   = gelu(LN2(x) . W1^T + b)  vt_gemm_fused  folded LN2 (after vt_row_moments) + GELU-tanh epilogue
+    x   = x + f . W2^T + b         vt_gemm_fused  residual epilogue + bf16 copy + statistics
+With fold_ln=False the two LayerNorms run as vt_layernorm passes (fp32 x -> bf16) before qkv / fc1.
 Patch embed (md2fast.py:148-150): vt_im2col (normalise + (c, py, px) patch order, K 588 in a 592 pitch)
 then vt_gemm_ex with the positional embedding as a row-periodic (period 729) fp32 addend.
 post-LN (md2fast.py:158) -> bf16 features; projection (md2fast.py:159-160) -> two GEMMs.
@@ -48,6 +52,9 @@ class _Bufs:
         self.x = torch.empty(M, W, dtype=F32, device=dev)
         self.h = torch.empty(M, W, dtype=BF16, device=dev)
         self.tiles = ops.attn_tiles(B, cfg.ntok, cfg.heads, cfg.head_dim, dev)
+        self.xb = torch.empty(M, W, dtype=BF16, device=dev)                 # bf16 copy of x (folded LN)
+        self.stats = torch.empty(M, W // 32, 2, dtype=F32, device=dev)     # per-32-column (mean, M2) of x
+        self.moments = torch.empty(M, 2, dtype=F32, device=dev)            # (mean, rstd) per row of x
         self.a = torch.empty(M, W, dtype=BF16, device=dev)
         self.f = torch.empty(M, _pad8(cfg.ff), dtype=BF16, device=dev)
         self.feats = torch.empty(M, W, dtype=BF16, device=dev)
@@ -60,8 +67,9 @@ class VisionTower:
     eps: LayerNorm eps (the benchmark configs use 1e-6; the reference's _ln uses torch's 1e-5).
     """
 
-    def __init__(self, weights, cfg: TowerConfig = TOWER, eps=None, device="cuda", projection=True):
+    def __init__(self, weights, cfg: TowerConfig = TOWER, eps=None, device="cuda", projection=True, fold_ln=True):
         self.cfg = cfg
+        self.fold_ln = fold_ln
         self.eps = cfg.eps if eps is None else float(eps)
         dev = self.dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -80,6 +88,12 @@ class VisionTower:
                 blk[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
             for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b"):
                 blk[n] = _dev_vec(W[p + n], dev)
+            if fold_ln:   # LN1 into qkv, LN2 into fc1: W * gamma, rowsum, b + W beta
+                for n, ln in (("qkv", "ln1"), ("fc1", "ln2")):
+                    wf, c, bf = ops.fold_layernorm(W[p + n + "_w"], W[p + n + "_b"], W[p + ln + "_w"], W[p + ln + "_b"])
+                    blk[n + "_wf"], blk[n + "_ldf"] = _dev_mat(wf, dev)
+                    blk[n + "_c"] = _dev_vec(c, dev)
+                    blk[n + "_bf"] = _dev_vec(bf, dev)
             self.blocks.append(blk)
         self.post_w = _dev_vec(W["post_ln_w"], dev)
         self.post_b = _dev_vec(W["post_ln_b"], dev)
@@ -120,8 +134,9 @@ class VisionTower:
         bf = self.buffers(B)
         T, Wd, H, D = cfg.ntok, cfg.width, cfg.heads, cfg.head_dim
         self._op("im2col", 0, ops.im2col, pix, cfg.patch, bf.a_pe)
+        fold = dict(out2=bf.xb, stats_out=bf.stats) if self.fold_ln else {}
         self._gemm("patch", bf.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
-                   res=self.pos, res_period=T, out=bf.x)
+                   res=self.pos, res_period=T, out=bf.x, **fold)
         self._blocks(bf, B, nb)
         dst = bf.feats if out is None else out.reshape(B * T, Wd)
         self._op("layernorm", 0, ops.layer_norm, bf.x, self.post_w, self.post_b, self.eps, out=dst)
@@ -133,16 +148,33 @@ class VisionTower:
         B = x.shape[0]
         bf = self.buffers(B)
         bf.x.copy_(x.reshape(bf.M, self.cfg.width))
+        if self.fold_ln:
+            self._op("rowstats", 0, ops.row_stats, bf.x, bf.stats, bf.xb)
         self._blocks(bf, B, self.n_blocks if n_blocks is None else n_blocks)
         return bf.x.reshape(B, self.cfg.ntok, self.cfg.width)
 
     def _blocks(self, bf, B, nb):
         cfg = self.cfg
         T, Wd, H, D = cfg.ntok, cfg.width, cfg.heads, cfg.head_dim
+        if self.fold_ln:
+            fold = dict(out2=bf.xb, stats_out=bf.stats)
+            for blk in self.blocks[:nb]:
+                self._op("row_moments", 0, ops.row_moments, bf.stats, self.eps, bf.moments)
+                self._gemm("qkv", bf.xb, blk["qkv_wf"], blk["qkv_ldf"], Wd, cfg.qkv_dim, blk["qkv_bf"], out=bf.tiles,
+                           ln=(bf.moments, blk["qkv_c"]), tiles=(T, H, D))
+                self._op("attention", 4 * B * T * T * D * H, ops.attention_tiles, bf.tiles, B, T, H, D, bf.a)
+                self._gemm("proj", bf.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=bf.x, out=bf.x,
+                           **fold)
+                self._op("row_moments", 0, ops.row_moments, bf.stats, self.eps, bf.moments)
+                self._gemm("fc1", bf.xb, blk["fc1_wf"], blk["fc1_ldf"], Wd, cfg.ff, blk["fc1_bf"], gelu=True,
+                           out=bf.f[:, :cfg.ff], ln=(bf.moments, blk["fc1_c"]))
+                self._gemm("fc2", bf.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=bf.x,
+                           out=bf.x, **fold)
+            return
         for blk in self.blocks[:nb]:
             self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln1_w"], blk["ln1_b"], self.eps, out=bf.h)
-            self._op("gemm_qkv", 2 * bf.M * Wd * cfg.qkv_dim, ops.gemm_qkv_tiles, bf.h, blk["qkv_w"], blk["qkv_ld"], Wd,
-                     blk["qkv_b"], bf.tiles, T, H, D)
+            self._gemm("qkv", bf.h, blk["qkv_w"], blk["qkv_ld"], Wd, cfg.qkv_dim, blk["qkv_b"], out=bf.tiles,
+                       tiles=(T, H, D))
             self._op("attention", 4 * B * T * T * D * H, ops.attention_tiles, bf.tiles, B, T, H, D, bf.a)
             self._gemm("proj", bf.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=bf.x, out=bf.x)
             self._op("layernorm", 0, ops.layer_norm, bf.x, blk["ln2_w"], blk["ln2_b"], self.eps, out=bf.h)

@@ -2,6 +2,8 @@
 bf16-rounded operands.  GEMM shapes: the reference's vision shapes (moondream/gpu/test_hgemm.py:16) plus
 tails and edge cases; tolerance rel < 5e-3 as test_hgemm.py:45.  Attention: the reference's
 (16, 729, 72) strided QKV layout (hattn.py:48-51) and the TAPNext (12, 1280, 64) case."""
+import os
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -78,6 +80,66 @@ def test_gemm_inplace_residual_periodic_addend_and_bf16_copy():
     ref2 = ref + F.linear(x.float(), w.float(), b)
     assert rel(x2, ref2) < 5e-3
     assert torch.equal(copy, x2.to(BF))
+
+
+@pytest.mark.parametrize("M", [729, 1000, 3 * 729])
+def test_gemm_residual_row_statistics(M):
+    K, N = 1152, 1152
+    x, w, b = _operands(M, K, N, 7)
+    res = torch.randn(M, N, device=DEV) * 3 + 1
+    out = torch.empty(M, N, device=DEV)
+    xb = torch.empty(M, N, device=DEV, dtype=BF)
+    stats = torch.empty(M, N // 32, 2, device=DEV)
+    ops.gemm(x, w, K, K, N, b, res=res, out=out, out2=xb, stats_out=stats)
+    ch = out.view(M, N // 32, 32)
+    assert torch.allclose(stats[..., 0], ch.mean(-1), rtol=1e-5, atol=1e-5)
+    assert torch.allclose(stats[..., 1], ((ch - ch.mean(-1, keepdim=True)) ** 2).sum(-1), rtol=1e-4, atol=1e-4)
+    assert torch.equal(xb, out.to(BF))
+    st2 = torch.empty_like(stats)
+    xb2 = torch.empty_like(xb)
+    ops.row_stats(out, st2, xb2)
+    assert torch.allclose(st2, stats, rtol=1e-5, atol=1e-5) and torch.equal(xb2, xb)
+
+
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_folded_layernorm(gelu):
+    """LN(x) . W^T + b computed as rstd * (x . (W gamma)^T - mean * rowsum) + b + W beta from row statistics."""
+    M, K, N = 1458, 1152, 4304
+    g = torch.Generator(device=DEV).manual_seed(8)
+    x = torch.randn(M, K, device=DEV, generator=g) * 2 + 0.3
+    w = torch.randn(N, K, device=DEV, generator=g) * 0.02
+    b = torch.randn(N, device=DEV, generator=g) * 0.1
+    gamma = 1 + 0.1 * torch.randn(K, device=DEV, generator=g)
+    beta = 0.05 * torch.randn(K, device=DEV, generator=g)
+    stats = torch.empty(M, K // 32, 2, device=DEV)
+    xb = torch.empty(M, K, device=DEV, dtype=BF)
+    ops.row_stats(x, stats, xb)
+    wf, c, bf = ops.fold_layernorm(w, b, gamma, beta)
+    mom = ops.row_moments(stats, 1e-6, torch.empty(M, 2, device=DEV))
+    assert torch.allclose(mom[:, 0], x.mean(-1), rtol=1e-4, atol=1e-5)
+    assert torch.allclose(mom[:, 1], torch.rsqrt(x.var(-1, unbiased=False) + 1e-6), rtol=1e-4)
+    out = ops.gemm(xb, wf.contiguous(), K, K, N, bf.to(DEV), gelu=gelu, ln=(mom, c.to(DEV)))
+    ref = F.linear(F.layer_norm(x, (K,), gamma, beta, 1e-6), w, b)
+    if gelu:
+        ref = F.gelu(ref, approximate="tanh")
+    assert rel(out, ref) < 8e-3
+
+
+@pytest.mark.parametrize("bn", ["192", "256"])
+def test_gemm_both_tile_widths_in_a_subprocess(bn):
+    """VT_GEMM_BN forces the 192- or 256-wide N tile: both give correct results on the tower shapes."""
+    import subprocess
+    import sys
+    code = ("import torch, torch.nn.functional as F; from strix_halo_maxx_b200 import ops\n"
+            "for M, K, N in [(1000, 1152, 1152), (729, 1152, 3456), (729, 4304, 1152), (300, 1152, 4304)]:\n"
+            "    x = torch.randn(M, K, device='cuda').to(torch.bfloat16)\n"
+            "    w = (torch.randn(N, K, device='cuda') * 0.02).to(torch.bfloat16)\n"
+            "    o = ops.VtLin(w, None)(x); r = F.linear(x.float(), w.float())\n"
+            "    e = float((o.float() - r).norm() / r.norm()); assert e < 5e-3, (M, K, N, e)\n")
+    env = dict(os.environ, VT_GEMM_BN=bn)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-2000:]
 
 
 def test_gemm_k588_in_padded_pitch_matches_contiguous():

@@ -34,11 +34,12 @@ def tower27(w27):
     return VisionTower(w27, CFG, device=DEV)
 
 
-def test_config0_one_block_random_affine():
+@pytest.mark.parametrize("fold_ln", [True, False])
+def test_config0_one_block_random_affine(fold_ln):
     W = wg.tower_weights(CFG, seed=6, n_blocks=1, affine="random")
     x = torch.from_numpy(wg.block_input(CFG, seed=4, batch=2))
     ref = tower_ref.block(x, W, 0, CFG.heads, CFG.eps)
-    out = VisionTower(W, CFG, device=DEV).run_blocks(x.to(DEV))
+    out = VisionTower(W, CFG, device=DEV, fold_ln=fold_ln).run_blocks(x.to(DEV))
     assert_tokens_close(out.cpu(), ref, what="config 0 block")
 
 
@@ -48,6 +49,13 @@ def test_config1_full_tower(tower27, w27):
     out = tower27.forward(pix.to(DEV))
     r, c = assert_tokens_close(out.float().cpu(), ref, what="config 1 tower (27 blocks)")
     print(f"config 1: max per-token rel {r:.3e}, min cos {c:.6f}")
+
+
+def test_config1_full_tower_unfolded_layernorm(w27):
+    pix = torch.from_numpy(wg.crop_pixels(1, CFG, seed=1))
+    ref = tower_ref.tower(pix, w27, CFG)
+    out = VisionTower(w27, CFG, device=DEV, fold_ln=False).forward(pix.to(DEV))
+    assert_tokens_close(out.float().cpu(), ref, what="config 1 tower, LayerNorm as separate passes")
 
 
 def test_batch_of_crops_is_bit_identical_to_single_crops(tower27):
@@ -68,11 +76,12 @@ def test_uint8_input_and_eps_1e5_against_reference_golden():
     assert rows_rel <= TOK_REL and proj_rel <= TOK_REL, (rows_rel, proj_rel)
 
 
-def test_affine_two_blocks_with_projection():
+@pytest.mark.parametrize("fold_ln", [True, False])
+def test_affine_two_blocks_with_projection(fold_ln):
     W = wg.tower_weights(CFG, seed=5, n_blocks=2, affine="random")
     img = wg.crop_u8(1, CFG, seed=3)[0]
     ref = tower_ref.vision_u8(img, W, CFG, eps=1e-5, n_blocks=2)
-    t = VisionTower(W, CFG, eps=1e-5, device=DEV)
+    t = VisionTower(W, CFG, eps=1e-5, device=DEV, fold_ln=fold_ln)
     out = t.vision_u8(torch.from_numpy(img).to(DEV))
     assert_tokens_close(out.float().cpu(), ref, what="vision_u8 2 blocks affine")
 
