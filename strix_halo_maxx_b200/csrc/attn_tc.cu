@@ -10,32 +10,36 @@
 // lanes d >= D are zero (the buffer is zeroed once at allocation and never written there).  The tower's
 // QKV GEMM writes this layout from its epilogue; vt_attn_pack builds it from any strided Q/K/V.
 //
-// CTA = one 128-query tile of one (crop, head); 6 warps:
-//   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 128-key tile);
-//   warp 5 lane 0: tcgen05.mma  S = Q K_j^T (M 128, N 128, K DP) into TMEM, then O += P_j V_j (M 128,
-//                  N DP, K 128; V is an MN-major B operand) into a TMEM accumulator;
+// CTA = one 128-query tile of one (crop, head), 2 CTAs per SM; 6 warps:
+//   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, 2-stage rings);
+//   warp 5 lane 0: tcgen05.mma  S_j = Q K_j^T (M 128, N 64, K DP) into one of two TMEM S buffers, then
+//                  O += P_j V_j (M 128, N DP, K 64; V is an MN-major B operand) into a TMEM accumulator;
 //   warps 0-3: softmax, thread i owns query row i (TMEM lane i): row max, P = 2^(s*scale*log2e - m),
 //              bf16 P written to shared memory in the K-major canonical layout, row sums in fp32.
 // O is rescaled only when a row max grows by more than 2^8 (P <= 256 otherwise, exact in fp32
-// accumulation), so TMEM round trips of O are rare.  tcgen05 ops of one thread complete in issue order,
-// so the commit after S_j also means PV_{j-1} is done when softmax sees S_j.
+// accumulation), so TMEM round trips of O are rare.  tcgen05 ops of one thread complete in issue order.
 #include "vt_common.cuh"
 #include "vt_host.h"
 
 namespace vt {
 namespace attn_tc {
 
-constexpr int BQ = 128, BKV = 128, THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;  // S: columns [0, 128), O: [128, 128 + DP)
+constexpr int BQ = 128, BKV = 64, THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;  // S buffers: columns [0, 64) and [64, 128); O: [128, 128 + DP)
 constexpr long long kDrainCycles = 200000000LL;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int NC>
 struct Smem {
-  static constexpr int TILE = NC * 2048;  // bytes of one 128-row operand tile
-  static constexpr int Q = 0, K = TILE, V = 2 * TILE, P = 3 * TILE;
-  static constexpr int BAR = P + 16 * 2048;  // P: 16 chunks of 128 rows x 16 B
-  static constexpr int BYTES = BAR + 128;
+  static constexpr int QT = NC * 2048;  // bytes of the 128-row Q tile
+  static constexpr int KT = NC * 1024;  // bytes of a 64-row K or V tile
+  static constexpr int PT = 8 * 2048;   // bytes of a P tile: 8 chunks (64 keys) of 128 rows x 16 B
+  static constexpr int Q = 0;
+  static constexpr int K = QT;                      // 2 stages
+  static constexpr int V = QT + 2 * KT;             // 2 stages
+  static constexpr int P = QT + 4 * KT;             // 2 buffers
+  static constexpr int BAR = P + 2 * PT;
+  static constexpr int BYTES = BAR + 256;
 };
 
 struct Args {
@@ -47,37 +51,44 @@ struct Args {
   int b0;
 };
 
+// Pipeline per CTA (one 128-query tile), key tiles of 64, j = 0 .. nkv-1:
+//   MMA thread:  S_0;  then for each j: S_(j+1) into the other S buffer, wait P_j, O += P_j V_j.
+//                So the tensor core computes S_(j+1) while the softmax warps work on S_j.
+//   softmax:     wait S_j, row max, (rare) O rescale after PV_(j-1) is done, P_j = 2^(s - m) -> smem
+//                buffer j%2, arrive.  The commit after S_j (issued after PV_(j-2)) means PV_(j-2) -- the
+//                last reader of P buffer j%2 -- has finished when S_j is visible.
 template <int NC>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   using L = Smem<NC>;
   constexpr int DP = NC * 8;
-  constexpr uint32_t TB = L::TILE;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* q_full = bar + 0;
-  uint64_t* k_full = bar + 1;
-  uint64_t* k_empty = bar + 2;
-  uint64_t* v_full = bar + 3;
-  uint64_t* v_empty = bar + 4;
-  uint64_t* s_full = bar + 5;
-  uint64_t* p_full = bar + 6;
-  uint64_t* o_full = bar + 7;
-  uint64_t* drain = bar + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
+  uint64_t* k_full = bar + 1;   // [2]
+  uint64_t* k_empty = bar + 3;  // [2]
+  uint64_t* v_full = bar + 5;   // [2]
+  uint64_t* v_empty = bar + 7;  // [2]
+  uint64_t* s_full = bar + 9;   // [2]
+  uint64_t* p_full = bar + 11;  // [2], 128 arrivals
+  uint64_t* pv_done = bar + 13;
+  uint64_t* o_full = bar + 14;
+  uint64_t* drain = bar + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tt = blockIdx.x, h = blockIdx.y, b = a.b0 + blockIdx.z;
   const int T = a.T, H = a.H, Tt = a.Tt;
   const int nkv = (T + BKV - 1) / BKV;
-  const size_t tile_elems = (size_t)NC * 1024;
+  const size_t tile_elems = (size_t)NC * 1024;  // one 128-row tile of one operand
   const uint16_t* q_src = a.tiles + ((((size_t)b * 3 + 0) * H + h) * Tt + tt) * tile_elems;
   const uint16_t* k_base = a.tiles + ((((size_t)b * 3 + 1) * H + h) * Tt) * tile_elems;
   const uint16_t* v_base = a.tiles + ((((size_t)b * 3 + 2) * H + h) * Tt) * tile_elems;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 9; i++) mbar_init(&bar[i], 1);
-    mbar_init(p_full, 128);
+    for (int i = 0; i < 16; i++) mbar_init(&bar[i], 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -89,29 +100,38 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t t_o = tmem + 128;
 
   if (warp == 4) {
     if (lane == 0) {
-      // ---------------- bulk loads
+      // ---------------- bulk loads: Q once (20 KB); per 64-key tile NC pieces of 1 KB for K and for V
       bool ok = true;
-      int pending_k = -1, pending_v = -1;  // phase of the last armed, not yet observed load
-      mbar_arrive_expect_tx(q_full, TB);
-      bulk_load(sm + L::Q, q_src, TB, q_full);
+      int last = -1;  // last key tile whose K and V copies were issued
+      mbar_arrive_expect_tx(q_full, L::QT);
+      bulk_load(sm + L::Q, q_src, L::QT, q_full);
       for (int j = 0; j < nkv && ok; j++) {
-        if (j > 0 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(k_full, TB);
-        bulk_load(sm + L::K, k_base + (size_t)j * tile_elems, TB, k_full);
-        pending_k = j & 1;
-        if (j > 0 && !mbar_wait(v_empty, (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(v_full, TB);
-        bulk_load(sm + L::V, v_base + (size_t)j * tile_elems, TB, v_full);
-        pending_v = j & 1;
+        const int s = j & 1;
+        const uint16_t* ks = k_base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
+        const uint16_t* vs = v_base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
+        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[s], L::KT);
+        for (int c = 0; c < NC; c++) bulk_load(sm + L::K + s * L::KT + c * 1024, ks + (size_t)c * 1024, 1024, &k_full[s]);
+        if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) {
+          // K_j is in flight: let it land before unwinding
+          mbar_wait_drain(&k_full[s], (j >> 1) & 1, kDrainCycles);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[s], L::KT);
+        for (int c = 0; c < NC; c++) bulk_load(sm + L::V + s * L::KT + c * 1024, vs + (size_t)c * 1024, 1024, &v_full[s]);
+        last = j;
       }
-      if (!ok) {  // unwinding: let every copy this thread issued land before the CTA exits
+      if (!ok) {  // unwinding: let the copies this thread issued land before the CTA exits
         mbar_wait_drain(q_full, 0, kDrainCycles);
-        if (pending_k >= 0) mbar_wait_drain(k_full, (uint32_t)pending_k, kDrainCycles);
-        if (pending_v >= 0) mbar_wait_drain(v_full, (uint32_t)pending_v, kDrainCycles);
+        for (int j = last > 0 ? last - 1 : 0; j <= last; j++) {
+          mbar_wait_drain(&k_full[j & 1], (j >> 1) & 1, kDrainCycles);
+          mbar_wait_drain(&v_full[j & 1], (j >> 1) & 1, kDrainCycles);
+        }
       }
     }
   } else if (warp == 5) {
@@ -121,24 +141,33 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       constexpr uint32_t IDESC_O = idesc_bf16(BQ, DP) | (1u << 16);  // B (= V) MN-major
       const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V),
                      sp = smem_u32(sm + L::P);
-      bool ok = mbar_wait(q_full, 0, abort_flag, ST_ATTN_MMA);
-      for (int j = 0; j < nkv && ok; j++) {
-        if (!mbar_wait(k_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into S buffer j%2
+        const int s = j & 1;
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) return false;
         tc_fence_after();
+        const uint32_t kb = sk + s * L::KT;
 #pragma unroll
-        for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA = two 8-element chunks, 2048 B apart
-          umma_f16(t_s, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(sk + k * 4096, 2048, 128), IDESC_S,
-                   k > 0 ? 1u : 0u);
-        umma_commit(k_empty);
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
-        if (!mbar_wait(v_full, j & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA: Q chunks 2k, 2k+1 (2048 B apart), K chunks (1024 B apart)
+          umma_f16(tmem + s * BKV, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(kb + k * 2048, 1024, 128),
+                   IDESC_S, k > 0 ? 1u : 0u);
+        umma_commit(&k_empty[s]);
+        umma_commit(&s_full[s]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, ST_ATTN_MMA) && issue_s(0);
+      for (int j = 0; j < nkv && ok; j++) {
+        const int s = j & 1;
+        if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        if (!mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t pb = sp + s * L::PT, vb = sv + s * L::KT;
 #pragma unroll
         for (int k = 0; k < BKV / 16; k++)  // 16 keys per MMA: P chunks 2k, 2k+1; V rows 16k..16k+15
-          umma_f16(t_o, sdesc_noswz(sp + k * 4096, 2048, 128), sdesc_noswz(sv + k * 256, 128, 2048), IDESC_O,
+          umma_f16(t_o, sdesc_noswz(pb + k * 4096, 2048, 128), sdesc_noswz(vb + k * 256, 128, 1024), IDESC_O,
                    (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(v_empty);
+        umma_commit(&v_empty[s]);
+        umma_commit(pv_done);
       }
       if (ok) umma_commit(o_full);
       umma_commit(drain);
@@ -148,35 +177,44 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
     // ---------------- softmax warps 0-3: thread = query row
     const int row = warp * 32 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    uint8_t* P = sm + L::P;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; j++) {
-      if (!mbar_wait(s_full, j & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t t_s = tmem + s * BKV + lane_off;
       const int kbase = j * BKV;
       const bool tail = kbase + BKV > T;  // only the last key tile has keys past T (zero rows, masked)
-      float mx = -INFINITY;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(t_s, r0);
+      tmem_ld32(t_s + 32, r1);
+      tmem_ld_wait();
+      // row max as a tree (no serial dependency chain); keys past T only exist in the last tile
+      float t32[32];
+      if (!tail) {
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t r[32];
-        tmem_ld32(t_s + lane_off + c * 32, r);
-        tmem_ld_wait();
-        if (!tail) {
+        for (int e = 0; e < 32; e++) t32[e] = fmaxf(__uint_as_float(r0[e]), __uint_as_float(r1[e]));
+      } else {
 #pragma unroll
-          for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(r[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; e++)
-            if (kbase + c * 32 + e < T) mx = fmaxf(mx, __uint_as_float(r[e]));
-        }
+        for (int e = 0; e < 32; e++)
+          t32[e] = fmaxf(kbase + e < T ? __uint_as_float(r0[e]) : -INFINITY,
+                         kbase + 32 + e < T ? __uint_as_float(r1[e]) : -INFINITY);
       }
+#pragma unroll
+      for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; e++) t32[e] = fmaxf(t32[e], t32[e + w]);
+      float mx = t32[0];
       mx *= a.scale_log2;
       if (j == 0) {
         m_used = mx;
       } else {
         const bool need = mx > m_used + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {  // O round trip through registers (warp-collective)
+        if (__any_sync(0xffffffffu, need)) {  // O round trip through registers (warp-collective), rare
+          // O must hold every P.V up to j-1: PV_(j-1) completes phase j-1 of pv_done
+          if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
+          tc_fence_after();
           const float m_new = need ? mx : m_used;
           const float alpha = exp2f(m_used - m_new);
           m_used = m_new;
@@ -194,12 +232,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         }
       }
       const float neg_m = -m_used, sl2 = a.scale_log2;
-      float sum = 0.f;
+      uint8_t* P = sm + L::P + s * L::PT;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t r[32];
-        tmem_ld32(t_s + lane_off + c * 32, r);
-        tmem_ld_wait();
+      for (int c = 0; c < 2; c++) {
+        const uint32_t* r = c ? r1 : r0;
         float p[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) p[e] = ex2_approx(fmaf(__uint_as_float(r[e]), sl2, neg_m));
@@ -211,7 +248,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-          sum += p[2 * e] + p[2 * e + 1];
+          sum4[e & 3] += p[2 * e] + p[2 * e + 1];
           pk[e] = pack_bf2(p[2 * e], p[2 * e + 1]);
         }
 #pragma unroll
@@ -219,10 +256,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           *reinterpret_cast<uint4*>(P + (c * 4 + q) * 2048 + row * 16) =
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
-      l += sum;
+      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[s]);
     }
     if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
       tc_fence_after();

@@ -60,7 +60,46 @@ struct Epi {
   // row m read from ln_moments[m] (written by vt_row_moments from the chunk statistics)
   const float2* ln_moments;
   const float* ln_c;
+  // all row-major outputs / the residual are 32-byte aligned with 32-byte multiple pitches: full chunks
+  // use 256-bit accesses (set by the launcher)
+  int wide;
 };
+
+// 32 consecutive 32-bit words at p: 256-bit accesses (one full 32-byte sector each, p 32-byte aligned) when
+// wide, else 128-bit ones.
+__device__ __forceinline__ void ld_words32(const void* p, uint32_t (&w)[32], bool wide) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+  if (wide) {
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      asm volatile("ld.global.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                   : "=r"(w[8 * i]), "=r"(w[8 * i + 1]), "=r"(w[8 * i + 2]), "=r"(w[8 * i + 3]), "=r"(w[8 * i + 4]),
+                     "=r"(w[8 * i + 5]), "=r"(w[8 * i + 6]), "=r"(w[8 * i + 7])
+                   : "l"(q + 8 * i));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint4 u = *reinterpret_cast<const uint4*>(q + 4 * i);
+      w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+    }
+  }
+}
+template <int NW>  // NW = 16 or 32 words
+__device__ __forceinline__ void st_words(void* p, const uint32_t* w, bool wide) {
+  uint32_t* q = reinterpret_cast<uint32_t*>(p);
+  if (wide) {
+#pragma unroll
+    for (int i = 0; i < NW / 8; i++)
+      asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(q + 8 * i), "r"(w[8 * i]), "r"(w[8 * i + 1]),
+                   "r"(w[8 * i + 2]), "r"(w[8 * i + 3]), "r"(w[8 * i + 4]), "r"(w[8 * i + 5]), "r"(w[8 * i + 6]),
+                   "r"(w[8 * i + 7])
+                   : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW / 4; i++)
+      *reinterpret_cast<uint4*>(q + 4 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+}
 
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
                                                float rstd) {
@@ -104,15 +143,16 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     if (ep.res_bf16) {
       const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.res) + rr * ep.ldr + n0;
       if (full) {
+        uint32_t w[16];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
           const uint4 u = *reinterpret_cast<const uint4*>(rp + 8 * j);
-          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          w[4 * j] = u.x; w[4 * j + 1] = u.y; w[4 * j + 2] = u.z; w[4 * j + 3] = u.w;
+        }
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            v[8 * j + 2 * e] += __uint_as_float(w[e] << 16);
-            v[8 * j + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
-          }
+        for (int e = 0; e < 16; e++) {
+          v[2 * e] += __uint_as_float(w[e] << 16);
+          v[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
         }
       } else {
 #pragma unroll
@@ -122,11 +162,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     } else {
       const float* rp = reinterpret_cast<const float*>(ep.res) + rr * ep.ldr + n0;
       if (full) {
+        uint32_t w[32];
+        ld_words32(rp, w, ep.wide != 0);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const float4 a = *reinterpret_cast<const float4*>(rp + 4 * j);
-          v[4 * j] += a.x; v[4 * j + 1] += a.y; v[4 * j + 2] += a.z; v[4 * j + 3] += a.w;
-        }
+        for (int j = 0; j < 32; j++) v[j] += __uint_as_float(w[j]);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; j++)
@@ -135,21 +174,22 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     }
   }
   if (ep.out_f32) {
-    if (ep.stats_out) {  // N % 32 == 0, so the chunk is full
-      float sm = 0.f;
+    if (ep.stats_out) {  // N % 32 == 0, so the chunk is full; 4 independent partial sums per pass
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 32; j++) sm += v[j];
-      const float mean = sm * (1.f / 32.f);
-      float m2 = 0.f;
+      for (int j = 0; j < 32; j++) sm[j & 3] += v[j];
+      const float mean = ((sm[0] + sm[1]) + (sm[2] + sm[3])) * (1.f / 32.f);
+      float q[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 32; j++) m2 = fmaf(v[j] - mean, v[j] - mean, m2);
-      ep.stats_out[(long long)m * (N / 32) + n0 / 32] = make_float2(mean, m2);
+      for (int j = 0; j < 32; j++) q[j & 3] = fmaf(v[j] - mean, v[j] - mean, q[j & 3]);
+      ep.stats_out[(long long)m * (N / 32) + n0 / 32] = make_float2(mean, (q[0] + q[1]) + (q[2] + q[3]));
     }
     float* op = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + n0;
     if (full) {
+      uint32_t w[32];
 #pragma unroll
-      for (int j = 0; j < 8; j++)
-        *reinterpret_cast<float4*>(op + 4 * j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int j = 0; j < 32; j++) w[j] = __float_as_uint(v[j]);
+      st_words<32>(op, w, ep.wide != 0);
     } else {
 #pragma unroll
       for (int j = 0; j < 32; j++)
@@ -158,11 +198,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     if (ep.out2) {
       uint16_t* o2 = ep.out2 + (long long)m * ep.ldo2 + n0;
       if (full) {
+        uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-          *reinterpret_cast<uint4*>(o2 + 8 * j) =
-              make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
-                         pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
+        for (int j = 0; j < 16; j++) w[j] = pack_bf2(v[2 * j], v[2 * j + 1]);
+        st_words<16>(o2, w, ep.wide != 0);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; j++)
@@ -194,11 +233,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     }
     uint16_t* op = reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0;
     if (full) {
+      uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 4; j++)
-        *reinterpret_cast<uint4*>(op + 8 * j) =
-            make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
-                       pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
+      for (int j = 0; j < 16; j++) w[j] = pack_bf2(v[2 * j], v[2 * j + 1]);
+      st_words<16>(op, w, ep.wide != 0);
     } else {
 #pragma unroll
       for (int j = 0; j < 32; j++)
@@ -396,7 +434,7 @@ static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const ui
 }
 
 static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
-                  int K, const Epi& ep) {
+                  int K, Epi ep) {
   if (M < 0 || N < 0 || K < 0) return set_error(E_SHAPE, "vt_gemm: negative shape M=%d N=%d K=%d", M, N, K);
   if (M == 0 || N == 0) return OK;
   if (K == 0) return set_error(E_SHAPE, "vt_gemm: K must be >= 1");
@@ -413,6 +451,13 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
     return set_error(E_SHAPE, "vt_gemm: bf16 copy pitch %lld invalid", ep.ldo2);
   if (ep.bias && !aligned16(ep.bias)) return set_error(E_SHAPE, "vt_gemm: bias must be 16-byte aligned");
   if (ep.gelu && ep.out_f32) return set_error(E_VARIANT, "vt_gemm: GELU is only fused for bf16 output");
+  {
+    auto a32 = [](const void* p, long long ld, int es) {
+      return p == nullptr || ((reinterpret_cast<uintptr_t>(p) & 31) == 0 && (ld * es) % 32 == 0);
+    };
+    ep.wide = (ep.pk_T > 0 || a32(ep.out, ep.ldo, ep.out_f32 ? 4 : 2)) && a32(ep.res, ep.ldr, ep.res_bf16 ? 2 : 4) &&
+             a32(ep.out2, ep.ldo2, 2);
+  }
   if (ep.stats_out && (!ep.out_f32 || N % 32 || (reinterpret_cast<uintptr_t>(ep.stats_out) & 7)))
     return set_error(E_VARIANT, "vt_gemm: row statistics need an fp32 output with N %% 32 == 0");
   if (ep.ln_moments && (!ep.ln_c || !aligned16(ep.ln_c) || (reinterpret_cast<uintptr_t>(ep.ln_moments) & 7)))
@@ -437,7 +482,7 @@ extern "C" {
 // C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias, optionally GELU-tanh (after bf16 rounding).
 int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
                  const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu) {
-  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0, 0, 0, 0, 0, 0, nullptr, nullptr, nullptr};
+  vt::gemm::Epi ep{bias, C, ldc, nullptr, 0, 0, 0, 0, gelu ? 1 : 0, nullptr, 0, 0, 0, 0, 0, 0, nullptr, nullptr, nullptr, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -448,7 +493,7 @@ int vt_gemm_ex(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t
                const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res, long long ldr,
                int res_period, int res_bf16, uint16_t* out2, long long ldo2) {
   vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
-                   0, 0, 0, 0, 0, nullptr, nullptr, nullptr};
+                   0, 0, 0, 0, 0, nullptr, nullptr, nullptr, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -469,7 +514,7 @@ int vt_gemm_fused(cudaStream_t st, const uint16_t* A, long long lda, const uint1
   vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
                    tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
-                   reinterpret_cast<const float2*>(ln_moments), ln_c};
+                   reinterpret_cast<const float2*>(ln_moments), ln_c, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 
@@ -484,7 +529,7 @@ int vt_gemm_qkv_tiles(cudaStream_t st, const uint16_t* A, long long lda, const u
                      T, H, D);
   if (!aligned16(tiles)) return set_error(E_SHAPE, "vt_gemm_qkv_tiles: tiles must be 16-byte aligned");
   vt::gemm::Epi ep{bias, tiles, 0, nullptr, 0, 0, 0, 0, 0, nullptr, 0, T, H, D, D <= 64 ? 8 : 10, (T + 127) / 128,
-                   nullptr, nullptr, nullptr};
+                   nullptr, nullptr, nullptr, 0};
   return vt::gemm::launch(st, A, lda, W, ldw, M, 3 * H * D, K, ep);
 }
 
