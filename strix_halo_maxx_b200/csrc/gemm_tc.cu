@@ -411,6 +411,213 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of 2 CTAs computes 256 x 256 output tiles.  Each CTA stages
+// its 128 rows of A and its 128 rows of B (B rows = output columns n0 + rank*128 ..) per 64-wide k-block;
+// the leader (rank 0) issues tcgen05.mma.cta_group::2 (M 256, N 256), which reads A and B from both CTAs'
+// shared memory and writes each CTA's 128 output rows into that CTA's TMEM.  Per SM the L2 -> shared
+// traffic is 32 KB per k-block instead of 48 KB for the single-CTA 128 x 256 tile.
+//   * TMA loads of both CTAs complete on the leader's full[s] (armed by the leader for both CTAs' bytes);
+//   * the leader's commits arrive on empty[s] / tfull[a] of each CTA (two commits, one per CTA);
+//   * the epilogue warps of both CTAs arrive on the leader's tempty[a] (one arrive per warp).
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                             int N, int K, Epi ep) {
+  constexpr int BN = 256;
+  constexpr uint32_t TMEM_COLS = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int nN = (N + BN - 1) / BN;
+  const int ntiles = ((M + 255) / 256) * nN;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < P_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrive per epilogue warp of each CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs): this CTA's 128 rows of A and of B per stage
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        const int mt = t / nN, nt = t % nN;
+        for (int kb = 0; kb < nk; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, ST_GEMM_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          uint8_t* sa = smem + stage * P_STAGE_BYTES;
+          const uint32_t fb = full_leader0 + stage * 8;
+          tma_load_2d_pair(&tmA, fb, sa, kb * BK, mt * 256 + (int)rank * 128);
+          tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BK, nt * BN + (int)rank * 128);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // no drain here: loads complete on the leader's barriers, which the leader's MMA thread (or its
+      // own unwinding below) observes before the final cluster barrier
+      if (!ok) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 200000) {
+        }  // ~0.1 ms: in-flight tile loads land long before this
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader CTA only)
+      constexpr uint32_t IDESC = idesc_bf16(256, BN);
+      const uint32_t empty0_self = smem_u32(&empty[0]), empty0_peer = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t tfull0_self = smem_u32(&tfull[0]), tfull0_peer = mapa_shared(smem_u32(&tfull[0]), 1);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, ST_GEMM_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; kb++) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, ST_GEMM_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + P_A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(empty0_self + stage * 8);
+          umma_commit_pair(empty0_peer + stage * 8);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(tfull0_self + acc * 8);
+          umma_commit_pair(tfull0_peer + acc * 8);
+        }
+      }
+      umma_commit_pair(smem_u32(drain));
+      mbar_wait_drain(drain, 0, kDrainCycles);
+      if (!ok) {  // let every armed stage's loads (both CTAs') land before the pair exits
+        for (int j = 0; j < P_STAGES; j++) mbar_wait_drain(&full[j], 0, 20000000LL);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256 x 256 tile
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int CH = BN / 64;
+    const int row = q * 32 + lane;
+    const uint32_t tempty0_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    int it = 0;
+    for (int t = cluster; t < ntiles; t += nclusters, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mt = t / nN, nt = t % nN;
+      const int m = mt * 256 + (int)rank * 128 + row;
+      float mu = 0.f, rstd = 1.f;
+      if (ep.ln_moments && m < M) {
+        const float2 mr = ep.ln_moments[m];
+        mu = mr.x;
+        rstd = mr.y;
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = half * CH; c < (half + 1) * CH; c++) {
+        const int n0 = nt * BN + c * 32;
+        if (n0 >= N) break;
+        uint32_t r[32];
+        tmem_ld32(tb + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        if (m < M) epilogue_chunk(r, m, n0, N, ep, mu, rstd);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0_leader + acc * 8);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into the peer's TMEM / smem are complete before either CTA exits
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                       int K, const Epi& ep) {
+  CUtensorMap ta, tb;
+  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128);
+  if (rc) return rc;
+  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, 128);
+  if (rc) return rc;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+    attr_done[dev] = true;
+  }
+  const long long ntiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
+  const int max_clusters = sm_count() / 2;
+  const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
+  gemm_bf16_tc_pair_kernel<<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  return check_launch("vt_gemm (CTA pair)");
+}
+
 template <int BN>
 static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
                      int K, const Epi& ep) {
@@ -471,6 +678,12 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
     return e ? atoi(e) : 0;
   }();
   if (forced == 192) return launch_bn<192>(st, A, lda, W, ldw, M, N, K, ep);
+  // CTA-pair 256 x 256 tiles unless VT_GEMM_2SM=0 (A/B switch) or the problem is a single small tile row
+  static const int pair = [] {
+    const char* e = getenv("VT_GEMM_2SM");
+    return e ? atoi(e) : 1;
+  }();
+  if (pair && M > 128) return launch_pair(st, A, lda, W, ldw, M, N, K, ep);
   return launch_bn<256>(st, A, lda, W, ldw, M, N, K, ep);
 }
 
