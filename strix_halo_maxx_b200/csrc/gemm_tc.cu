@@ -5,7 +5,7 @@
 //
 // Design (one CTA per SM, persistent over output tiles):
 //   * tile 128 x 256 x 64, 4-stage shared-memory ring (48 KB per stage), 128-byte swizzle;
-//   * warp 0 lane 0 issues the TMA loads (no multicast), warp 1 lane 0 issues tcgen05.mma
+//   * warp 0 lane 0 issues the TMA loads (each fills only its own CTA), warp 1 lane 0 issues tcgen05.mma
 //     (M=128, N=256, K=16 each, fp32 accumulators in TMEM), warps 2-9 run the epilogue (two warps per
 //     TMEM lane quarter, each on half of the tile's columns, so one warp's loads hide behind the other's);
 //   * two 256-column TMEM accumulators, so the epilogue of tile i overlaps the MMAs of tile i+1;

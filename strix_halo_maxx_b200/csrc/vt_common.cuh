@@ -118,7 +118,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   return true;
 }
 
-// ---------------------------------------------------------------- TMA (no multicast anywhere)
+// ---------------------------------------------------------------- TMA (every load reads this GPU and fills one CTA)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)m) : "memory");
 }
@@ -195,7 +195,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Non-tensor bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completion
-// counted on the mbarrier.  No multicast.
+// counted on the mbarrier; it fills only the issuing CTA.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
@@ -226,7 +226,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA tile load issued by either CTA of a pair; completion is counted on the mbarrier at `bar_addr`, a
-// shared::cluster address (the leader CTA's barrier).  No multicast.
+// shared::cluster address (the leader CTA's barrier); it fills only the issuing CTA.
 __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* m, uint32_t bar_addr, void* dst, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
