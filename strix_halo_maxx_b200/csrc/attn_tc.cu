@@ -25,6 +25,7 @@ namespace vt {
 namespace attn_tc {
 
 constexpr int BQ = 128, BKV = 64, THREADS = 192;
+constexpr int KVS = 3;  // K and V ring stages: two CTAs of 112 KB share an SM's 228 KB
 constexpr uint32_t TMEM_COLS = 256;  // S buffers: columns [0, 64) and [64, 128); O: [128, 128 + DP)
 constexpr long long kDrainCycles = 200000000LL;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -35,9 +36,9 @@ struct Smem {
   static constexpr int KT = NC * 1024;  // bytes of a 64-row K or V tile
   static constexpr int PT = 8 * 2048;   // bytes of a P tile: 8 chunks (64 keys) of 128 rows x 16 B
   static constexpr int Q = 0;
-  static constexpr int K = QT;                      // 2 stages
-  static constexpr int V = QT + 2 * KT;             // 2 stages
-  static constexpr int P = QT + 4 * KT;             // 2 buffers
+  static constexpr int K = QT;                      // KVS stages
+  static constexpr int V = QT + KVS * KT;           // KVS stages
+  static constexpr int P = QT + 2 * KVS * KT;       // 2 buffers
   static constexpr int BAR = P + 2 * PT;
   static constexpr int BYTES = BAR + 256;
 };
@@ -64,16 +65,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   extern __shared__ __align__(1024) uint8_t sm[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* q_full = bar + 0;
-  uint64_t* k_full = bar + 1;   // [2]
-  uint64_t* k_empty = bar + 3;  // [2]
-  uint64_t* v_full = bar + 5;   // [2]
-  uint64_t* v_empty = bar + 7;  // [2]
-  uint64_t* s_full = bar + 9;   // [2]
-  uint64_t* p_full = bar + 11;  // [2], 128 arrivals
-  uint64_t* pv_done = bar + 13;
-  uint64_t* o_full = bar + 14;
-  uint64_t* drain = bar + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* k_full = bar + 1;            // [KVS]
+  uint64_t* k_empty = bar + 1 + KVS;     // [KVS]
+  uint64_t* v_full = bar + 1 + 2 * KVS;  // [KVS]
+  uint64_t* v_empty = bar + 1 + 3 * KVS; // [KVS]
+  uint64_t* s_full = bar + 1 + 4 * KVS;  // [2]
+  uint64_t* p_full = s_full + 2;         // [2], 128 arrivals
+  uint64_t* pv_done = s_full + 4;
+  uint64_t* o_full = s_full + 5;
+  uint64_t* drain = s_full + 6;
+  constexpr int NBAR = 1 + 4 * KVS + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,7 +88,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   const uint16_t* v_base = a.tiles + ((((size_t)b * 3 + 2) * H + h) * Tt) * tile_elems;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 16; i++) mbar_init(&bar[i], 1);
+    for (int i = 0; i < NBAR; i++) mbar_init(&bar[i], 1);
     mbar_init(&p_full[0], 128);
     mbar_init(&p_full[1], 128);
     *abort_flag = 0;
@@ -104,34 +106,37 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
 
   if (warp == 4) {
     if (lane == 0) {
-      // ---------------- bulk loads: Q once (20 KB); per 64-key tile NC pieces of 1 KB for K and for V
+      // ---------------- bulk loads: Q once (20 KB); per 64-key tile NC pieces of 1 KB for K and for V.
+      // The MMA thread needs K_(j+1) (for S_(j+1)) before V_j (for PV_j), and K_(j+1)'s stage frees when
+      // S_(j+1-KVS) completes while V_j's frees only when PV_(j-KVS) does: so K is issued one tile ahead
+      // of V and never queues behind a V wait.
       bool ok = true;
-      int last = -1;  // last key tile whose K and V copies were issued
+      int last_k = 0, last_v = -1;  // last key tiles whose K / V copies were issued
+      auto load_kv = [&](uint64_t* full, const uint16_t* base, int j, int off) {
+        const uint16_t* src = base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
+        mbar_arrive_expect_tx(full, L::KT);
+        for (int c = 0; c < NC; c++) bulk_load(sm + off + (j % KVS) * L::KT + c * 1024, src + (size_t)c * 1024, 1024, full);
+      };
       mbar_arrive_expect_tx(q_full, L::QT);
       bulk_load(sm + L::Q, q_src, L::QT, q_full);
+      load_kv(&k_full[0], k_base, 0, L::K);
       for (int j = 0; j < nkv && ok; j++) {
-        const int s = j & 1;
-        const uint16_t* ks = k_base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
-        const uint16_t* vs = v_base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
-        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[s], L::KT);
-        for (int c = 0; c < NC; c++) bulk_load(sm + L::K + s * L::KT + c * 1024, ks + (size_t)c * 1024, 1024, &k_full[s]);
-        if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) {
-          // K_j is in flight: let it land before unwinding
-          mbar_wait_drain(&k_full[s], (j >> 1) & 1, kDrainCycles);
-          ok = false;
-          break;
+        const int k1 = j + 1;
+        if (k1 < nkv) {
+          if (k1 >= KVS && !mbar_wait(&k_empty[k1 % KVS], (k1 / KVS - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
+          load_kv(&k_full[k1 % KVS], k_base, k1, L::K);
+          last_k = k1;
         }
-        mbar_arrive_expect_tx(&v_full[s], L::KT);
-        for (int c = 0; c < NC; c++) bulk_load(sm + L::V + s * L::KT + c * 1024, vs + (size_t)c * 1024, 1024, &v_full[s]);
-        last = j;
+        if (j >= KVS && !mbar_wait(&v_empty[j % KVS], (j / KVS - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) { ok = false; break; }
+        load_kv(&v_full[j % KVS], v_base, j, L::V);
+        last_v = j;
       }
       if (!ok) {  // unwinding: let the copies this thread issued land before the CTA exits
         mbar_wait_drain(q_full, 0, kDrainCycles);
-        for (int j = last > 0 ? last - 1 : 0; j <= last; j++) {
-          mbar_wait_drain(&k_full[j & 1], (j >> 1) & 1, kDrainCycles);
-          mbar_wait_drain(&v_full[j & 1], (j >> 1) & 1, kDrainCycles);
-        }
+        for (int j = last_k >= KVS ? last_k - KVS + 1 : 0; j <= last_k; j++)
+          mbar_wait_drain(&k_full[j % KVS], (j / KVS) & 1, kDrainCycles);
+        for (int j = last_v >= KVS ? last_v - KVS + 1 : 0; j <= last_v; j++)
+          mbar_wait_drain(&v_full[j % KVS], (j / KVS) & 1, kDrainCycles);
       }
     }
   } else if (warp == 5) {
@@ -143,14 +148,15 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
                      sp = smem_u32(sm + L::P);
       auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into S buffer j%2
         const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) return false;
+        const int ks = j % KVS;
+        if (!mbar_wait(&k_full[ks], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) return false;
         tc_fence_after();
-        const uint32_t kb = sk + s * L::KT;
+        const uint32_t kb = sk + ks * L::KT;
 #pragma unroll
         for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA: Q chunks 2k, 2k+1 (2048 B apart), K chunks (1024 B apart)
           umma_f16(tmem + s * BKV, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(kb + k * 2048, 1024, 128),
                    IDESC_S, k > 0 ? 1u : 0u);
-        umma_commit(&k_empty[s]);
+        umma_commit(&k_empty[ks]);
         umma_commit(&s_full[s]);
         return true;
       };
@@ -159,14 +165,14 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         const int s = j & 1;
         if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
-        if (!mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        if (!mbar_wait(&v_full[j % KVS], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pb = sp + s * L::PT, vb = sv + s * L::KT;
+        const uint32_t pb = sp + s * L::PT, vb = sv + (j % KVS) * L::KT;
 #pragma unroll
         for (int k = 0; k < BKV / 16; k++)  // 16 keys per MMA: P chunks 2k, 2k+1; V rows 16k..16k+15
           umma_f16(t_o, sdesc_noswz(pb + k * 4096, 2048, 128), sdesc_noswz(vb + k * 256, 128, 1024), IDESC_O,
                    (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&v_empty[s]);
+        umma_commit(&v_empty[j % KVS]);
         umma_commit(pv_done);
       }
       if (ok) umma_commit(o_full);
@@ -190,22 +196,29 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       tmem_ld32(t_s, r0);
       tmem_ld32(t_s + 32, r1);
       tmem_ld_wait();
-      // row max as a tree (no serial dependency chain); keys past T only exist in the last tile
-      float t32[32];
-      if (!tail) {
+      // row max as a tree of three-input maxima (64 -> 22 -> 8 -> 3 -> 1); keys past T only exist in the
+      // last tile
+      float t[64];
 #pragma unroll
-        for (int e = 0; e < 32; e++) t32[e] = fmaxf(__uint_as_float(r0[e]), __uint_as_float(r1[e]));
-      } else {
+      for (int e = 0; e < 32; e++) {
+        t[e] = __uint_as_float(r0[e]);
+        t[32 + e] = __uint_as_float(r1[e]);
+      }
+      if (tail) {
 #pragma unroll
-        for (int e = 0; e < 32; e++)
-          t32[e] = fmaxf(kbase + e < T ? __uint_as_float(r0[e]) : -INFINITY,
-                         kbase + 32 + e < T ? __uint_as_float(r1[e]) : -INFINITY);
+        for (int e = 0; e < 64; e++)
+          if (kbase + e >= T) t[e] = -INFINITY;
       }
 #pragma unroll
-      for (int w = 16; w > 0; w >>= 1)
+      for (int e = 0; e < 21; e++) t[e] = max3f(t[3 * e], t[3 * e + 1], t[3 * e + 2]);
+      t[21] = t[63];
 #pragma unroll
-        for (int e = 0; e < w; e++) t32[e] = fmaxf(t32[e], t32[e + w]);
-      float mx = t32[0];
+      for (int e = 0; e < 7; e++) t[e] = max3f(t[3 * e], t[3 * e + 1], t[3 * e + 2]);
+      t[7] = t[21];
+      t[0] = max3f(t[0], t[1], t[2]);
+      t[1] = max3f(t[3], t[4], t[5]);
+      t[2] = fmaxf(t[6], t[7]);
+      float mx = max3f(t[0], t[1], t[2]);
       mx *= a.scale_log2;
       if (j == 0) {
         m_used = mx;
@@ -231,32 +244,38 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           tmem_st_wait();
         }
       }
-      const float neg_m = -m_used, sl2 = a.scale_log2;
+      // P = 2^(s * scale_log2 - m) with the scale and shift done two lanes at a time (fma.rn.f32x2); the
+      // row sum accumulates in four independent fp32x2 partial sums
+      const unsigned long long sl2 = f2_pack(a.scale_log2, a.scale_log2), neg_m = f2_pack(-m_used, -m_used);
       uint8_t* P = sm + L::P + s * L::PT;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums
+      unsigned long long sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int c = 0; c < 2; c++) {
         const uint32_t* r = c ? r1 : r0;
-        float p[32];
-#pragma unroll
-        for (int e = 0; e < 32; e++) p[e] = ex2_approx(fmaf(__uint_as_float(r[e]), sl2, neg_m));
-        if (tail) {
-#pragma unroll
-          for (int e = 0; e < 32; e++)
-            if (kbase + c * 32 + e >= T) p[e] = 0.f;
-        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-          sum4[e & 3] += p[2 * e] + p[2 * e + 1];
-          pk[e] = pack_bf2(p[2 * e], p[2 * e + 1]);
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), sl2, neg_m), x0, x1);
+          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          if (tail) {
+            if (kbase + c * 32 + 2 * e >= T) p0 = 0.f;
+            if (kbase + c * 32 + 2 * e + 1 >= T) p1 = 0.f;
+          }
+          sum2[e & 3] = f2_add(sum2[e & 3], f2_pack(p0, p1));
+          pk[e] = pack_bf2(p0, p1);
         }
 #pragma unroll
         for (int q = 0; q < 4; q++)
           *reinterpret_cast<uint4*>(P + (c * 4 + q) * 2048 + row * 16) =
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
-      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      {
+        const unsigned long long s01 = f2_add(sum2[0], sum2[1]), s23 = f2_add(sum2[2], sum2[3]);
+        float lo, hi;
+        f2_unpack(f2_add(s01, s23), lo, hi);
+        l += lo + hi;
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
@@ -328,6 +347,8 @@ static int launch_nc(cudaStream_t st, Args a, int B) {
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     cudaFuncSetAttribute(attn_tc_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<NC>::BYTES);
+    // two CTAs per SM need (almost) the whole 228 KB as shared memory
+    cudaFuncSetAttribute(attn_tc_kernel<NC>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr_done[dev] = true;
   }
   for (int b0 = 0; b0 < B; b0 += 65535) {
