@@ -101,7 +101,8 @@ __device__ __forceinline__ void st_words(void* p, const uint32_t* w, bool wide) 
   }
 }
 
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
+// The scalar path for a chunk that crosses N (only the last column tile of a launch).
+__device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
                                                float rstd) {
   float v[32];
 #pragma unroll
@@ -243,6 +244,133 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
         if (n0 + j < N) op[j] = f2bf(v[j]);
     }
   }
+}
+
+// Applies the epilogue to one 32-column chunk of row m (columns n0 .. n0+31) held in r.  Full chunks
+// (every column < N) do their arithmetic two columns at a time with the packed fp32x2 instructions.
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
+                                               float rstd) {
+  if (n0 + 32 > N) {
+    epilogue_chunk_partial(r, m, n0, N, ep, mu, rstd);
+    return;
+  }
+  unsigned long long v[16];
+#pragma unroll
+  for (int j = 0; j < 16; j++) v[j] = f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+  if (ep.ln_moments) {  // rstd * (acc - mean * c) + bias = rstd * acc + (bias - rstd * mean * c)
+    const unsigned long long rs = f2_pack(rstd, rstd), nrm = f2_pack(-rstd * mu, -rstd * mu);
+    const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
+    const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float4 c = __ldg(c4 + j);
+      const float4 b = ep.bias ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[2 * j] = f2_fma(rs, v[2 * j], f2_fma(nrm, f2_pack(c.x, c.y), f2_pack(b.x, b.y)));
+      v[2 * j + 1] = f2_fma(rs, v[2 * j + 1], f2_fma(nrm, f2_pack(c.z, c.w), f2_pack(b.z, b.w)));
+    }
+  } else if (ep.bias) {
+    const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float4 b = __ldg(b4 + j);
+      v[2 * j] = f2_add(v[2 * j], f2_pack(b.x, b.y));
+      v[2 * j + 1] = f2_add(v[2 * j + 1], f2_pack(b.z, b.w));
+    }
+  }
+  if (ep.res) {
+    const long long rr = ep.res_period > 0 ? (long long)(m % ep.res_period) : (long long)m;
+    if (ep.res_bf16) {
+      const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.res) + rr * ep.ldr + n0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint4 u = *reinterpret_cast<const uint4*>(rp + 8 * j);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          v[4 * j + e] = f2_add(v[4 * j + e], f2_pack(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u)));
+      }
+    } else {
+      uint32_t w[32];
+      ld_words32(reinterpret_cast<const float*>(ep.res) + rr * ep.ldr + n0, w, ep.wide != 0);
+#pragma unroll
+      for (int j = 0; j < 16; j++) v[j] = f2_add(v[j], f2_pack(__uint_as_float(w[2 * j]), __uint_as_float(w[2 * j + 1])));
+    }
+  }
+  uint32_t w[32];
+  if (ep.out_f32) {
+    if (ep.stats_out) {  // N % 32 == 0; four independent fp32x2 partial sums per pass
+      unsigned long long a[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+      for (int j = 0; j < 16; j++) a[j & 3] = f2_add(a[j & 3], v[j]);
+      float s0, s1;
+      f2_unpack(f2_add(f2_add(a[0], a[1]), f2_add(a[2], a[3])), s0, s1);
+      const float mean = (s0 + s1) * (1.f / 32.f);
+      const unsigned long long nm = f2_pack(-mean, -mean);
+#pragma unroll
+      for (int j = 0; j < 4; j++) a[j] = 0ull;
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const unsigned long long d = f2_add(v[j], nm);
+        a[j & 3] = f2_fma(d, d, a[j & 3]);
+      }
+      f2_unpack(f2_add(f2_add(a[0], a[1]), f2_add(a[2], a[3])), s0, s1);
+      ep.stats_out[(long long)m * (N / 32) + n0 / 32] = make_float2(mean, s0 + s1);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      float x0, x1;
+      f2_unpack(v[j], x0, x1);
+      w[2 * j] = __float_as_uint(x0);
+      w[2 * j + 1] = __float_as_uint(x1);
+    }
+    st_words<32>(reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + n0, w, ep.wide != 0);
+    if (ep.out2) {
+#pragma unroll
+      for (int j = 0; j < 16; j++) w[j] = pack_bf2(__uint_as_float(w[2 * j]), __uint_as_float(w[2 * j + 1]));
+      st_words<16>(ep.out2 + (long long)m * ep.ldo2 + n0, w, ep.wide != 0);
+    }
+    return;
+  }
+  // bf16 outputs: round to bf16 first (GELU is applied to the bf16 linear output)
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    float x0, x1;
+    f2_unpack(v[j], x0, x1);
+    w[j] = pack_bf2(x0, x1);
+  }
+  if (ep.gelu) {
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      float g0, g1;
+      f2_unpack(gelu_tanh2(f2_pack(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u))), g0, g1);
+      w[j] = pack_bf2(g0, g1);
+    }
+  }
+  if (ep.pk_T > 0) {
+    // attention tiles: the chunk's four 8-column groups each lie in one head (D % 8 == 0); the head and
+    // d offset advance incrementally from the chunk's first column instead of being divided out per group
+    const int HD = ep.pk_H * ep.pk_D;
+    const int crop = m / ep.pk_T, t = m - crop * ep.pk_T;
+    int wsel = n0 / HD;
+    const int rem = n0 - wsel * HD;
+    int hh = rem / ep.pk_D, d = rem - hh * ep.pk_D;
+    const size_t tile_elems = (size_t)ep.pk_NC * 1024;
+    const size_t row_off = (size_t)(t >> 7) * tile_elems + (size_t)(t & 127) * 8;
+    uint16_t* base = reinterpret_cast<uint16_t*>(ep.out);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const size_t off = (((size_t)crop * 3 + wsel) * ep.pk_H + hh) * (size_t)ep.pk_Tt * tile_elems + row_off +
+                         (size_t)(d >> 3) * 1024;
+      *reinterpret_cast<uint4*>(base + off) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      d += 8;
+      if (d >= ep.pk_D) {
+        d = 0;
+        if (++hh == ep.pk_H) { hh = 0; ++wsel; }
+      }
+    }
+    return;
+  }
+  st_words<16>(reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0, w, ep.wide != 0);
 }
 
 template <int BN>

@@ -86,6 +86,17 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.0f + tanh_approx(u));
 }
+// The same on two lanes: u = x (k0 + k1 x^2), gelu = h + h tanh(u) with h = x / 2.
+__device__ __forceinline__ unsigned long long gelu_tanh2(unsigned long long x) {
+  const unsigned long long k0 = f2_pack(0.7978845608028654f, 0.7978845608028654f);
+  const unsigned long long k1 = f2_pack(0.7978845608028654f * 0.044715f, 0.7978845608028654f * 0.044715f);
+  const unsigned long long half = f2_pack(0.5f, 0.5f);
+  const unsigned long long u = f2_mul(x, f2_fma(k1, f2_mul(x, x), k0));
+  float u0, u1;
+  f2_unpack(u, u0, u1);
+  const unsigned long long h = f2_mul(half, x);
+  return f2_fma(h, f2_pack(tanh_approx(u0), tanh_approx(u1)), h);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
