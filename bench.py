@@ -287,7 +287,7 @@ def run_vt(a):
     traffic = None
     tp = os.path.join(ROOT, "profiles", "gemm_traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
+        traffic = json.load(open(tp)).get("bytes_per_launch")
     total_ms = sum(v["ms"] for v in ops_summary.values())
     breakdown = {k: {"launches": v["launches"], "ms_per_step": v["ms"] / a.steps,
                      "share": v["ms"] / total_ms if total_ms else None,
@@ -334,7 +334,7 @@ def run_vt(a):
             "ms_per_frame_13crop_latency": frame_ms,
             "tflops_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12,
             "frac_of_peak_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12 / (sustained * world),
-            "roofline": {"kernel": "gemm_bf16_tc_kernel (tcgen05, all GEMM launches of the timed region)",
+            "roofline": {"kernel": "gemm_bf16_tc_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
                          "bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
                          "frac": achieved / sustained, "traffic": traffic,
                          "peak_source": f"{src} bf16_tflops_sustained" + (" of measured" if src == "measured" else " of fallback"),
