@@ -246,10 +246,31 @@ __device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], 
   }
 }
 
-// Applies the epilogue to one 32-column chunk of row m (columns n0 .. n0+31) held in r.  Full chunks
-// (every column < N) do their arithmetic two columns at a time with the packed fp32x2 instructions.
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, int N, const Epi& ep, float mu,
-                                               float rstd) {
+// The residual words of one full 32-column chunk of row m (fp32: 32 words; bf16: the first 16), loaded
+// ahead of the chunk's epilogue so that the loads overlap other work.  Nothing is loaded without a
+// residual, for rows past M or for a chunk that crosses N (the scalar path loads its own).
+__device__ __forceinline__ void res_load(uint32_t (&w)[32], int m, int n0, int M, int N, const Epi& ep) {
+  if (!ep.res || m >= M || n0 + 32 > N) return;
+  const long long rr = ep.res_period > 0 ? (long long)(m % ep.res_period) : (long long)m;
+  if (ep.res_bf16) {
+    const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.res) + rr * ep.ldr + n0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint4 u = *reinterpret_cast<const uint4*>(rp + 8 * j);
+      w[4 * j] = u.x; w[4 * j + 1] = u.y; w[4 * j + 2] = u.z; w[4 * j + 3] = u.w;
+    }
+  } else {
+    ld_words32(reinterpret_cast<const float*>(ep.res) + rr * ep.ldr + n0, w, ep.wide != 0);
+  }
+}
+
+// Applies the epilogue to one 32-column chunk of row m (columns n0 .. n0+31) held in r.  PRE: the chunk's
+// residual words are already in rw (res_load, issued earlier); otherwise they are loaded here, where they
+// are added.  Full chunks (every column < N) do their arithmetic two columns at a time with the packed
+// fp32x2 instructions.
+template <bool PRE>
+__device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const uint32_t (&rw_in)[32], int m, int M,
+                                                  int n0, int N, const Epi& ep, float mu, float rstd) {
   if (n0 + 32 > N) {
     epilogue_chunk_partial(r, m, n0, N, ep, mu, rstd);
     return;
@@ -278,22 +299,16 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     }
   }
   if (ep.res) {
-    const long long rr = ep.res_period > 0 ? (long long)(m % ep.res_period) : (long long)m;
+    uint32_t rw_local[32];
+    if constexpr (!PRE) res_load(rw_local, m, n0, M, N, ep);
+    const uint32_t* rw = PRE ? rw_in : rw_local;
     if (ep.res_bf16) {
-      const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.res) + rr * ep.ldr + n0;
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(rp + 8 * j);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++)
-          v[4 * j + e] = f2_add(v[4 * j + e], f2_pack(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u)));
-      }
+      for (int e = 0; e < 16; e++)
+        v[e] = f2_add(v[e], f2_pack(__uint_as_float(rw[e] << 16), __uint_as_float(rw[e] & 0xffff0000u)));
     } else {
-      uint32_t w[32];
-      ld_words32(reinterpret_cast<const float*>(ep.res) + rr * ep.ldr + n0, w, ep.wide != 0);
 #pragma unroll
-      for (int j = 0; j < 16; j++) v[j] = f2_add(v[j], f2_pack(__uint_as_float(w[2 * j]), __uint_as_float(w[2 * j + 1])));
+      for (int j = 0; j < 16; j++) v[j] = f2_add(v[j], f2_pack(__uint_as_float(rw[2 * j]), __uint_as_float(rw[2 * j + 1])));
     }
   }
   uint32_t w[32];
@@ -371,6 +386,12 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     return;
   }
   st_words<16>(reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0, w, ep.wide != 0);
+}
+
+// The same with the residual loaded where it is added.
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int M, int n0, int N, const Epi& ep,
+                                               float mu, float rstd) {
+  epilogue_chunk_rw<false>(r, r, m, M, n0, N, ep, mu, rstd);
 }
 
 template <int BN>
@@ -524,7 +545,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tb + (uint32_t)(c * 32), r);
         tmem_ld_wait();
-        if (m < M) epilogue_chunk(r, m, n0, N, ep, mu, rstd);
+        if (m < M) epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -553,6 +574,9 @@ constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = 128 * BK * 2, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 
+// RES: the epilogue adds a residual, which is then loaded one 32-column chunk ahead (a separate
+// instantiation keeps the register budget of the other epilogues unchanged).
+template <bool RES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                              int N, int K, Epi ep) {
@@ -616,7 +640,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           const uint32_t fb = full_leader0 + stage * 8;
           tma_load_2d_pair(&tmA, fb, sa, kb * BK, mt * 256 + (int)rank * 128);
-          tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BK, nt * BN + (int)rank * 128);
+          // a column tile with at most 128 valid columns runs as N = 128: each CTA then holds 64 B rows
+          const int bhalf = (N - nt * BN <= 128) ? 64 : 128;
+          tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BK, nt * BN + (int)rank * bhalf);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -634,7 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader CTA only)
-      constexpr uint32_t IDESC = idesc_bf16(256, BN);
+      constexpr uint32_t IDESC = idesc_bf16(256, BN), IDESC_HALF = idesc_bf16(256, BN / 2);
       const uint32_t empty0_self = smem_u32(&empty[0]), empty0_peer = mapa_shared(smem_u32(&empty[0]), 1);
       const uint32_t tfull0_self = smem_u32(&tfull[0]), tfull0_peer = mapa_shared(smem_u32(&tfull[0]), 1);
       uint32_t stage = 0, phase = 0;
@@ -649,6 +675,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t idesc = (N - (t % nN) * BN <= 128) ? IDESC_HALF : IDESC;  // see the producer
         for (int kb = 0; kb < nk; kb++) {
           if (!mbar_wait(&full[stage], phase, abort_flag, ST_GEMM_MMA)) {
             ok = false;
@@ -659,7 +686,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + P_A_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
-            umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit_pair(empty0_self + stage * 8);
           umma_commit_pair(empty0_peer + stage * 8);
           if (++stage == P_STAGES) {
@@ -697,17 +724,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         mu = mr.x;
         rstd = mr.y;
       }
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
-      tc_fence_after();
-      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * CH * 32);
+      const int nbase = nt * BN + half * CH * 32;
+      if constexpr (RES) {
+        // the residual of chunk i+1 is loaded while chunk i is processed, the first chunk's before the
+        // accumulator wait (the residual does not depend on the MMAs)
+        uint32_t rw[2][32];
+        res_load(rw[0], m, nbase, M, N, ep);
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+          const int n0 = nbase + i * 32;
+          if (n0 >= N) break;  // uniform across the warp
+          if (i + 1 < CH) res_load(rw[(i + 1) & 1], m, n0 + 32, M, N, ep);
+          uint32_t r[32];
+          tmem_ld32(tb + (uint32_t)(i * 32), r);
+          tmem_ld_wait();
+          if (m < M) epilogue_chunk_rw<true>(r, rw[i & 1], m, M, n0, N, ep, mu, rstd);
+        }
+      } else {
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = half * CH; c < (half + 1) * CH; c++) {
-        const int n0 = nt * BN + c * 32;
-        if (n0 >= N) break;
-        uint32_t r[32];
-        tmem_ld32(tb + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
-        if (m < M) epilogue_chunk(r, m, n0, N, ep, mu, rstd);
+        for (int i = 0; i < CH; i++) {
+          const int n0 = nbase + i * 32;
+          if (n0 >= N) break;
+          uint32_t r[32];
+          tmem_ld32(tb + (uint32_t)(i * 32), r);
+          tmem_ld_wait();
+          if (m < M) epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -735,14 +782,18 @@ static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
     attr_done[dev] = true;
   }
   const long long ntiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int max_clusters = sm_count() / 2;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
-  gemm_bf16_tc_pair_kernel<<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  if (ep.res)
+    gemm_bf16_tc_pair_kernel<true><<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  else
+    gemm_bf16_tc_pair_kernel<false><<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
   return check_launch("vt_gemm (CTA pair)");
 }
 
