@@ -570,26 +570,43 @@ __global__ void __launch_bounds__(THREADS, 1)
 //   * TMA loads of both CTAs complete on the leader's full[s] (armed by the leader for both CTAs' bytes);
 //   * the leader's commits arrive on empty[s] / tfull[a] of each CTA (two commits, one per CTA);
 //   * the epilogue warps of both CTAs arrive on the leader's tempty[a] (one arrive per warp).
-constexpr int P_STAGES = 6;
-constexpr int P_A_BYTES = 128 * BK * 2, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+// Epilogue modes of the pair kernel (one instantiation each, so that each keeps its own register budget):
+//   0  no residual: the accumulator chunk goes straight through epilogue_chunk;
+//   1  residual in registers: the residual of the next 32-column chunk is loaded while this one is done;
+//   2  staged fp32 residual epilogue (out = acc + bias + res in fp32, optional bf16 copy and row
+//      statistics; the proj GEMM): each epilogue warp TMA-loads its 32 x 32 residual box into shared
+//      memory one chunk ahead, adds in place and TMA-stores the fp32 box (and a bf16 box), so every
+//      global access is a whole-line bulk copy instead of one 32-byte sector in each of 32 rows.  It
+//      trades two of the six mainloop stages for the 96 KB of staging buffers.
+template <int MODE>
+struct PairCfg {
+  static constexpr int STAGES = MODE == 2 ? 4 : 6;
+  static constexpr int STAGE_BYTES = 2 * 128 * BK * 2;  // this CTA's 128 rows of A and of B
+  static constexpr int EPI_WARP_BYTES = MODE == 2 ? 2 * 4096 + 2 * 2048 : 0;  // 2 fp32 + 2 bf16 32x32 boxes
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * EPI_WARP_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 1024 + 512;
+};
+constexpr int P_A_BYTES = 128 * BK * 2;
 
-// RES: the epilogue adds a residual, which is then loaded one 32-column chunk ahead (a separate
-// instantiation keeps the register budget of the other epilogues unchanged).
-template <bool RES>
+template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                             int N, int K, Epi ep) {
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
+                             const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epi ep) {
+  using C = PairCfg<MODE>;
+  constexpr int P_STAGES = C::STAGES, P_STAGE_BYTES = C::STAGE_BYTES;
   constexpr int BN = 256;
   constexpr uint32_t TMEM_COLS = 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + P_STAGES;
   uint64_t* tfull = empty + P_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rbar = drain + 1;  // [EPI_WARPS][2] residual-box barriers (mode 2)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -602,6 +619,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (MODE == 2) {
+      tma_prefetch_desc(&tmR);
+      tma_prefetch_desc(&tmO);
+      if (ep.out2) tma_prefetch_desc(&tmO2);
+    }
     for (int s = 0; s < P_STAGES; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -611,6 +633,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrive per epilogue warp of each CTA
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2 * EPI_WARPS; i++) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -631,6 +654,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int t = cluster; t < ntiles && ok; t += nclusters) {
         const int mt = t / nN, nt = t % nN;
+        // a column tile with at most 128 valid columns runs as N = 128: each CTA then holds 64 B rows
+        const int bhalf = (N - nt * BN <= 128) ? 64 : 128;
         for (int kb = 0; kb < nk; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, ST_GEMM_PRODUCER)) {
             ok = false;
@@ -640,8 +665,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           const uint32_t fb = full_leader0 + stage * 8;
           tma_load_2d_pair(&tmA, fb, sa, kb * BK, mt * 256 + (int)rank * 128);
-          // a column tile with at most 128 valid columns runs as N = 128: each CTA then holds 64 B rows
-          const int bhalf = (N - nt * BN <= 128) ? 64 : 128;
           tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BK, nt * BN + (int)rank * bhalf);
           if (++stage == P_STAGES) {
             stage = 0;
@@ -706,12 +729,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256 x 256 tile
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256 x 256 tile; warp w reads TMEM
+    // lanes 32*(w%4) .. +31 and the columns [half * 128, half * 128 + 128) of the tile
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int ew = warp - 2;
+    const int half = ew >> 2;
     constexpr int CH = BN / 64;
     const int row = q * 32 + lane;
     const uint32_t tempty0_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    // mode 2: this warp's staging buffers and residual barriers, the chunk counter g (buffer g & 1, use
+    // g >> 1 of it) and which buffers have a load in flight
+    uint8_t* stg = smem + C::EPI_OFF + ew * C::EPI_WARP_BYTES;
+    uint64_t* rb = rbar + 2 * ew;
+    uint32_t g = 0;
+    bool pend[2] = {false, false};
+    bool ok = true;
     int it = 0;
     for (int t = cluster; t < ntiles; t += nclusters, ++it) {
       const int acc = it & 1;
@@ -726,7 +758,103 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * CH * 32);
       const int nbase = nt * BN + half * CH * 32;
-      if constexpr (RES) {
+      if constexpr (MODE == 2) {
+        const int mw = mt * 256 + (int)rank * 128 + q * 32;  // the warp's first row
+        const bool rows_in = mw < M;                          // uniform across the warp
+        auto issue_load = [&](int n0, uint32_t gg) {          // lane 0: residual box of chunk gg
+          const int b = gg & 1;
+          bulk_wait_read<0>();  // the store that last read buffer b has finished reading it
+          mbar_arrive_expect_tx(&rb[b], 4096);
+          tma_load_2d(&tmR, &rb[b], stg + b * 4096, n0, mw);
+          pend[b] = true;
+        };
+        if (rows_in && nbase < N && lane == 0) issue_load(nbase, g);
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (rows_in) {
+#pragma unroll 1
+          for (int i = 0; i < CH; i++) {
+            const int n0 = nbase + i * 32;
+            if (n0 >= N) break;  // uniform across the warp
+            const int b = g & 1;
+            if (i + 1 < CH && n0 + 32 < N && lane == 0) issue_load(n0 + 32, g + 1);
+            uint32_t r[32];
+            tmem_ld32(tb + (uint32_t)(i * 32), r);
+            tmem_ld_wait();
+            if (!mbar_wait(&rb[b], (g >> 1) & 1, abort_flag, ST_GEMM_EPILOGUE)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) pend[b] = false;
+            // row `lane` of the 32 x 32 fp32 box: 16-byte chunk c lives at chunk c ^ (lane & 7) (128-byte
+            // swizzle); the bf16 box's row is 64 bytes with chunk c at c ^ ((lane >> 1) & 3) (64-byte swizzle)
+            uint8_t* fr = stg + b * 4096 + lane * 128;
+            uint8_t* br = stg + 8192 + b * 2048 + lane * 64;
+            unsigned long long v[16];
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              const float4 x = *reinterpret_cast<const float4*>(fr + ((c ^ (lane & 7)) << 4));
+              v[2 * c] = f2_add(f2_pack(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1])), f2_pack(x.x, x.y));
+              v[2 * c + 1] =
+                  f2_add(f2_pack(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), f2_pack(x.z, x.w));
+            }
+            if (ep.bias) {
+              const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const float4 bb = __ldg(b4 + j);
+                v[2 * j] = f2_add(v[2 * j], f2_pack(bb.x, bb.y));
+                v[2 * j + 1] = f2_add(v[2 * j + 1], f2_pack(bb.z, bb.w));
+              }
+            }
+            if (ep.stats_out && m < M) {  // four independent fp32x2 partial sums per pass
+              unsigned long long a4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+              for (int j = 0; j < 16; j++) a4[j & 3] = f2_add(a4[j & 3], v[j]);
+              float s0, s1;
+              f2_unpack(f2_add(f2_add(a4[0], a4[1]), f2_add(a4[2], a4[3])), s0, s1);
+              const float mean = (s0 + s1) * (1.f / 32.f);
+              const unsigned long long nm = f2_pack(-mean, -mean);
+#pragma unroll
+              for (int j = 0; j < 4; j++) a4[j] = 0ull;
+#pragma unroll
+              for (int j = 0; j < 16; j++) {
+                const unsigned long long dd = f2_add(v[j], nm);
+                a4[j & 3] = f2_fma(dd, dd, a4[j & 3]);
+              }
+              f2_unpack(f2_add(f2_add(a4[0], a4[1]), f2_add(a4[2], a4[3])), s0, s1);
+              ep.stats_out[(long long)m * (N / 32) + n0 / 32] = make_float2(mean, s0 + s1);
+            }
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              float x0, x1, x2, x3;
+              f2_unpack(v[2 * c], x0, x1);
+              f2_unpack(v[2 * c + 1], x2, x3);
+              *reinterpret_cast<float4*>(fr + ((c ^ (lane & 7)) << 4)) = make_float4(x0, x1, x2, x3);
+              if (ep.out2 && (c & 1)) {  // two fp32 chunks = one 16-byte bf16 chunk
+                float y0, y1, y2, y3;
+                f2_unpack(v[2 * c - 2], y0, y1);
+                f2_unpack(v[2 * c - 1], y2, y3);
+                const int bc = c >> 1;
+                *reinterpret_cast<uint4*>(br + ((bc ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(pack_bf2(y0, y1), pack_bf2(y2, y3), pack_bf2(x0, x1), pack_bf2(x2, x3));
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmO, stg + b * 4096, n0, mw);
+              if (ep.out2) tma_store_2d(&tmO2, stg + 8192 + b * 2048, n0, mw);
+              bulk_commit();
+            }
+            ++g;
+          }
+          if (!ok) break;
+        }
+      } else if constexpr (MODE == 1) {
         // the residual of chunk i+1 is loaded while chunk i is processed, the first chunk's before the
         // accumulator wait (the residual does not depend on the MMAs)
         uint32_t rw[2][32];
@@ -760,6 +888,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0_leader + acc * 8);
     }
+    if constexpr (MODE == 2) {
+      if (lane == 0) {
+        // unwinding: residual loads still in flight land before the CTA exits; every store completes
+        for (int b = 0; b < 2; b++)
+          if (pend[b]) mbar_wait_drain(&rb[b], ((g + (uint32_t)((b - (int)(g & 1)) & 1)) >> 1) & 1, kDrainCycles);
+        bulk_wait_all<0>();
+      }
+      __syncwarp();
+    }
+    (void)ok;
   }
   tc_fence_before();
   __syncthreads();
@@ -771,29 +909,64 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   }
 }
 
+// The staged epilogue (mode 2) applies to fp32 out = acc (+ bias) + fp32 residual (+ bf16 copy, + row
+// statistics) with N % 32 == 0 and 16-byte pitches, when K <= 2048: there a tile's mainloop is shorter
+// than its register epilogue (proj, K 1152: 0.49 -> 0.33 ms per 130-crop launch), while a long mainloop
+// (fc2, K 4304) already hides that epilogue and would only lose the two mainloop stages.
+// VT_GEMM_TMA_EPI=0 turns it off.
+static bool pair_mode2_ok(const Epi& ep, int N, int K) {
+  static const int enabled = [] {
+    const char* e = getenv("VT_GEMM_TMA_EPI");
+    return e ? atoi(e) : 1;
+  }();
+  return enabled && K <= 2048 && ep.res && !ep.res_bf16 && ep.res_period == 0 && ep.out_f32 && !ep.gelu &&
+         ep.pk_T == 0 && !ep.ln_moments && N % 32 == 0 && ep.ldr % 4 == 0 && ep.ldo % 4 == 0 &&
+         (!ep.out2 || ep.ldo2 % 8 == 0);
+}
+
+template <int MODE>
+static void pair_attr(int dev) {
+  static bool done[64] = {false};
+  if (dev >= 0 && dev < 64 && !done[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PairCfg<MODE>::SMEM_BYTES);
+    done[dev] = true;
+  }
+}
+
 static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
                        int K, const Epi& ep) {
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tr, to, to2;
+  memset(&tr, 0, sizeof(tr));
+  memset(&to, 0, sizeof(to));
+  memset(&to2, 0, sizeof(to2));
   int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128);
   if (rc) return rc;
   rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, 128);
   if (rc) return rc;
-  static bool attr_done[64] = {false};
+  const int mode = !ep.res ? 0 : pair_mode2_ok(ep, N, K) ? 2 : 1;
+  if (mode == 2) {
+    rc = make_tmap_epi(&tr, ep.res, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldr, 32, 32, 128);
+    if (!rc) rc = make_tmap_epi(&to, ep.out, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo, 32, 32, 128);
+    if (!rc && ep.out2) rc = make_tmap_epi(&to2, ep.out2, 2, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo2, 32, 32, 64);
+    if (rc) return rc;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-    attr_done[dev] = true;
-  }
   const long long ntiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int max_clusters = sm_count() / 2;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
-  if (ep.res)
-    gemm_bf16_tc_pair_kernel<true><<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
-  else
-    gemm_bf16_tc_pair_kernel<false><<<2 * clusters, THREADS, P_SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  if (mode == 2) {
+    pair_attr<2>(dev);
+    gemm_bf16_tc_pair_kernel<2><<<2 * clusters, THREADS, PairCfg<2>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+  } else if (mode == 1) {
+    pair_attr<1>(dev);
+    gemm_bf16_tc_pair_kernel<1><<<2 * clusters, THREADS, PairCfg<1>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+  } else {
+    pair_attr<0>(dev);
+    gemm_bf16_tc_pair_kernel<0><<<2 * clusters, THREADS, PairCfg<0>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+  }
   return check_launch("vt_gemm (CTA pair)");
 }
 

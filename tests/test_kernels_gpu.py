@@ -82,9 +82,9 @@ def test_gemm_inplace_residual_periodic_addend_and_bf16_copy():
     assert torch.equal(copy, x2.to(BF))
 
 
-@pytest.mark.parametrize("M", [729, 1000, 3 * 729])
-def test_gemm_residual_row_statistics(M):
-    K, N = 1152, 1152
+@pytest.mark.parametrize("M,N", [(729, 1152), (1000, 1152), (3 * 729, 1152), (300, 96), (1000, 1184)])
+def test_gemm_residual_row_statistics(M, N):
+    K = 1152
     x, w, b = _operands(M, K, N, 7)
     res = torch.randn(M, N, device=DEV) * 3 + 1
     out = torch.empty(M, N, device=DEV)
