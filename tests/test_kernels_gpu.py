@@ -213,6 +213,23 @@ def test_attention_strided_qkv(B, H, T, D):
     assert rel(out, ref) < 3 * max(rel(sdpa_bf16, ref), 2e-3)
 
 
+@pytest.mark.parametrize("B,H,T,D", [(8, 16, 729, 72), (40, 16, 64, 64), (30, 12, 200, 64)])
+def test_attention_many_items_each_within_tolerance(B, H, T, D):
+    """More (query tile, head, crop) items than resident CTAs (2 per SM), so CTAs start while others run;
+    T = 64 gives one key tile per item.  The error is checked per item, so one wrong item cannot hide in
+    the global norm."""
+    qkv = torch.randn(B, T, 3 * H * D, device=DEV).to(BF)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    out = ops.VtAttn(H, T, D)(q, k, v).float().view(B, T, H, D)
+    ref = _attn_ref(q, k, v).transpose(1, 2).float()
+    Tt = (T + 127) // 128
+    pad = Tt * 128 - T
+    e = F.pad((out - ref).transpose(1, 2), (0, 0, 0, pad)).reshape(B, H, Tt, 128 * D).norm(dim=-1)
+    r = F.pad(ref.transpose(1, 2), (0, 0, 0, pad)).reshape(B, H, Tt, 128 * D).norm(dim=-1)
+    assert B * H * Tt > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    assert float((e / r).max()) < 1e-2
+
+
 @pytest.mark.parametrize("B,H,T,D", ATTN_CASES[:3])
 def test_attention_tcgen05_matches_mma_sync_kernel(B, H, T, D):
     qkv = torch.randn(B, T, 3 * H * D, device=DEV).to(BF)
