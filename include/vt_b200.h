@@ -152,6 +152,29 @@ int vt_crop_combine(cudaStream_t stream, const uint16_t* f, long long crop_strid
 int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_param, const uint16_t* u,
              long long ldu, float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first);
 
+/* One recurrent step of the full TAPNext++ block's temporal mixing for R tokens of width W (W % 64 == 0,
+ * 64-channel heads): xc = conv_1d over the taps hist_old, hist_mid, hist_new (x_(t-3), x_(t-2), x_(t-1),
+ * bf16) and xx (x_t, bf16), oldest first, + conv_b; the block-diagonal gates gx = sigmoid(xc_q wx[q] + bx),
+ * ga = sigmoid(xc_q wa[q] + ba) per head q (wx / wa fp32 [W/64][64 in][64 out]); log_a = -8 ga softplus_a;
+ * h = xc gx (first != 0) or a h + (xc gx) sqrt(1 - a^2) (fp32 state h, updated in place); z = bf16(h) yg.
+ * Rounding follows the reference's bf16 restatement.  x_t is written over hist_old (the caller rotates
+ * the three history roles); conv_w fp32 [4][W], conv_b / softplus_a / bx / ba fp32 [W].
+ * Replaces: the recurrent block's conv_1d + rg_lru + (x * gelu(y)) of tapnext/npu/step8.py:477-480, whose
+ * element-wise numerics the reference restates in tapnext/npu/pack8.py:252-279 (ssm_ref). */
+int vt_ssm_step(cudaStream_t stream, const uint16_t* yg, const uint16_t* xx, long long ldi, uint16_t* hist_old,
+                const uint16_t* hist_mid, const uint16_t* hist_new, long long ldh, float* h, long long ldhs,
+                const float* conv_w, const float* conv_b, const float* softplus_a, const float* wx, const float* bx,
+                const float* wa, const float* ba, uint16_t* z, long long ldz, int R, int W, int first);
+
+/* Gated MLP combine: out[r, j] = bf16(bf16(gelu_tanh(G[r, j])) * G[r, F + j]), j < F, for the bf16
+ * ffw_up output G = [gate | up] [R][2F] (F % 8 == 0, 16-byte aligned rows).
+ * Replaces: the gated_a / gated_b GEMM epilogues of tapnext/npu/mm8.cc:937-960 (mlp_block, step8.py:483). */
+int vt_gated_gelu_mul(cudaStream_t stream, const uint16_t* G, long long ldg, uint16_t* out, long long ldo, int R, int F);
+
+/* Exact GELU in place on a bf16 [R][N] matrix (N % 8 == 0): x = bf16(x (1 + erf(x / sqrt 2)) / 2).
+ * Replaces: the ViT MLP's nn.GELU() (the gelu_pan epilogue, tapnext/npu/pack8.py:246-250 gelu_erf_ref). */
+int vt_gelu_erf(cudaStream_t stream, uint16_t* x, long long ld, int R, int N);
+
 #ifdef __cplusplus
 }
 #endif

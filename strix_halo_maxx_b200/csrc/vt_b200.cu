@@ -6,3 +6,4 @@
 #include "attn_tc.cu"
 #include "attn_noalloc.cu"
 #include "elementwise.cu"
+#include "ssm.cu"

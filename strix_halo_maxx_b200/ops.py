@@ -247,3 +247,33 @@ def rglru(G, a_param, u, state, x, c, first):
     rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), u.data_ptr(), u.stride(0),
                         state.data_ptr(), state.stride(0), x.data_ptr(), x.stride(0), M, W, float(c), int(bool(first)))
     check(rc, "vt_rglru")
+
+
+def ssm_step(yg, xx, hist, h, conv_w, conv_b, softplus_a, wx, bx, wa, ba, z, first):
+    """TAPNext++ recurrent step (vt_ssm_step): yg, xx [R, W] bf16 views; hist = (x_(t-3), x_(t-2), x_(t-1))
+    bf16 [R, W] -- x_t is written over hist[0], so the caller rotates; h [R, W] fp32 state in place;
+    z [R, W] bf16 out."""
+    R, W = z.shape
+    old, mid, new = hist
+    rc = lib().vt_ssm_step(_stream(), yg.data_ptr(), xx.data_ptr(), yg.stride(0), old.data_ptr(), mid.data_ptr(),
+                           new.data_ptr(), old.stride(0), h.data_ptr(), h.stride(0), conv_w.data_ptr(),
+                           conv_b.data_ptr(), softplus_a.data_ptr(), wx.data_ptr(), bx.data_ptr(), wa.data_ptr(),
+                           ba.data_ptr(), z.data_ptr(), z.stride(0), R, W, int(bool(first)))
+    check(rc, "vt_ssm_step")
+    return z
+
+
+def gated_gelu_mul(G, out):
+    """out [R, F] = gelu_tanh(G[:, :F]) * G[:, F:] in bf16 (vt_gated_gelu_mul)."""
+    R, F = out.shape
+    rc = lib().vt_gated_gelu_mul(_stream(), G.data_ptr(), G.stride(0), out.data_ptr(), out.stride(0), R, F)
+    check(rc, "vt_gated_gelu_mul")
+    return out
+
+
+def gelu_erf(x):
+    """Exact GELU in place on a bf16 [R, N] matrix (vt_gelu_erf)."""
+    R, N = x.shape
+    rc = lib().vt_gelu_erf(_stream(), x.data_ptr(), x.stride(0), R, N)
+    check(rc, "vt_gelu_erf")
+    return x

@@ -1,0 +1,115 @@
+"""The full TAPNext++ per-frame block step on B200 (the reference's block, tapnext/npu/step8.py:469-486;
+the BASELINE config 3 step in tapnext.py simplifies it).  Token layout and sizes as config 3: 8x8 patches
+of a 256x256 frame (1024 tokens) + position embedding, then the point-query tokens, width 768, 12 heads x 64.
+
+Per block, in the reference's order:
+    t   = RMSNorm(x) (1 + scale)                       vt_rmsnorm
+    yg  = gelu_tanh(t Wy^T + by), xx = t Wx^T + bx     two vt_gemm launches (linear_yx split), bf16
+    z   = RG-LRU(conv_1d(xx)) * yg                     vt_ssm_step (4-tap history ring, fp32 state)
+    x  += z Wout^T + bout                              vt_gemm, fp32 residual epilogue
+    G   = RMSNorm(x) (1 + scale) Wup^T + bup           vt_rmsnorm, vt_gemm (N = 2 x 3072: [gate | up])
+    x  += (gelu_tanh(gate) * up) Wdown^T + bdown       vt_gated_gelu_mul, vt_gemm + residual
+    x  += MHA(LN_1(x))                                 the tower's qkv-tile GEMM + tcgen05 attention (d 64)
+    x  += gelu_erf(LN_2(x) W0^T + b0) W3^T + b3        vt_gemm, vt_gelu_erf, vt_gemm + residual
+and the encoder LayerNorm after the last block.  The recurrent state (h fp32 and the last three xx of every
+block) lives on the device, owned by this object; reset() starts a new video.
+"""
+import torch
+import torch.nn.functional as F
+
+from .config import TAPNEXT, TapNextConfig
+from . import ops
+from .ops import BF16, _pad8
+from .tower import _dev_mat, _dev_vec
+
+F32 = torch.float32
+
+
+class TapNextPPStep:
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda"):
+        self.cfg = cfg
+        dev = self.dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = self.dev = torch.device("cuda", torch.cuda.current_device())
+        W = weights
+        Wd, Fh = cfg.width, cfg.ff
+        self.n_blocks = sum(1 for k in W if k.endswith(".yx_w"))
+        self.pe_w, self.pe_ld = _dev_mat(W["patch_w"], dev)
+        self.pe_b = _dev_vec(W["patch_b"], dev)
+        self.pos = _dev_vec(W["pos_emb"], dev).reshape(cfg.n_img_tok, Wd)
+        self.blocks = []
+        for i in range(self.n_blocks):
+            p = f"blocks.{i}."
+            b = {}
+            yx_w, yx_b = torch.as_tensor(W[p + "yx_w"]), torch.as_tensor(W[p + "yx_b"])
+            b["y_w"], b["y_ld"] = _dev_mat(yx_w[:Wd], dev)
+            b["x_w"], b["x_ld"] = _dev_mat(yx_w[Wd:], dev)
+            b["y_b"], b["x_b"] = _dev_vec(yx_b[:Wd], dev), _dev_vec(yx_b[Wd:], dev)
+            for n in ("out", "up", "down", "qkv", "proj", "fc1", "fc2"):
+                b[n + "_w"], b[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
+                b[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
+            b["rms0"] = _dev_vec(1.0 + torch.as_tensor(W[p + "rms0_scale"]).float(), dev)
+            b["rms1"] = _dev_vec(1.0 + torch.as_tensor(W[p + "rms1_scale"]).float(), dev)
+            for n in ("conv_w", "conv_b", "gx_w", "gx_b", "ga_w", "ga_b", "ln1_w", "ln1_b", "ln2_w", "ln2_b"):
+                b[n] = _dev_vec(W[p + n], dev)
+            b["softplus_a"] = _dev_vec(F.softplus(torch.as_tensor(W[p + "a_param"]).double()).float(), dev)
+            self.blocks.append(b)
+        self.fin_w = _dev_vec(W["final_ln_w"], dev)
+        self.fin_b = _dev_vec(W["final_ln_b"], dev)
+        T = cfg.ntok
+        self.a_pe = torch.zeros(cfg.n_img_tok, _pad8(cfg.patch_k), dtype=BF16, device=dev)
+        self.x = torch.empty(T, Wd, dtype=F32, device=dev)
+        self.t = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.yx = torch.empty(T, 2 * Wd, dtype=BF16, device=dev)
+        self.z = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.G = torch.empty(T, 2 * Fh, dtype=BF16, device=dev)
+        self.m = torch.empty(T, Fh, dtype=BF16, device=dev)
+        self.tiles = ops.attn_tiles(1, T, cfg.heads, cfg.head_dim, dev)
+        self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.f = torch.empty(T, Fh, dtype=BF16, device=dev)
+        self.h = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
+        self.hist = torch.zeros(self.n_blocks, 3, T, Wd, dtype=BF16, device=dev)
+        self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
+        self.reset()
+
+    def reset(self):
+        """A new video: zero conv history, no recurrent state."""
+        self.hist.zero_()
+        self.frame = 0
+
+    def step(self, frame, queries):
+        """frame [3, 256, 256] in [-1, 1], queries [n_queries, 768] fp32 (device) -> [ntok, 768] bf16."""
+        cfg = self.cfg
+        T, Wd, NI, Fh = cfg.ntok, cfg.width, cfg.n_img_tok, cfg.ff
+        ops.im2col(frame.reshape(1, *frame.shape[-3:]), cfg.patch, self.a_pe)
+        ops.gemm(self.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
+                 res=self.pos, res_period=NI, out=self.x[:NI])
+        self.x[NI:].copy_(queries)
+        k = self.frame % 3  # history roles: x_(t-3) = slot k, x_(t-2) = k+1, x_(t-1) = k+2 (mod 3)
+        first = self.frame == 0
+        for i, b in enumerate(self.blocks):
+            hist = (self.hist[i, k], self.hist[i, (k + 1) % 3], self.hist[i, (k + 2) % 3])
+            # recurrent block (step8.py:474-481)
+            ops.rms_norm(self.x, b["rms0"], cfg.eps, out=self.t)
+            ops.gemm(self.t, b["y_w"], b["y_ld"], Wd, Wd, b["y_b"], gelu=True, out=self.yx[:, :Wd])
+            ops.gemm(self.t, b["x_w"], b["x_ld"], Wd, Wd, b["x_b"], out=self.yx[:, Wd:])
+            ops.ssm_step(self.yx[:, :Wd], self.yx[:, Wd:], hist, self.h[i], b["conv_w"], b["conv_b"],
+                         b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first)
+            ops.gemm(self.z, b["out_w"], b["out_ld"], Wd, Wd, b["out_b"], res=self.x, out=self.x)
+            # gated MLP (step8.py:482-483)
+            ops.rms_norm(self.x, b["rms1"], cfg.eps, out=self.t)
+            ops.gemm(self.t, b["up_w"], b["up_ld"], Wd, 2 * Fh, b["up_b"], out=self.G)
+            ops.gated_gelu_mul(self.G, self.m)
+            ops.gemm(self.m, b["down_w"], b["down_ld"], Fh, Wd, b["down_b"], res=self.x, out=self.x)
+            # ViT block (step8.py:484-486)
+            ops.layer_norm(self.x, b["ln1_w"], b["ln1_b"], cfg.eps, out=self.t)
+            ops.gemm_qkv_tiles(self.t, b["qkv_w"], b["qkv_ld"], Wd, b["qkv_b"], self.tiles, T, cfg.heads, cfg.head_dim)
+            ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
+            ops.gemm(self.a, b["proj_w"], b["proj_ld"], Wd, Wd, b["proj_b"], res=self.x, out=self.x)
+            ops.layer_norm(self.x, b["ln2_w"], b["ln2_b"], cfg.eps, out=self.t)
+            ops.gemm(self.t, b["fc1_w"], b["fc1_ld"], Wd, Fh, b["fc1_b"], out=self.f)
+            ops.gelu_erf(self.f)
+            ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x)
+        ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+        self.frame += 1
+        return self.out

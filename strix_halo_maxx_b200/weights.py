@@ -20,6 +20,12 @@ def _draw(seed, idx, shape, kind, affine):
         return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
     if kind == "normal1":
         return rng.standard_normal(shape, dtype=np.float32)
+    if kind == "conv":  # temporal conv taps
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.5)
+    if kind == "scale":  # RMSNorm scale of the (1 + scale) convention
+        if affine != "random":
+            return np.zeros(shape, np.float32)
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.1)
     if affine != "random":
         return np.ones(shape, np.float32) if kind == "gamma" else np.zeros(shape, np.float32)
     if kind == "gamma":
@@ -83,6 +89,41 @@ def tapnext_spec(cfg: TapNextConfig, n_blocks=None):
 
 def tapnext_weights(cfg: TapNextConfig, seed=0, n_blocks=None, affine="zero"):
     return _generate(tapnext_spec(cfg, n_blocks), seed, affine)
+
+
+def tapnextpp_spec(cfg: TapNextConfig, n_blocks=None):
+    """The full TAPNext++ block's weight set (tapnext/npu/step8.py:161-183, 205-215): per block the recurrent
+    block (temporal RMSNorm scale, linear_yx 768 -> 1536, conv_1d 4 taps, block-diagonal RG-LRU gates
+    [12, 64 in, 64 out], a_param, linear_out), the gated MLP (channel RMSNorm scale, ffw_up 768 -> 2 x 3072 as
+    [gate | up], ffw_down 3072 -> 768) and the ViT block (ln_1, qkv, out_proj, ln_2, mlp.0, mlp.3)."""
+    W, F = cfg.width, cfg.ff
+    H, D = cfg.heads, cfg.head_dim
+    nb = cfg.n_blocks if n_blocks is None else n_blocks
+    s = [("patch_w", (W, cfg.patch_k), "w"), ("patch_b", (W,), "bias"), ("pos_emb", (cfg.n_img_tok, W), "w")]
+    for i in range(nb):
+        p = f"blocks.{i}."
+        s += [(p + "rms0_scale", (W,), "scale"),
+              (p + "yx_w", (2 * W, W), "w"), (p + "yx_b", (2 * W,), "bias"),
+              (p + "conv_w", (4, W), "conv"), (p + "conv_b", (W,), "bias"),
+              (p + "gx_w", (H, D, D), "w"), (p + "gx_b", (W,), "bias"),
+              (p + "ga_w", (H, D, D), "w"), (p + "ga_b", (W,), "bias"),
+              (p + "a_param", (W,), "normal1"),
+              (p + "out_w", (W, W), "w"), (p + "out_b", (W,), "bias"),
+              (p + "rms1_scale", (W,), "scale"),
+              (p + "up_w", (2 * F, W), "w"), (p + "up_b", (2 * F,), "bias"),
+              (p + "down_w", (W, F), "w"), (p + "down_b", (W,), "bias"),
+              (p + "ln1_w", (W,), "gamma"), (p + "ln1_b", (W,), "beta"),
+              (p + "qkv_w", (3 * W, W), "w"), (p + "qkv_b", (3 * W,), "bias"),
+              (p + "proj_w", (W, W), "w"), (p + "proj_b", (W,), "bias"),
+              (p + "ln2_w", (W,), "gamma"), (p + "ln2_b", (W,), "beta"),
+              (p + "fc1_w", (F, W), "w"), (p + "fc1_b", (F,), "bias"),
+              (p + "fc2_w", (W, F), "w"), (p + "fc2_b", (W,), "bias")]
+    s += [("final_ln_w", (W,), "gamma"), ("final_ln_b", (W,), "beta")]
+    return s
+
+
+def tapnextpp_weights(cfg: TapNextConfig, seed=0, n_blocks=None, affine="zero"):
+    return _generate(tapnextpp_spec(cfg, n_blocks), seed, affine)
 
 
 def crop_pixels(n, cfg: TowerConfig, seed=1, first=0):

@@ -1,6 +1,8 @@
 """Pin the CPU oracle (oracle/tower_ref.py) to the reference: the fixtures in tests/golden were produced
 by the reference's own FastMD2._vision (moondream/gpu/md2fast.py:147-160) on the same seeded weights
 and inputs (tests/golden/make_golden.py)."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -69,3 +71,27 @@ def test_golden_detects_a_planted_error():
     pix = tower_ref.normalize_u8(img)
     bad = tower_ref.tower(pix.transpose(2, 3), W, CFG, eps=m["eps"], n_blocks=2)[0]
     assert max(golden_rel(bad, g)) > 1e-2
+
+
+@pytest.mark.parametrize("case,first", [("first", True), ("next", False)])
+def test_ssm_restatement_matches_reference_ssm_ref(case, first):
+    """oracle.tapnextpp_ref.ssm_bf16 against the outputs of the reference's own tapnext/npu/pack8.py
+    ssm_ref (tests/golden/make_golden_ssm.py): bit-exact z and h."""
+    import numpy as np
+    from oracle.tapnextpp_ref import ssm_bf16
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "ssm_ref_cases.npz"))
+    a = {k.split(".", 1)[1]: g[k] for k in g.files if k.startswith(case + ".")}
+    z, h = ssm_bf16(a["y"], a["x"], a["xm1"], a["xm2"], a["xm3"], a["h0"], a["conv_w"], a["conv_b"], a["a_param"],
+                    a["wx"], a["bx"], a["wa"], a["ba"], first)
+    assert np.array_equal(z.numpy(), a["z"]) and np.array_equal(h.numpy(), a["h"])
+
+
+def test_ssm_restatement_detects_a_planted_error():
+    """The same check fails for a restatement with the conv taps in the wrong order."""
+    import numpy as np
+    from oracle.tapnextpp_ref import ssm_bf16
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "ssm_ref_cases.npz"))
+    a = {k.split(".", 1)[1]: g[k] for k in g.files if k.startswith("next.")}
+    z, _ = ssm_bf16(a["y"], a["x"], a["xm1"], a["xm2"], a["xm3"], a["h0"], a["conv_w"][::-1].copy(), a["conv_b"],
+                    a["a_param"], a["wx"], a["bx"], a["wa"], a["ba"], False)
+    assert not np.array_equal(z.numpy(), a["z"])

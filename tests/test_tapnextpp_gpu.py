@@ -1,0 +1,86 @@
+"""Full TAPNext++ block step on the GPU: its new kernels against the oracle's restatements, and the whole
+step against the CPU fp32 oracle over several frames (recurrent state and conv history carried)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from strix_halo_maxx_b200.config import TapNextConfig
+from strix_halo_maxx_b200 import ops, weights as wg
+from strix_halo_maxx_b200.tapnextpp import TapNextPPStep
+from strix_halo_maxx_b200._lib import device_status
+from oracle import tapnextpp_ref as R
+from helpers import assert_tokens_close
+
+CFG = TapNextConfig()
+BF = torch.bfloat16
+DEV = "cuda"
+
+
+def _bf(a):
+    return torch.as_tensor(a, dtype=torch.float32).to(BF)
+
+
+@pytest.mark.parametrize("first", [True, False])
+def test_ssm_step_matches_bf16_restatement(first):
+    """vt_ssm_step against ssm_bf16 (the reference's ssm_ref rounding points) on every head, with a
+    partial row block (R = 100); the float64 gate sums make it agree to the last bf16 bit almost always."""
+    g = torch.Generator().manual_seed(5)
+    Rn, W, H = 100, 768, 12
+    rnd = lambda *s, sc=1.0: torch.randn(*s, generator=g) * sc
+    y, xx, xm1, xm2, xm3 = [_bf(rnd(Rn, W)) for _ in range(5)]
+    h0 = rnd(Rn, W)
+    conv_w, conv_b = rnd(4, W, sc=0.5), rnd(W, sc=0.1)
+    a_param = rnd(W)
+    wx, wa = _bf(rnd(H, 64, 64, sc=0.15)).float(), _bf(rnd(H, 64, 64, sc=0.15)).float()  # bf16 weights
+    bx, ba = rnd(W, sc=0.1), rnd(W, sc=0.1)
+    hist = [t.to(DEV).contiguous() for t in (xm3, xm2, xm1)]
+    h = h0.clone().to(DEV)
+    z = torch.empty(Rn, W, dtype=BF, device=DEV)
+    sp = torch.nn.functional.softplus(a_param.double()).float()
+    dv = lambda t: t.to(DEV).contiguous()
+    ops.ssm_step(dv(y), dv(xx), hist, h, dv(conv_w), dv(conv_b), dv(sp), dv(wx), dv(bx), dv(wa), dv(ba), z, first)
+    zr, hr = [], []
+    for q in range(H):
+        s = slice(64 * q, 64 * q + 64)
+        zq, hq = R.ssm_bf16(y[:, s].float(), xx[:, s].float(), xm1[:, s].float(), xm2[:, s].float(), xm3[:, s].float(),
+                            h0[:, s], conv_w[:, s], conv_b[s], a_param[s], wx[q], bx[s], wa[q], ba[s], first)
+        zr.append(zq)
+        hr.append(hq)
+    zr, hr = torch.cat(zr, 1), torch.cat(hr, 1)
+    zg = z.float().cpu()
+    mism = (zg != zr)
+    assert mism.float().mean() < 1e-3, float(mism.float().mean())
+    # any mismatch is one bf16 step at most
+    assert torch.all((zg - zr).abs() <= zr.abs() * 2 ** -7 + 1e-30)
+    assert torch.allclose(h.cpu(), hr, rtol=2e-6, atol=1e-6)
+    assert torch.equal(hist[0].cpu(), xx)  # x_t replaced the oldest tap
+
+
+def test_gated_gelu_mul_and_gelu_erf():
+    g = torch.Generator().manual_seed(6)
+    G = _bf(torch.randn(77, 2 * 3072, generator=g) * 2).to(DEV)
+    out = torch.empty(77, 3072, dtype=BF, device=DEV)
+    ops.gated_gelu_mul(G, out)
+    gf = G.float()
+    ref = (R.gelu_tanh(gf[:, :3072]).to(BF).float() * gf[:, 3072:]).to(BF).float()
+    assert torch.allclose(out.float(), ref, rtol=2e-2, atol=1e-3)
+    x = _bf(torch.randn(50, 3072, generator=g) * 3).to(DEV)
+    ref2 = R.gelu_erf(x.float()).to(BF).float()
+    ops.gelu_erf(x)
+    assert torch.allclose(x.float(), ref2, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("n_blocks,n_frames,affine", [(12, 2, "zero"), (2, 6, "random")])
+def test_tapnextpp_stream(n_blocks, n_frames, affine):
+    device_status(clear=True)
+    W = wg.tapnextpp_weights(CFG, seed=9, n_blocks=n_blocks, affine=affine)
+    frames, queries = wg.tapnext_inputs(CFG, n_frames, seed=2)
+    eng = TapNextPPStep(W, CFG, device=DEV)
+    state = None
+    for f in range(n_frames):
+        ref, state = R.step(frames[f], queries[f], W, CFG, state, n_blocks)
+        out = eng.step(torch.from_numpy(frames[f]).to(DEV), torch.from_numpy(queries[f]).to(DEV))
+        assert_tokens_close(out.float().cpu(), ref, what=f"frame {f}")
+    assert device_status(clear=True) == 0
