@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--no-frame", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     ap.add_argument("--no-fold", action="store_true", help="LayerNorm as separate passes instead of folded into GEMMs")
+    ap.add_argument("--no-tapnext", action="store_true", help="skip the TAPNext per-frame step timings (N=1 only)")
     return ap.parse_args()
 
 
@@ -314,6 +315,10 @@ def run_vt(a):
         torch.cuda.synchronize()
         frame_ms = g0.elapsed_time(g1) / 10
 
+    tap = None
+    if world == 1 and not a.no_tapnext:
+        tap = tapnext_frame_ms(dev)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         v, cores = cpu_oracle_rate(W, cfg, 1, 2)
@@ -332,6 +337,7 @@ def run_vt(a):
                        "l2": "inputs larger than L2 (pixels %.0f MB per step, activations GBs)" % (a.crops * 3 * 378 * 378 * 2 / 1e6)},
             "ms_per_frame_13crop_throughput": 13 * 1000.0 / value,
             "ms_per_frame_13crop_latency": frame_ms,
+            "tapnext_ms_per_frame": tap,
             "tflops_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12,
             "frac_of_peak_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12 / (sustained * world),
             "roofline": {"kernel": "gemm_bf16_tc_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
@@ -350,6 +356,34 @@ def run_vt(a):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def tapnext_frame_ms(dev, n_frames=16):
+    """Config 3 (the BASELINE simplification) and the full TAPNext++ block: 12 blocks, 1280 tokens, the
+    state carried over n_frames frames of one video; mean ms per frame (CUDA events, 3 warm-up frames)."""
+    from strix_halo_maxx_b200.config import TAPNEXT
+    from strix_halo_maxx_b200.weights import tapnext_weights, tapnextpp_weights, tapnext_inputs
+    from strix_halo_maxx_b200.tapnext import TapNextStep
+    from strix_halo_maxx_b200.tapnextpp import TapNextPPStep
+    frames, queries = tapnext_inputs(TAPNEXT, n_frames, seed=2)
+    fr, qs = torch.from_numpy(frames).to(dev), torch.from_numpy(queries).to(dev)
+    out = {}
+    for name, cls, wfn in (("config3", TapNextStep, tapnext_weights), ("tapnextpp", TapNextPPStep, tapnextpp_weights)):
+        eng = cls(wfn(TAPNEXT, seed=9), TAPNEXT, device=dev)
+        for f in range(3):
+            eng.step(fr[f], qs[f])
+        eng.reset()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for f in range(n_frames):
+            eng.step(fr[f], qs[f])
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = e0.elapsed_time(e1) / n_frames
+        del eng
+    out["frames"] = n_frames
+    return out
 
 
 def main():

@@ -12,7 +12,6 @@ namespace ssm {
 constexpr int RB = 32, HD = 64, THREADS = 256;
 
 __device__ __forceinline__ float bfr(float v) { return bfround(v); }
-__device__ __forceinline__ float bfr_d(double v) { return bfround((float)v); }  // float64 -> float32 -> bf16
 
 // One CTA: RB rows x one head (64 channels).  hist_old / hist_mid / hist_new hold x_(t-3) / x_(t-2) / x_(t-1)
 // (zeros before the first frames); x_t is written over hist_old, so the caller rotates the three roles.
@@ -47,24 +46,27 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
     xcs[r][c] = xc;
   }
   __syncthreads();
-  // gates (float64 dot products, as the reference's float64 matmul), RG-LRU, z
+  // gates, RG-LRU, z.  The reference sums the 64 bf16 x bf16 products in float64 and evaluates sigmoid / exp
+  // in float64 before rounding to bf16; here the products are exact in fp32, the sums and transcendentals
+  // are fp32, and the bf16 results differ from the float64 path only when a value falls within a few fp32
+  // ulps of a bf16 rounding boundary (about 1e-4 of the elements, by one bf16 step).
   const int o = tid % HD, col = c0 + o;
   const float bxo = bfr(bx[col]), bao = bfr(ba[col]), spo = bfr(sp[col]);
   for (int r = tid / HD; r < RB; r += THREADS / HD) {
     const int row = r0 + r;
     if (row >= R) break;
-    double dx = 0.0, da = 0.0;
-#pragma unroll 8
+    float dx = 0.f, da = 0.f;
+#pragma unroll 16
     for (int i = 0; i < HD; i++) {
-      const double v = (double)xcs[r][i];
-      dx = fma(v, (double)wxs[i][o], dx);
-      da = fma(v, (double)was[i][o], da);
+      const float v = xcs[r][i];
+      dx = fmaf(v, wxs[i][o], dx);
+      da = fmaf(v, was[i][o], da);
     }
-    const float gx_pre = bfr(__fadd_rn(bfr_d(dx), bxo)), ga_pre = bfr(__fadd_rn(bfr_d(da), bao));
-    const float gx = bfr_d(1.0 / (1.0 + exp(-(double)gx_pre)));
-    const float ga = bfr_d(1.0 / (1.0 + exp(-(double)ga_pre)));
+    const float gx_pre = bfr(__fadd_rn(bfr(dx), bxo)), ga_pre = bfr(__fadd_rn(bfr(da), bao));
+    const float gx = bfr(1.f / (1.f + expf(-gx_pre)));
+    const float ga = bfr(1.f / (1.f + expf(-ga_pre)));
     const float log_a = bfr(__fmul_rn(bfr(-8.f * ga), spo));
-    const float a = bfr_d(exp((double)log_a));
+    const float a = bfr(expf(log_a));
     const float xc = xcs[r][o];
     const float gated = bfr(__fmul_rn(xc, gx));
     const size_t is = (size_t)row * ldhs + col;
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
       hn = gated;
       hb = gated;
     } else {
-      const float e2 = bfr_d(exp((double)bfr(2.f * log_a)));
+      const float e2 = bfr(expf(bfr(2.f * log_a)));
       const float mult = bfr(sqrtf(bfr(__fsub_rn(1.f, e2))));
       const float nx = bfr(__fmul_rn(gated, mult));
       hn = __fadd_rn(__fmul_rn(a, h[is]), nx);
