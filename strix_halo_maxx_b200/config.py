@@ -87,5 +87,36 @@ class TapNextConfig:
         return self.n_blocks * (vit + gates) + pe
 
 
+@dataclass(frozen=True)
+class TextConfig:
+    """The moondream2 text decoder that consumes the tower's features (FastMD2._text_layers / _encode /
+    _query, moondream/gpu/md2fast.py:162-212; dims as moondream/gpu/gemm_bench.py:14): 24 parallel
+    attention + MLP blocks of width 2048, 32 heads x 64 with rotary embedding on the first 32 dims of each
+    head (md2fast.py:29, 162-167), a 730-token prefix (bos + 729 image tokens) and a 32-token question
+    whose yes / no logits are read at its last real token."""
+    dim: int = 2048
+    heads: int = 32
+    head_dim: int = 64
+    ff: int = 8192
+    n_layers: int = 24
+    rot: int = 32
+    theta: float = 10000.0
+    prefix: int = 730
+    q_len: int = 32
+    vocab: int = 1024           # synthetic embedding rows (the tokenizer and 51200-row table are not needed)
+    n_yn: int = 4               # yes / no rows of the lm head (lm_small, md2fast.py:139-143)
+    eps: float = 1e-5           # torch's layer_norm default, as _ln (md2fast.py:43-44)
+
+    @property
+    def ctx(self) -> int:
+        return self.prefix + self.q_len
+
+    def flops(self, n) -> int:
+        """GEMM FLOPs of n tokens through all layers (attention excluded)."""
+        D, Fh = self.dim, self.ff
+        return self.n_layers * 2 * n * D * (3 * D + D + 2 * Fh)
+
+
 TOWER = TowerConfig()
 TAPNEXT = TapNextConfig()
+TEXT = TextConfig()

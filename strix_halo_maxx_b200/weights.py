@@ -126,6 +126,39 @@ def tapnextpp_weights(cfg: TapNextConfig, seed=0, n_blocks=None, affine="zero"):
     return _generate(tapnextpp_spec(cfg, n_blocks), seed, affine)
 
 
+def text_spec(cfg, n_layers=None):
+    """The text decoder's weight set, named after FastMD2's attributes (md2fast.py:111-117, 143): wte,
+    tblocks[i].{ln, qkv, proj, fc1, fc2}, tpost_ln, lm_small (the yes / no rows of lm_head)."""
+    D, Fh = cfg.dim, cfg.ff
+    nl = cfg.n_layers if n_layers is None else n_layers
+    s = [("wte", (cfg.vocab, D), "normal1")]
+    for i in range(nl):
+        p = f"tblocks.{i}."
+        s += [(p + "ln_w", (D,), "gamma"), (p + "ln_b", (D,), "beta"),
+              (p + "qkv_w", (3 * D, D), "w"), (p + "qkv_b", (3 * D,), "bias"),
+              (p + "proj_w", (D, D), "w"), (p + "proj_b", (D,), "bias"),
+              (p + "fc1_w", (Fh, D), "w"), (p + "fc1_b", (Fh,), "bias"),
+              (p + "fc2_w", (D, Fh), "w"), (p + "fc2_b", (D,), "bias")]
+    s += [("tpost_ln_w", (D,), "gamma"), ("tpost_ln_b", (D,), "beta"),
+          ("lm_small_w", (cfg.n_yn, D), "w"), ("lm_small_b", (cfg.n_yn,), "bias")]
+    return s
+
+
+def text_weights(cfg, seed=0, n_layers=None, affine="zero"):
+    return _generate(text_spec(cfg, n_layers), seed, affine)
+
+
+def text_inputs(cfg, seed=5):
+    """Image-token embeddings N(0, 1) [729, dim] (the projection output), bos id, and a question: token ids
+    [q_len] in the synthetic vocabulary with its last real position."""
+    rng = np.random.default_rng(np.random.SeedSequence([int(seed), 11]))
+    emb = rng.standard_normal((cfg.prefix - 1, cfg.dim), dtype=np.float32)
+    n_real = int(rng.integers(cfg.q_len // 2, cfg.q_len + 1))
+    ids = np.zeros(cfg.q_len, np.int64)
+    ids[:n_real] = rng.integers(1, cfg.vocab, n_real)
+    return emb, 0, ids, n_real - 1
+
+
 def crop_pixels(n, cfg: TowerConfig, seed=1, first=0):
     """Crops n pixels U[-1,1] as float32 [n, 3, img, img]; crop i uses stream (seed, 1_000_000 + first + i)."""
     out = np.empty((n, cfg.in_ch, cfg.img, cfg.img), np.float32)

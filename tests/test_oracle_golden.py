@@ -95,3 +95,32 @@ def test_ssm_restatement_detects_a_planted_error():
     z, _ = ssm_bf16(a["y"], a["x"], a["xm1"], a["xm2"], a["xm3"], a["h0"], a["conv_w"][::-1].copy(), a["conv_b"],
                     a["a_param"], a["wx"], a["bx"], a["wa"], a["ba"], False)
     assert not np.array_equal(z.numpy(), a["z"])
+
+
+def _text_case():
+    from strix_halo_maxx_b200.config import TEXT
+    from oracle import text_ref
+    W = wg.text_weights(TEXT, seed=3, n_layers=2, affine="random")
+    emb, bos, ids, last = wg.text_inputs(TEXT, seed=5)
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "text_2_random.npz"))
+    return TEXT, text_ref, W, emb, bos, ids, last, g
+
+
+def test_text_oracle_matches_reference_text_layers_and_query():
+    """oracle.text_ref against the reference's own FastMD2._text_layers / _query outputs
+    (tests/golden/make_golden_text.py): the prefix hidden states and the yes / no logits."""
+    TEXT, text_ref, W, emb, bos, ids, last, g = _text_case()
+    x, cache = text_ref.encode(emb, bos, W, TEXT, n_layers=2)
+    logits = text_ref.query(ids, last, W, TEXT, cache, n_layers=2)
+    assert np.allclose(x.numpy()[g["rows"]], g["out_rows"], rtol=1e-5, atol=1e-5)
+    assert np.allclose(np.linalg.norm(x.numpy(), axis=1), g["norms"], rtol=1e-5)
+    assert np.allclose(logits.numpy(), g["logits"], rtol=1e-5, atol=1e-5)
+
+
+def test_text_oracle_detects_a_planted_error():
+    """The same fixture rejects a restatement with the wrong rotary base (theta 1000 instead of 10000).
+    (A wrong pair layout of the rotated dims would not show: it permutes q and k alike, so q.k is unchanged.)"""
+    import dataclasses
+    TEXT, text_ref, W, emb, bos, ids, last, g = _text_case()
+    x, _ = text_ref.encode(emb, bos, W, dataclasses.replace(TEXT, theta=1000.0), n_layers=2)
+    assert not np.allclose(x.numpy()[g["rows"]], g["out_rows"], rtol=1e-3, atol=1e-3)
