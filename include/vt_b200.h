@@ -175,6 +175,23 @@ int vt_gated_gelu_mul(cudaStream_t stream, const uint16_t* G, long long ldg, uin
  * Replaces: the ViT MLP's nn.GELU() (the gelu_pan epilogue, tapnext/npu/pack8.py:246-250 gelu_erf_ref). */
 int vt_gelu_erf(cudaStream_t stream, uint16_t* x, long long ld, int R, int N);
 
+/* Rotary embedding and KV-cache write for n new tokens at positions pos0 .. pos0+n-1 of H heads x 64:
+ * qkv bf16 [n][ld] = q | k | v (head-major, ld >= 3*H*64); the first 32 dims of each q / k head rotate as
+ * pairs (x_i, x_(16+i)) -> (x_i cos - x_(16+i) sin, x_i sin + x_(16+i) cos) at dims 2i, 2i+1 with the
+ * angle tables cos_t / sin_t fp32 [ctx][16]; q -> q bf16 [H][n][64], k / v -> kc / vc bf16 [H][ctx][64].
+ * Replaces: the rope + cache write of FastMD2._text_layers (moondream/gpu/md2fast.py:162-167, 186-191), the
+ * unfused form of the reference's rope_cache. */
+int vt_rope_qkv(cudaStream_t stream, const uint16_t* qkv, long long ld, int n, int H, int pos0, const float* cos_t,
+                const float* sin_t, uint16_t* q, uint16_t* kc, uint16_t* vc, int ctx);
+
+/* Causal attention of n new tokens over a KV cache: token i (position pos0 + i) attends to cache positions
+ * 0 .. pos0 + i (q bf16 [H][n][64], kc / vc bf16 [H][ctx][64], ctx <= 2048), softmax(scale q k^T) v in fp32;
+ * out bf16 [n][ldo], head h at columns h*64 .. h*64+63.
+ * Replaces: the masked scaled_dot_product_attention of the question prefill, md2fast.py:192-193 with the
+ * query mask of md2fast.py:132-136. */
+int vt_attn_causal(cudaStream_t stream, const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int n, int H,
+                   int pos0, int ctx, float scale, uint16_t* out, long long ldo);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,8 @@ SIGNATURES = {
     "vt_ssm_step": (I, [P, P, P, LL, P, P, P, LL, P, LL, P, P, P, P, P, P, P, P, LL, I, I, I]),
     "vt_gated_gelu_mul": (I, [P, P, LL, P, LL, I, I]),
     "vt_gelu_erf": (I, [P, P, LL, I, I]),
+    "vt_rope_qkv": (I, [P, P, LL, I, I, I, P, P, P, P, P, I]),
+    "vt_attn_causal": (I, [P, P, P, P, I, I, I, I, F, P, LL]),
 }
 
 

@@ -7,3 +7,4 @@
 #include "attn_noalloc.cu"
 #include "elementwise.cu"
 #include "ssm.cu"
+#include "text.cu"

@@ -277,3 +277,24 @@ def gelu_erf(x):
     rc = lib().vt_gelu_erf(_stream(), x.data_ptr(), x.stride(0), R, N)
     check(rc, "vt_gelu_erf")
     return x
+
+
+def rope_qkv(qkv, pos0, cos_t, sin_t, q, kc, vc):
+    """vt_rope_qkv: qkv [n, 3*H*64] bf16 -> q [H, n, 64]; k, v into the caches kc / vc [H, ctx, 64]."""
+    n = qkv.shape[0]
+    H, ctx = kc.shape[0], kc.shape[1]
+    rc = lib().vt_rope_qkv(_stream(), qkv.data_ptr(), qkv.stride(0), n, H, int(pos0), cos_t.data_ptr(), sin_t.data_ptr(),
+                           q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ctx)
+    check(rc, "vt_rope_qkv")
+    return q
+
+
+def attn_causal(q, kc, vc, pos0, out, scale=None):
+    """vt_attn_causal: q [H, n, 64] at positions pos0 .. over the caches -> out [n, H*64] bf16."""
+    H, n, hd = q.shape
+    ctx = kc.shape[1]
+    s = float(hd ** -0.5 if scale is None else scale)
+    rc = lib().vt_attn_causal(_stream(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), n, H, int(pos0), ctx, s,
+                              out.data_ptr(), out.stride(0))
+    check(rc, "vt_attn_causal")
+    return out

@@ -1,0 +1,100 @@
+"""The moondream2 text decoder that consumes the tower's features, on B200: FastMD2's image prefill and question
+prefill (moondream/gpu/md2fast.py:169-212) with the tower's kernels plus the rotary / KV-cache and causal
+attention kernels of csrc/text.cu.
+
+Per layer (md2fast.py:169-199, the parallel block):
+    h = LN(x)                                   vt_layernorm, bf16
+    qkv = h Wqkv^T + b                          vt_gemm (N = 3 x 2048)
+    rope(q, k), cache k / v                     vt_rope_qkv
+    a = attention                               prefix: tcgen05 attention over its 730 keys (no mask, as
+                                                md2fast.py:182-183); question: vt_attn_causal over the cache
+    x += a Wproj^T + b                          vt_gemm, fp32 residual epilogue
+    x += gelu_tanh(h W1^T + b1) W2^T + b2       vt_gemm (GELU epilogue), vt_gemm + residual
+The yes / no logits are LN(x[last]) Wyn^T + byn (md2fast.py:210-212).  The reference runs these GEMMs as int8
+W8A8 (hgemm.HI8Lin); here they are the bf16 tcgen05 GEMMs of the tower.  The KV caches ([layers][H][762][64]
+bf16) live on the device, owned by this object: encode() fills positions 0 .. 729, query() 730 .. 761.
+"""
+import torch
+
+from .config import TEXT, TextConfig
+from . import ops
+from .ops import BF16
+from .tower import _dev_mat, _dev_vec
+
+F32 = torch.float32
+
+
+def rope_tables(cfg: TextConfig, device):
+    """cos, sin fp32 [ctx, rot / 2]: angle pos * theta^(-2i / rot), evaluated in float64."""
+    inv = cfg.theta ** (-torch.arange(0, cfg.rot, 2, dtype=torch.float64) / cfg.rot)
+    ang = torch.arange(cfg.ctx, dtype=torch.float64)[:, None] * inv[None]
+    return torch.cos(ang).float().contiguous().to(device), torch.sin(ang).float().contiguous().to(device)
+
+
+class TextDecoder:
+    def __init__(self, weights, cfg: TextConfig = TEXT, device="cuda"):
+        self.cfg = cfg
+        dev = self.dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = self.dev = torch.device("cuda", torch.cuda.current_device())
+        W = weights
+        self.n_layers = sum(1 for k in W if k.endswith(".qkv_w"))
+        self.wte = _dev_vec(W["wte"], dev)
+        self.layers = []
+        for i in range(self.n_layers):
+            p = f"tblocks.{i}."
+            b = {"ln_w": _dev_vec(W[p + "ln_w"], dev), "ln_b": _dev_vec(W[p + "ln_b"], dev)}
+            for n in ("qkv", "proj", "fc1", "fc2"):
+                b[n + "_w"], b[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
+                b[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
+            self.layers.append(b)
+        self.post_w, self.post_b = _dev_vec(W["tpost_ln_w"], dev), _dev_vec(W["tpost_ln_b"], dev)
+        self.yn_w, self.yn_ld = _dev_mat(W["lm_small_w"], dev)
+        self.yn_b = _dev_vec(W["lm_small_b"], dev)
+        self.cos, self.sin = rope_tables(cfg, dev)
+        D, H, hd, P = cfg.dim, cfg.heads, cfg.head_dim, cfg.prefix
+        self.x = torch.empty(P, D, dtype=F32, device=dev)
+        self.h = torch.empty(P, D, dtype=BF16, device=dev)
+        self.qkv = torch.empty(P, 3 * D, dtype=BF16, device=dev)
+        self.qflat = torch.empty(H * P * hd, dtype=BF16, device=dev)
+        self.a = torch.empty(P, D, dtype=BF16, device=dev)
+        self.f = torch.empty(P, cfg.ff, dtype=BF16, device=dev)
+        self.kc = torch.zeros(self.n_layers, H, cfg.ctx, hd, dtype=BF16, device=dev)
+        self.vc = torch.zeros(self.n_layers, H, cfg.ctx, hd, dtype=BF16, device=dev)
+        self.hl = torch.empty(1, D, dtype=BF16, device=dev)
+        self.logits = torch.empty(1, 8, dtype=F32, device=dev)
+        self.attn = ops.VtAttn(H, P, hd, dev)
+
+    def _layers(self, n, pos0, full):
+        cfg = self.cfg
+        D, H, hd, Fh = cfg.dim, cfg.heads, cfg.head_dim, cfg.ff
+        x, h, qkv, a, f = self.x[:n], self.h[:n], self.qkv[:n], self.a[:n], self.f[:n]
+        q = self.qflat[:H * n * hd].view(H, n, hd)
+        for i, b in enumerate(self.layers):
+            ops.layer_norm(x, b["ln_w"], b["ln_b"], cfg.eps, out=h)
+            ops.gemm(h, b["qkv_w"], b["qkv_ld"], D, 3 * D, b["qkv_b"], out=qkv)
+            ops.rope_qkv(qkv, pos0, self.cos, self.sin, q, self.kc[i], self.vc[i])
+            if full:  # the prefix: no mask, its own n keys (md2fast.py:182-183)
+                self.attn(q[None], self.kc[i][None, :, pos0:pos0 + n], self.vc[i][None, :, pos0:pos0 + n], out=a[None])
+            else:     # the question: causal over the cache (md2fast.py:184-185 with the query mask)
+                ops.attn_causal(q, self.kc[i], self.vc[i], pos0, a)
+            ops.gemm(a, b["proj_w"], b["proj_ld"], D, D, b["proj_b"], res=x, out=x)
+            ops.gemm(h, b["fc1_w"], b["fc1_ld"], D, Fh, b["fc1_b"], gelu=True, out=f)
+            ops.gemm(f, b["fc2_w"], b["fc2_ld"], Fh, D, b["fc2_b"], res=x, out=x)
+
+    def encode(self, emb, bos):
+        """Image prefill (md2fast.py:201-206): emb [729, D] fp32 / bf16 on the device, bos id."""
+        self.x[0].copy_(self.wte[bos])
+        self.x[1:self.cfg.prefix].copy_(emb)
+        self._layers(self.cfg.prefix, 0, True)
+        return self.x
+
+    def query(self, ids, last):
+        """Question prefill (md2fast.py:208-212): ids [q_len] int64 on the device, `last` the index of the
+        question's last real token -> yes / no logits [n_yn] fp32."""
+        cfg = self.cfg
+        self.x[:cfg.q_len].copy_(self.wte[ids])
+        self._layers(cfg.q_len, cfg.prefix, False)
+        ops.layer_norm(self.x[last:last + 1], self.post_w, self.post_b, cfg.eps, out=self.hl)
+        ops.gemm(self.hl, self.yn_w, self.yn_ld, cfg.dim, cfg.n_yn, self.yn_b, out=self.logits[:, :cfg.n_yn])
+        return self.logits[0, :cfg.n_yn]

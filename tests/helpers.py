@@ -11,6 +11,12 @@ TOK_REL = 2e-2
 TOK_COS = 0.999
 
 
+def rel(a, b):
+    """Relative L2 error ||a - b|| / ||b|| over the whole tensor (both moved to the CPU)."""
+    a, b = torch.as_tensor(a).double().cpu(), torch.as_tensor(b).double().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
 def token_metrics(out, ref):
     """(max over tokens of ||out - ref|| / ||ref||, min over tokens of cos(out, ref)); last dim = features."""
     o = torch.as_tensor(out).double().reshape(-1, out.shape[-1])
