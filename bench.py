@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--no-frame", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     ap.add_argument("--no-fold", action="store_true", help="LayerNorm as separate passes instead of folded into GEMMs")
-    ap.add_argument("--no-tapnext", action="store_true", help="skip the TAPNext per-frame step timings (N=1 only)")
+    ap.add_argument("--no-tapnext", action="store_true",
+                    help="skip the TAPNext per-frame step and text-decoder timings (N=1 only)")
     return ap.parse_args()
 
 
@@ -315,9 +316,10 @@ def run_vt(a):
         torch.cuda.synchronize()
         frame_ms = g0.elapsed_time(g1) / 10
 
-    tap = None
+    tap = txt = None
     if world == 1 and not a.no_tapnext:
         tap = tapnext_frame_ms(dev)
+        txt = text_ms(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -338,6 +340,7 @@ def run_vt(a):
             "ms_per_frame_13crop_throughput": 13 * 1000.0 / value,
             "ms_per_frame_13crop_latency": frame_ms,
             "tapnext_ms_per_frame": tap,
+            "text_decoder": txt,
             "tflops_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12,
             "frac_of_peak_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12 / (sustained * world),
             "roofline": {"kernel": "gemm_bf16_tc_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
@@ -356,6 +359,44 @@ def run_vt(a):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def text_ms(dev, reps=10):
+    """The text decoder after the tower (24 layers, 2048 wide): image prefill of 730 tokens and the 32-token
+    question, mean ms over `reps` (3 warm-ups).  Timing only, so the weights are drawn N(0, 0.02) (LayerNorm
+    gamma 1, beta 0) directly on the device from a seeded generator instead of the host generator the parity
+    tests use."""
+    from strix_halo_maxx_b200.config import TEXT
+    from strix_halo_maxx_b200.weights import text_spec
+    from strix_halo_maxx_b200.text import TextDecoder
+    g = torch.Generator(device=dev).manual_seed(0)
+    W = {}
+    for name, shape, kind in text_spec(TEXT):
+        if kind == "gamma":
+            W[name] = torch.ones(shape, device=dev)
+        elif kind in ("beta", "bias"):
+            W[name] = torch.zeros(shape, device=dev)
+        else:
+            W[name] = torch.randn(shape, device=dev, generator=g) * (1.0 if kind == "normal1" else 0.02)
+    dec = TextDecoder(W, TEXT, device=dev)
+    del W
+    emb = torch.randn(TEXT.prefix - 1, TEXT.dim, device=dev, generator=g)
+    ids = torch.randint(1, TEXT.vocab, (TEXT.q_len,), device=dev, generator=g)
+    out = {}
+    for name, fn in (("prefill_ms", lambda: dec.encode(emb, 0)), ("question_ms", lambda: dec.query(ids, TEXT.q_len - 1))):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = e0.elapsed_time(e1) / reps
+    out["prefill_gemm_tflops"] = TEXT.flops(TEXT.prefix) / (out["prefill_ms"] / 1000) / 1e12
+    del dec
+    return out
 
 
 def tapnext_frame_ms(dev, n_frames=16):

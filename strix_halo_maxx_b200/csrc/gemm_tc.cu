@@ -32,7 +32,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 5;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192) ? 5 : 8;  // BN 64: 24 KB stages
   static constexpr uint32_t TMEM_COLS = 512;  // two BN-column accumulators, rounded to a power of two
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 };
@@ -1035,8 +1035,17 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
     const char* e = getenv("VT_GEMM_2SM");
     return e ? atoi(e) : 1;
   }();
-  if (pair && M > 128) return launch_pair(st, A, lda, W, ldw, M, N, K, ep);
-  return launch_bn<256>(st, A, lda, W, ldw, M, N, K, ep);
+  // Tile shape by how many tiles keep the GPU busy: CTA-pair 256 x 256 tiles when a quarter of the SM pairs
+  // get one (measured: the text prefill's 24-tile proj / fc2 still run faster as pairs); 128 x 256 tiles when
+  // half of the SMs get one; else 128 x 64 tiles (small-M or narrow GEMMs: the text decoder's 32-token
+  // question, the TAPNext 768-wide GEMMs with 15 pair tiles), which spread the weights over 4x more SMs.
+  // VT_GEMM_BN=256 keeps the 128 x 256 tile for those.
+  const int sms = sm_count();
+  const long long tiles_pair = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  const long long tiles_256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
+  if (pair && M > 128 && tiles_pair >= sms / 8) return launch_pair(st, A, lda, W, ldw, M, N, K, ep);
+  if (forced == 256 || tiles_256 >= sms / 2) return launch_bn<256>(st, A, lda, W, ldw, M, N, K, ep);
+  return launch_bn<64>(st, A, lda, W, ldw, M, N, K, ep);
 }
 
 }  // namespace gemm
