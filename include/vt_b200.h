@@ -192,6 +192,17 @@ int vt_rope_qkv(cudaStream_t stream, const uint16_t* qkv, long long ld, int n, i
 int vt_attn_causal(cudaStream_t stream, const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int n, int H,
                    int pos0, int ctx, float scale, uint16_t* out, long long ldo);
 
+/* One pass of the LANCZOS frame squash on 3-channel uint8 images: out[o, j, c] = clip(2^21 + sum_k
+ * in[x0(o) + k, j, c] * w[o][k] >> 22) for o < n_out positions on the resampled axis and j < n_other along
+ * the other, with bounds int32 [n_out][2] = (x0, count) and fixed-point weights int32 [n_out][ksize]
+ * (22 fraction bits); element (a, b, c) of the input at in + a*sa + b*sb + c*sc bytes (a on the resampled
+ * axis), of the output at out + a*oa + b*ob + c*oc.  Two passes (columns of the rows the second needs, then
+ * rows) reproduce Pillow's Image.resize(..., LANCZOS) bit for bit.
+ * Replaces: the host-side img.resize((378, 378), LANCZOS) of FastMD2.set_image (moondream/gpu/md2fast.py:223-228). */
+int vt_resize_pass_u8(cudaStream_t stream, const uint8_t* in, long long sa, long long sb, long long sc, uint8_t* out,
+                      long long oa, long long ob, long long oc, int n_out, int n_other, const int* bounds,
+                      const int* weights, int ksize);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,7 @@ SIGNATURES = {
     "vt_gelu_erf": (I, [P, P, LL, I, I]),
     "vt_rope_qkv": (I, [P, P, LL, I, I, I, P, P, P, P, P, I]),
     "vt_attn_causal": (I, [P, P, P, P, I, I, I, I, F, P, LL]),
+    "vt_resize_pass_u8": (I, [P, P, LL, LL, LL, P, LL, LL, LL, I, I, P, P, I]),
 }
 
 

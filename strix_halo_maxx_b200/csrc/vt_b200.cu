@@ -8,3 +8,4 @@
 #include "elementwise.cu"
 #include "ssm.cu"
 #include "text.cu"
+#include "resize.cu"

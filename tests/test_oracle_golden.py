@@ -124,3 +124,17 @@ def test_text_oracle_detects_a_planted_error():
     TEXT, text_ref, W, emb, bos, ids, last, g = _text_case()
     x, _ = text_ref.encode(emb, bos, W, dataclasses.replace(TEXT, theta=1000.0), n_layers=2)
     assert not np.allclose(x.numpy()[g["rows"]], g["out_rows"], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("h,w", [(480, 640), (375, 500), (1080, 1920), (300, 200), (378, 378)])
+def test_resize_restatement_matches_pillow_bit_for_bit(h, w):
+    """oracle.resize_ref (Pillow's two-pass LANCZOS restated) against Pillow's own Image.resize, the call
+    FastMD2.set_image makes (md2fast.py:223-228)."""
+    from PIL import Image
+    from oracle.resize_ref import resize_lanczos
+    rng = np.random.default_rng(h * w)
+    img = rng.integers(0, 256, (h, w, 3), dtype=np.uint8)
+    yy, xx = np.mgrid[0:h, 0:w]
+    img[..., 1] = ((np.sin(xx / 13.0) + np.cos(yy / 7.0)) * 60 + 128).astype(np.uint8)
+    ref = np.asarray(Image.fromarray(img).resize((378, 378), Image.Resampling.LANCZOS))
+    assert np.array_equal(resize_lanczos(img, 378, 378), ref)
