@@ -316,10 +316,11 @@ def run_vt(a):
         torch.cuda.synchronize()
         frame_ms = g0.elapsed_time(g1) / 10
 
-    tap = txt = None
+    tap = txt = fin = None
     if world == 1 and not a.no_tapnext:
         tap = tapnext_frame_ms(dev)
         txt = text_ms(dev)
+        fin = frame_input_ms(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -341,6 +342,7 @@ def run_vt(a):
             "ms_per_frame_13crop_latency": frame_ms,
             "tapnext_ms_per_frame": tap,
             "text_decoder": txt,
+            "frame_input": fin,
             "tflops_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12,
             "frac_of_peak_whole_step": fl["total"] * a.crops * a.steps / (ms / 1000.0) / 1e12 / (sustained * world),
             "roofline": {"kernel": "gemm_bf16_tc_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
@@ -397,6 +399,34 @@ def text_ms(dev, reps=10):
     out["prefill_gemm_tflops"] = TEXT.flops(TEXT.prefix) / (out["prefill_ms"] / 1000) / 1e12
     del dec
     return out
+
+
+def frame_input_ms(dev, reps=20):
+    """One 640 x 480 JPEG frame to the tower's 378 x 378 uint8 input: nvJPEG decode + the LANCZOS squash
+    kernels on the device, next to Pillow's decode + resize on the host (the reference's FastMD2.set_image
+    path, md2fast.py:223-228), mean ms over `reps`."""
+    import io
+    from PIL import Image
+    from strix_halo_maxx_b200 import imgproc
+    yy, xx = np.mgrid[0:480, 0:640].astype(np.float64)
+    img = np.stack([np.sin(xx / 23.0) * np.cos(yy / 17.0), np.cos(xx / 31.0 + yy / 29.0), np.sin((xx + yy) / 41.0)], -1)
+    buf = io.BytesIO()
+    Image.fromarray((img * 100 + 128).clip(0, 255).astype(np.uint8)).save(buf, format="JPEG", quality=92)
+    data = buf.getvalue()
+    out = torch.empty(378, 378, 3, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        imgproc.load_frame(data, dev, out=out)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        imgproc.load_frame(data, dev, out=out)
+    torch.cuda.synchronize()
+    gpu = (time.perf_counter() - t0) * 1000 / reps
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        Image.open(io.BytesIO(data)).convert("RGB").resize((378, 378), Image.Resampling.LANCZOS)
+    host = (time.perf_counter() - t0) * 1000 / reps
+    return {"gpu_ms": gpu, "pillow_host_ms": host, "jpeg": "640x480 q92", "timing": "host wall clock incl. launch"}
 
 
 def tapnext_frame_ms(dev, n_frames=16):

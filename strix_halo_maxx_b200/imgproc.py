@@ -32,7 +32,8 @@ def _lanczos(x):
 
 
 def resize_tables(in_size, out_size, device):
-    """(bounds int32 [out, 2] = (first input index, count), weights int32 [out, ksize], ksize) on `device`."""
+    """(bounds int32 [out, 2] = (first input index, count), weights int32 [out, ksize], ksize, (first, end) of
+    the input range the whole output reads) with the tables on `device`."""
     key = (in_size, out_size, str(device))
     if key in _TABLES:
         return _TABLES[key]
@@ -53,7 +54,8 @@ def resize_tables(in_size, out_size, device):
             v = ks[k] / tot if tot != 0.0 else ks[k]
             w[o, k] = int(-0.5 + v * one) if v < 0 else int(0.5 + v * one)
         bounds[o] = (x0, n)
-    t = (torch.from_numpy(bounds).to(device), torch.from_numpy(w).to(device), ksize)
+    t = (torch.from_numpy(bounds).to(device), torch.from_numpy(w).to(device), ksize,
+         (int(bounds[0, 0]), int(bounds[-1, 0] + bounds[-1, 1])))
     _TABLES[key] = t
     return t
 
@@ -70,11 +72,8 @@ def resize_lanczos(img, out_h=378, out_w=378, chw=False, out=None):
     H, W = (img.shape[1], img.shape[2]) if chw else (img.shape[0], img.shape[1])
     sc, sy, sx = (img.stride(0), img.stride(1), img.stride(2)) if chw else (img.stride(2), img.stride(0), img.stride(1))
     dev = img.device
-    bh, kh, ksh = resize_tables(W, out_w, dev)
-    bv, kv, ksv = resize_tables(H, out_h, dev)
-    bv_host = bv.cpu()
-    y0 = int(bv_host[0, 0])
-    y1 = int(bv_host[-1, 0] + bv_host[-1, 1])
+    bh, kh, ksh, _ = resize_tables(W, out_w, dev)
+    bv, kv, ksv, (y0, y1) = resize_tables(H, out_h, dev)
     rows = y1 - y0
     if out is None:
         out = torch.empty(out_h, out_w, 3, dtype=torch.uint8, device=dev)
@@ -82,8 +81,10 @@ def resize_lanczos(img, out_h=378, out_w=378, chw=False, out=None):
     # horizontal: resampled axis x, other axis the rows y0 .. y1
     _pass(img.data_ptr() + y0 * sy, sx, sy, sc, tmp, 3, out_w * 3, 1, out_w, rows, bh, kh, ksh)
     # vertical: resampled axis the rows of tmp (bounds shifted by y0), other axis x
-    bvs = bv.clone()
-    bvs[:, 0] -= y0
+    key = (H, out_h, str(dev), "shifted")
+    bvs = _TABLES.get(key)
+    if bvs is None:
+        bvs = _TABLES[key] = bv - torch.tensor([y0, 0], dtype=torch.int32, device=dev)
     _pass(tmp.data_ptr(), out_w * 3, 3, 1, out, out_w * 3, 3, 1, out_h, out_w, bvs, kv, ksv)
     return out
 
