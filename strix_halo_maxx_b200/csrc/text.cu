@@ -38,14 +38,20 @@ __global__ void rope_qkv_kernel(const uint16_t* __restrict__ qkv, long long ld, 
   *reinterpret_cast<uint32_t*>(vc + oc) = *reinterpret_cast<const uint32_t*>(row + (size_t)2 * H * HD + (size_t)h * HD + 2 * i);
 }
 
-// One warp per (head h, new token i): scores over keys 0 .. pos0 + i (lane = key stride 32, full 64-dim dots
-// from the cache rows), softmax in fp32, then P.V with lane = output dims 2*lane, 2*lane+1.  out [n][H*64].
-__global__ void __launch_bounds__(128) attn_causal_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
-                                                          const uint16_t* __restrict__ vc, int n, int H, int pos0, int ctx,
-                                                          float scale, uint16_t* __restrict__ out, long long ldo) {
-  __shared__ float p_s[4][MAX_CTX];
+// One warp per (head h, new token i), two warps per CTA: scores over keys 0 .. pos0 + i with lane = key
+// stride 32 (full 64-dim dots from the cache rows), softmax in fp32, then P.V with the same key split -- each
+// lane a full 64-dim partial output over its keys -- and the 32 partials summed through shared memory.
+// out [n][H*64].
+constexpr int AW = 2;  // warps per CTA
+__global__ void __launch_bounds__(AW * 32) attn_causal_kernel(const uint16_t* __restrict__ q,
+                                                             const uint16_t* __restrict__ kc,
+                                                             const uint16_t* __restrict__ vc, int n, int H, int pos0,
+                                                             int ctx, float scale, uint16_t* __restrict__ out,
+                                                             long long ldo) {
+  __shared__ float p_s[AW][MAX_CTX];
+  __shared__ float red[AW][32][HD + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wi = blockIdx.x * 4 + warp;
+  const int wi = blockIdx.x * AW + warp;
   if (wi >= n * H) return;
   const int h = wi % H, i = wi / H;
   const int nk = pos0 + i + 1;  // keys 0 .. pos0 + i
@@ -82,20 +88,33 @@ __global__ void __launch_bounds__(128) attn_causal_kernel(const uint16_t* __rest
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
+#pragma unroll
+  for (int d = 0; d < HD; d++) qv[d] = 0.f;  // reused as this lane's partial output
   for (int j = lane; j < nk; j += 32) {
     const float p = expf(ps[j] - mx);
-    ps[j] = p;
     sum += p;
+    const uint16_t* vr = vc + ((size_t)h * ctx + j) * HD;
+#pragma unroll
+    for (int d = 0; d < HD; d += 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(vr + d);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        qv[d + 2 * e] = fmaf(p, __uint_as_float(w[e] << 16), qv[d + 2 * e]);
+        qv[d + 2 * e + 1] = fmaf(p, __uint_as_float(w[e] & 0xffff0000u), qv[d + 2 * e + 1]);
+      }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+  for (int d = 0; d < HD; d++) red[warp][lane][d] = qv[d];
   __syncwarp();
   float o0 = 0.f, o1 = 0.f;
-  for (int j = 0; j < nk; j++) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(vc + ((size_t)h * ctx + j) * HD + 2 * lane);
-    const float p = ps[j];
-    o0 = fmaf(p, __uint_as_float(w << 16), o0);
-    o1 = fmaf(p, __uint_as_float(w & 0xffff0000u), o1);
+#pragma unroll 8
+  for (int l = 0; l < 32; l++) {
+    o0 += red[warp][l][2 * lane];
+    o1 += red[warp][l][2 * lane + 1];
   }
   const float inv = 1.f / sum;
   *reinterpret_cast<uint32_t*>(out + (size_t)i * ldo + (size_t)h * HD + 2 * lane) = pack_bf2(o0 * inv, o1 * inv);
@@ -132,7 +151,8 @@ int vt_attn_causal(cudaStream_t st, const uint16_t* q, const uint16_t* kc, const
       !aligned16(vc) || (reinterpret_cast<uintptr_t>(out) & 3))
     return set_error(E_SHAPE, "vt_attn_causal: null pointer, pitch or alignment invalid");
   const int warps = n * H;
-  text::attn_causal_kernel<<<(warps + 3) / 4, 128, 0, st>>>(q, kc, vc, n, H, pos0, ctx, scale, out, ldo);
+  text::attn_causal_kernel<<<(warps + text::AW - 1) / text::AW, text::AW * 32, 0, st>>>(q, kc, vc, n, H, pos0, ctx,
+                                                                                      scale, out, ldo);
   return check_launch("vt_attn_causal");
 }
 
