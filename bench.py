@@ -197,8 +197,10 @@ def run_e2e(a, tower, n_local, mb, pix_host, feats_all, local_out, dev, world, b
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1))
-    e2e = {"value": a.crops * a.steps / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes(),
-           "d2h_bytes_per_step": pipe.d2h_bytes(), "api": "strix_halo_maxx_b200.multigpu.HostPipeline.run"}
+    # bytes of the whole job (every rank copies its own crops in and its features out)
+    e2e = {"value": a.crops * a.steps / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes() * world,
+           "d2h_bytes_per_step": pipe.d2h_bytes() * world, "h2d_bytes_per_step_per_rank": pipe.h2d_bytes(),
+           "api": "strix_halo_maxx_b200.multigpu.HostPipeline.run"}
     # the e2e output must equal the device-resident path
     e2e_ok = bool(torch.equal(out_host[:mb].to(dev), (local_out if world > 1 else feats_all)[:mb]))
 
