@@ -25,7 +25,10 @@ namespace vt {
 namespace attn_tc {
 
 constexpr int BQ = 128, BKV = 64, THREADS = 192;
-constexpr int KVS = 3;  // K and V ring stages: two CTAs of 112 KB share an SM's 228 KB
+#ifndef VT_ATTN_KVS
+#define VT_ATTN_KVS 3
+#endif
+constexpr int KVS = VT_ATTN_KVS;  // K and V ring stages (two CTAs share an SM's 228 KB)
 constexpr uint32_t TMEM_COLS = 256;  // S buffers: columns [0, 64) and [64, 128); O: [128, 128 + DP)
 constexpr long long kDrainCycles = 200000000LL;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -38,8 +41,8 @@ struct Smem {
   static constexpr int Q = 0;
   static constexpr int K = QT;                      // KVS stages
   static constexpr int V = QT + KVS * KT;           // KVS stages
-  static constexpr int P = QT + 2 * KVS * KT;       // 2 buffers
-  static constexpr int BAR = P + 2 * PT;
+  // P lives in tensor memory, over the S buffer it was computed from (bf16 pairs in its first 32 columns)
+  static constexpr int BAR = QT + 2 * KVS * KT;
   static constexpr int BYTES = BAR + 256;
 };
 
@@ -55,9 +58,10 @@ struct Args {
 // Pipeline per CTA (one 128-query tile), key tiles of 64, j = 0 .. nkv-1:
 //   MMA thread:  S_0;  then for each j: S_(j+1) into the other S buffer, wait P_j, O += P_j V_j.
 //                So the tensor core computes S_(j+1) while the softmax warps work on S_j.
-//   softmax:     wait S_j, row max, (rare) O rescale after PV_(j-1) is done, P_j = 2^(s - m) -> smem
-//                buffer j%2, arrive.  The commit after S_j (issued after PV_(j-2)) means PV_(j-2) -- the
-//                last reader of P buffer j%2 -- has finished when S_j is visible.
+//   softmax:     wait S_j, row max, (rare) O rescale after PV_(j-1) is done, P_j = 2^(s - m) as bf16 pairs
+//                into the first 32 columns of S buffer j%2 (tcgen05.st), arrive.  The MMA reads P_j from tensor
+//                memory (A operand); S_(j+2), the next writer of that buffer, is issued after PV_j and the
+//                tensor core runs them in order.
 template <int NC>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   using L = Smem<NC>;
@@ -144,8 +148,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       // ---------------- MMA issuer
       constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV);
       constexpr uint32_t IDESC_O = idesc_bf16(BQ, DP) | (1u << 16);  // B (= V) MN-major
-      const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V),
-                     sp = smem_u32(sm + L::P);
+      const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V);
       auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into S buffer j%2
         const int s = j & 1;
         const int ks = j % KVS;
@@ -167,11 +170,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         if (!mbar_wait(&p_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
         if (!mbar_wait(&v_full[j % KVS], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pb = sp + s * L::PT, vb = sv + (j % KVS) * L::KT;
+        const uint32_t vb = sv + (j % KVS) * L::KT;
 #pragma unroll
-        for (int k = 0; k < BKV / 16; k++)  // 16 keys per MMA: P chunks 2k, 2k+1; V rows 16k..16k+15
-          umma_f16(t_o, sdesc_noswz(pb + k * 4096, 2048, 128), sdesc_noswz(vb + k * 256, 128, 1024), IDESC_O,
-                   (j > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < BKV / 16; k++)  // 16 keys per MMA: P columns 8k .. 8k+7 of S buffer s; V rows 16k ..
+          umma_f16_ts(t_o, tmem + s * BKV + k * 8, sdesc_noswz(vb + k * 256, 128, 1024), IDESC_O,
+                      (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&v_empty[j % KVS]);
         umma_commit(pv_done);
       }
@@ -247,7 +250,6 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       // P = 2^(s * scale_log2 - m) with the scale and shift done two lanes at a time (fma.rn.f32x2); the
       // row sum accumulates in four independent fp32x2 partial sums
       const unsigned long long sl2 = f2_pack(a.scale_log2, a.scale_log2), neg_m = f2_pack(-m_used, -m_used);
-      uint8_t* P = sm + L::P + s * L::PT;
       unsigned long long sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int c = 0; c < 2; c++) {
@@ -265,10 +267,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           sum2[e & 3] = f2_add(sum2[e & 3], f2_pack(p0, p1));
           pk[e] = pack_bf2(p0, p1);
         }
-#pragma unroll
-        for (int q = 0; q < 4; q++)
-          *reinterpret_cast<uint4*>(P + (c * 4 + q) * 2048 + row * 16) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        tmem_st16(t_s + c * 16, pk);  // keys 32c .. 32c+31 as bf16 pairs: S columns 16c .. 16c+15 (S is in r0 / r1)
       }
       {
         const unsigned long long s01 = f2_add(sum2[0], sum2[1]), s23 = f2_add(sum2[2], sum2[3]);
@@ -276,7 +275,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         f2_unpack(f2_add(s01, s23), lo, hi);
         l += lo + hi;
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
     }
