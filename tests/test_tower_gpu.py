@@ -65,6 +65,17 @@ def test_batch_of_crops_is_bit_identical_to_single_crops(tower27):
     assert torch.equal(both[1], one[0])
 
 
+def test_bench_chunk_of_130_crops_is_bit_identical_to_single_crops(tower27):
+    """At the bench's chunk size (130 crops, M = 94,770) the GEMMs run as CTA pairs (proj with the staged TMA
+    epilogue) while a single crop's proj takes 128 x 64 tiles: every row is computed the same way regardless,
+    so crops must come out bit-identical."""
+    pix = torch.from_numpy(wg.crop_pixels(130, CFG, seed=12)).to(DEV)
+    chunk = tower27.forward(pix).clone()
+    for i in (0, 64, 129):
+        one = tower27.forward(pix[i:i + 1]).clone()
+        assert torch.equal(chunk[i], one[0]), i
+
+
 def test_uint8_input_and_eps_1e5_against_reference_golden():
     """The product path against the reference's own FastMD2._vision output (golden, eps 1e-5, 27 blocks)."""
     g = load_golden("vision_u8_27_zero")
