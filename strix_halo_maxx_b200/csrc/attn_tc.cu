@@ -11,11 +11,12 @@
 // QKV GEMM writes this layout from its epilogue; vt_attn_pack builds it from any strided Q/K/V.
 //
 // CTA = one 128-query tile of one (crop, head), 2 CTAs per SM; 6 warps:
-//   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, 2-stage rings);
+//   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, KVS-stage rings);
 //   warp 5 lane 0: tcgen05.mma  S_j = Q K_j^T (M 128, N 64, K DP) into one of two TMEM S buffers, then
-//                  O += P_j V_j (M 128, N DP, K 64; V is an MN-major B operand) into a TMEM accumulator;
-//   warps 0-3: softmax, thread i owns query row i (TMEM lane i): row max, P = 2^(s*scale*log2e - m),
-//              bf16 P written to shared memory in the K-major canonical layout, row sums in fp32.
+//                  O += P_j V_j (M 128, N DP, K 64; P read from TMEM, V an MN-major B operand in shared
+//                  memory) into a TMEM accumulator;
+//   warps 0-3: softmax, thread i owns query row i (TMEM lane i): row max, P = 2^(s*scale*log2e - m) as
+//              bf16 pairs written back over S, row sums in fp32.
 // O is rescaled only when a row max grows by more than 2^8 (P <= 256 otherwise, exact in fp32
 // accumulation), so TMEM round trips of O are rare.  tcgen05 ops of one thread complete in issue order.
 #include "vt_common.cuh"
@@ -199,18 +200,21 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       tmem_ld32(t_s, r0);
       tmem_ld32(t_s + 32, r1);
       tmem_ld_wait();
-      // row max as a tree of three-input maxima (64 -> 22 -> 8 -> 3 -> 1); keys past T only exist in the
-      // last tile
+      // keys past T only exist in the last tile: their scores become -inf in place, so the max below ignores
+      // them and the exponentials give exactly 0 (ex2.approx(-inf) = +0) with no per-key test in the loop
+      if (tail) {
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          if (kbase + e >= T) r0[e] = 0xff800000u;
+          if (kbase + 32 + e >= T) r1[e] = 0xff800000u;
+        }
+      }
+      // row max as a tree of three-input maxima (64 -> 22 -> 8 -> 3 -> 1)
       float t[64];
 #pragma unroll
       for (int e = 0; e < 32; e++) {
         t[e] = __uint_as_float(r0[e]);
         t[32 + e] = __uint_as_float(r1[e]);
-      }
-      if (tail) {
-#pragma unroll
-        for (int e = 0; e < 64; e++)
-          if (kbase + e >= T) t[e] = -INFINITY;
       }
 #pragma unroll
       for (int e = 0; e < 21; e++) t[e] = max3f(t[3 * e], t[3 * e + 1], t[3 * e + 2]);
@@ -259,11 +263,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         for (int e = 0; e < 16; e++) {
           float x0, x1;
           f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), sl2, neg_m), x0, x1);
-          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-          if (tail) {
-            if (kbase + c * 32 + 2 * e >= T) p0 = 0.f;
-            if (kbase + c * 32 + 2 * e + 1 >= T) p1 = 0.f;
-          }
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
           sum2[e & 3] = f2_add(sum2[e & 3], f2_pack(p0, p1));
           pk[e] = pack_bf2(p0, p1);
         }
