@@ -2,7 +2,8 @@
 //   rope_qkv_kernel     rotary embedding of q and k (md2fast.py:162-167) and the KV-cache write of k and v
 //                       (md2fast.py:190-191): the unfused equivalent of the reference's fused rope_cache
 //   attn_causal_kernel  attention of n new tokens at positions pos0 .. pos0+n-1 over the cache with the
-//                       question mask (md2fast.py:132-136: position p sees keys 0 .. p), for the question prefill
+//                       question mask (md2fast.py:132-136: position p sees keys 0 .. p), for the question prefill;
+//                       one CTA per (head, 8 new tokens), so each cache row is read once per group
 #include "vt_common.cuh"
 #include "vt_host.h"
 
@@ -38,86 +39,116 @@ __global__ void rope_qkv_kernel(const uint16_t* __restrict__ qkv, long long ld, 
   *reinterpret_cast<uint32_t*>(vc + oc) = *reinterpret_cast<const uint32_t*>(row + (size_t)2 * H * HD + (size_t)h * HD + 2 * i);
 }
 
-// One warp per (head h, new token i), two warps per CTA: scores over keys 0 .. pos0 + i with lane = key
-// stride 32 (full 64-dim dots from the cache rows), softmax in fp32, then P.V with the same key split -- each
-// lane a full 64-dim partial output over its keys -- and the 32 partials summed through shared memory.
-// out [n][H*64].
-constexpr int AW = 2;  // warps per CTA
-__global__ void __launch_bounds__(AW * 32) attn_causal_kernel(const uint16_t* __restrict__ q,
-                                                             const uint16_t* __restrict__ kc,
-                                                             const uint16_t* __restrict__ vc, int n, int H, int pos0,
-                                                             int ctx, float scale, uint16_t* __restrict__ out,
-                                                             long long ldo) {
-  __shared__ float p_s[AW][MAX_CTX];
-  __shared__ float red[AW][32][HD + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wi = blockIdx.x * AW + warp;
-  if (wi >= n * H) return;
-  const int h = wi % H, i = wi / H;
-  const int nk = pos0 + i + 1;  // keys 0 .. pos0 + i
-  float qv[HD];
-  const uint16_t* qr = q + ((size_t)h * n + i) * HD;
-#pragma unroll
-  for (int d = 0; d < HD; d += 8) {
-    const uint4 u = *reinterpret_cast<const uint4*>(qr + d);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      qv[d + 2 * e] = __uint_as_float(w[e] << 16) * scale;
-      qv[d + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u) * scale;
-    }
+// CTA = (head h, group of QG consecutive new tokens), 8 warps.  The group's tokens share the cache rows, so
+// each K and V row is read once per CTA:
+//   scores   thread = key j (stride CT): its K row (128 B) against the QG scaled q rows (shared memory,
+//            broadcast reads); token i sees keys 0 .. pos0 + i, later keys get -inf;
+//   softmax  warp w = token w of the group: max and exp over its keys in fp32 (expf), row sum;
+//   P.V      thread = (key slice w = warp, dim pair 2*lane): every 8th key, QG x 2 accumulators; the 8
+//            slices are summed through shared memory and scaled by 1 / sum.
+// Dynamic shared memory: qs [QG][64] | ps [QG][nkp] | red [8][QG][64] | lsum [QG] (fp32).
+constexpr int QG = 8, CT = 256;
+__host__ __device__ constexpr int causal_smem_floats(int nkp) { return QG * HD + QG * nkp + 8 * QG * HD + QG; }
+
+__global__ void __launch_bounds__(CT) attn_causal_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
+                                                         const uint16_t* __restrict__ vc, int n, int H, int pos0, int ctx,
+                                                         int nkp, float scale, uint16_t* __restrict__ out,
+                                                         long long ldo) {
+  extern __shared__ float smf[];
+  const int h = blockIdx.x, g0 = blockIdx.y * QG;
+  const int nq = min(QG, n - g0);
+  const int nk = pos0 + g0 + nq;  // keys the group's last token sees
+  float* qs = smf;
+  float* ps = qs + QG * HD;
+  float* red = ps + QG * nkp;
+  float* lsum = red + 8 * QG * HD;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < QG * HD; e += CT) {
+    const int qi = e / HD;
+    qs[e] = qi < nq ? bf2f(q[((size_t)h * n + g0 + qi) * HD + e % HD]) * scale : 0.f;
   }
-  float* ps = p_s[warp];
-  float mx = -INFINITY;
-  for (int j = lane; j < nk; j += 32) {
+  __syncthreads();
+  for (int j = tid; j < nk; j += CT) {
     const uint16_t* kr = kc + ((size_t)h * ctx + j) * HD;
-    float s = 0.f;
+    float sc[QG];
+#pragma unroll
+    for (int qi = 0; qi < QG; qi++) sc[qi] = 0.f;
 #pragma unroll
     for (int d = 0; d < HD; d += 8) {
       const uint4 u = *reinterpret_cast<const uint4*>(kr + d);
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      float kv[8];
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        s = fmaf(qv[d + 2 * e], __uint_as_float(w[e] << 16), s);
-        s = fmaf(qv[d + 2 * e + 1], __uint_as_float(w[e] & 0xffff0000u), s);
+        kv[2 * e] = __uint_as_float(w[e] << 16);
+        kv[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int qi = 0; qi < QG; qi++) {
+        const float4 qa = *reinterpret_cast<const float4*>(qs + qi * HD + d);
+        const float4 qb = *reinterpret_cast<const float4*>(qs + qi * HD + d + 4);
+        float t = sc[qi];
+        t = fmaf(qa.x, kv[0], t);
+        t = fmaf(qa.y, kv[1], t);
+        t = fmaf(qa.z, kv[2], t);
+        t = fmaf(qa.w, kv[3], t);
+        t = fmaf(qb.x, kv[4], t);
+        t = fmaf(qb.y, kv[5], t);
+        t = fmaf(qb.z, kv[6], t);
+        t = fmaf(qb.w, kv[7], t);
+        sc[qi] = t;
       }
     }
-    ps[j] = s;
-    mx = fmaxf(mx, s);
+#pragma unroll
+    for (int qi = 0; qi < QG; qi++) ps[qi * nkp + j] = j <= pos0 + g0 + qi ? sc[qi] : -INFINITY;
   }
+  __syncthreads();
+  {  // softmax of token `warp` of the group (rows past nq see keys up to nk too; they are never stored)
+    float* pr = ps + warp * nkp;
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pr[j]);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < nk; j += 32) {
+      const float p = expf(pr[j] - mx);
+      pr[j] = p;
+      sum += p;
+    }
 #pragma unroll
-  for (int d = 0; d < HD; d++) qv[d] = 0.f;  // reused as this lane's partial output
-  for (int j = lane; j < nk; j += 32) {
-    const float p = expf(ps[j] - mx);
-    sum += p;
-    const uint16_t* vr = vc + ((size_t)h * ctx + j) * HD;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) lsum[warp] = sum;
+  }
+  __syncthreads();
+  float acc[QG][2];
 #pragma unroll
-    for (int d = 0; d < HD; d += 8) {
-      const uint4 u = *reinterpret_cast<const uint4*>(vr + d);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  for (int qi = 0; qi < QG; qi++) acc[qi][0] = acc[qi][1] = 0.f;
+  for (int j = warp; j < nk; j += 8) {
+    const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vc + ((size_t)h * ctx + j) * HD + 2 * lane);
+    const float vx = __uint_as_float(v2 << 16), vy = __uint_as_float(v2 & 0xffff0000u);
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        qv[d + 2 * e] = fmaf(p, __uint_as_float(w[e] << 16), qv[d + 2 * e]);
-        qv[d + 2 * e + 1] = fmaf(p, __uint_as_float(w[e] & 0xffff0000u), qv[d + 2 * e + 1]);
-      }
+    for (int qi = 0; qi < QG; qi++) {
+      const float p = ps[qi * nkp + j];
+      acc[qi][0] = fmaf(p, vx, acc[qi][0]);
+      acc[qi][1] = fmaf(p, vy, acc[qi][1]);
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  for (int qi = 0; qi < QG; qi++)
+    *reinterpret_cast<float2*>(red + (warp * QG + qi) * HD + 2 * lane) = make_float2(acc[qi][0], acc[qi][1]);
+  __syncthreads();
+  if (warp < nq) {  // token g0 + warp, dims 2*lane, 2*lane+1
+    float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-  for (int d = 0; d < HD; d++) red[warp][lane][d] = qv[d];
-  __syncwarp();
-  float o0 = 0.f, o1 = 0.f;
-#pragma unroll 8
-  for (int l = 0; l < 32; l++) {
-    o0 += red[warp][l][2 * lane];
-    o1 += red[warp][l][2 * lane + 1];
+    for (int sl = 0; sl < 8; sl++) {
+      const float2 r = *reinterpret_cast<const float2*>(red + (sl * QG + warp) * HD + 2 * lane);
+      o0 += r.x;
+      o1 += r.y;
+    }
+    const float inv = 1.f / lsum[warp];
+    *reinterpret_cast<uint32_t*>(out + (size_t)(g0 + warp) * ldo + (size_t)h * HD + 2 * lane) =
+        pack_bf2(o0 * inv, o1 * inv);
   }
-  const float inv = 1.f / sum;
-  *reinterpret_cast<uint32_t*>(out + (size_t)i * ldo + (size_t)h * HD + 2 * lane) = pack_bf2(o0 * inv, o1 * inv);
 }
 
 }  // namespace text
@@ -150,9 +181,19 @@ int vt_attn_causal(cudaStream_t st, const uint16_t* q, const uint16_t* kc, const
   if (!q || !kc || !vc || !out || ldo < (long long)H * text::HD || ldo % 2 || !aligned16(q) || !aligned16(kc) ||
       !aligned16(vc) || (reinterpret_cast<uintptr_t>(out) & 3))
     return set_error(E_SHAPE, "vt_attn_causal: null pointer, pitch or alignment invalid");
-  const int warps = n * H;
-  text::attn_causal_kernel<<<(warps + text::AW - 1) / text::AW, text::AW * 32, 0, st>>>(q, kc, vc, n, H, pos0, ctx,
-                                                                                      scale, out, ldo);
+  if (H > 65535 || (n + text::QG - 1) / text::QG > 65535)
+    return set_error(E_SHAPE, "vt_attn_causal: grid too large (H=%d, n=%d)", H, n);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(text::attn_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         text::causal_smem_floats(text::MAX_CTX) * 4);
+    attr_done[dev] = true;
+  }
+  const int nkp = (pos0 + n + 3) & ~3;  // row pitch of the score rows (floats), 16-byte multiple
+  text::attn_causal_kernel<<<dim3(H, (n + text::QG - 1) / text::QG), text::CT, text::causal_smem_floats(nkp) * 4, st>>>(
+      q, kc, vc, n, H, pos0, ctx, nkp, scale, out, ldo);
   return check_launch("vt_attn_causal");
 }
 
