@@ -70,6 +70,23 @@ int vt_gemm_fused(cudaStream_t stream, const uint16_t* A, long long lda, const u
                   long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
                   const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D);
 
+/* Bytes of the workspace vt_gemm_fused_ws takes for an M x N output (0 for an empty one). */
+long long vt_gemm_ws_bytes(int M, int N);
+
+/* vt_gemm_fused with a caller-owned workspace (16-byte aligned, >= vt_gemm_ws_bytes(M, N) bytes, zero-filled
+ * once when allocated; every call leaves it zero-filled again; calls sharing one workspace must not run
+ * concurrently).  With it, a GEMM too small to occupy the GPU with 128 x 64 tiles -- few output columns or
+ * a long K at small M, e.g. the text decoder's 32-token question -- splits K across CTAs: each adds its
+ * fp32 partial sum into the workspace and the last one runs the epilogue on the total.  Results equal
+ * vt_gemm_fused's up to fp32 summation order.  ws = NULL is vt_gemm_fused.
+ * Replaces: the same call sites as vt_gemm_fused (here the question prefill's linears, md2fast.py:192-199);
+ * the reference's HIP GEMM has no split-K variant. */
+int vt_gemm_fused_ws(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M,
+                     int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+                     long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
+                     const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D, void* ws,
+                     long long ws_bytes);
+
 /* Row statistics of x[M, N] fp32 (N % 32 == 0) in the stats_out format of vt_gemm_fused, and optionally the
  * bf16 copy xb: the LayerNorm inputs for a residual stream that no vt_gemm_fused epilogue produced.
  * Replaces: the statistics half of _ln, md2fast.py:43-44. */

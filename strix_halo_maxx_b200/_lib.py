@@ -21,6 +21,8 @@ SIGNATURES = {
     "vt_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, F]),
     "vt_gemm_qkv_tiles": (I, [P, P, LL, P, LL, P, P, I, I, I, I, I]),
     "vt_gemm_fused": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, P, I, I, I]),
+    "vt_gemm_ws_bytes": (LL, [I, I]),
+    "vt_gemm_fused_ws": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, P, I, I, I, P, LL]),
     "vt_rowstats": (I, [P, P, LL, P, LL, P, I, I]),
     "vt_row_moments": (I, [P, P, I, I, F, P]),
     "vt_attn_tiles_bytes": (LL, [I, I, I, I]),

@@ -42,15 +42,21 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
   if (row >= M) return;
   const int nv = N / 4;
   float4 v[MAXV];
+  // the whole row is loaded before any arithmetic (the input-type test outside the loop), so all of a
+  // lane's loads are in flight together
+  if (in_bf16) {
+#pragma unroll
+    for (int i = 0; i < MAXV; i++)
+      if (i * 32 + lane < nv) v[i] = load4(x, row * ldx + 4LL * (i * 32 + lane), 1);
+  } else {
+#pragma unroll
+    for (int i = 0; i < MAXV; i++)
+      if (i * 32 + lane < nv) v[i] = load4(x, row * ldx + 4LL * (i * 32 + lane), 0);
+  }
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < MAXV; i++) {
-    const int c = (i * 32 + lane);
-    if (c < nv) {
-      v[i] = load4(x, row * ldx + 4LL * c, in_bf16);
-      s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    }
-  }
+  for (int i = 0; i < MAXV; i++)
+    if (i * 32 + lane < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   const float mean = RMS ? 0.f : warp_sum(s) / (float)N;
   float q = 0.f;
 #pragma unroll
@@ -62,19 +68,27 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
     }
   }
   const float rstd = rsqrtf(warp_sum(q) / (float)N + eps);
+  // all gamma / beta loads before the first store (the compiler may not move a load past a store to y)
 #pragma unroll
   for (int i = 0; i < MAXV; i++) {
     const int c = (i * 32 + lane);
     if (c < nv) {
       const float4 gg = *reinterpret_cast<const float4*>(g + 4 * c);
       const float4 bb = bta ? *reinterpret_cast<const float4*>(bta + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 o;
-      o.x = (v[i].x - mean) * rstd * gg.x + bb.x;
-      o.y = (v[i].y - mean) * rstd * gg.y + bb.y;
-      o.z = (v[i].z - mean) * rstd * gg.z + bb.z;
-      o.w = (v[i].w - mean) * rstd * gg.w + bb.w;
-      store4(y, row * ldy + 4LL * c, o, out_f32);
+      v[i].x = (v[i].x - mean) * rstd * gg.x + bb.x;
+      v[i].y = (v[i].y - mean) * rstd * gg.y + bb.y;
+      v[i].z = (v[i].z - mean) * rstd * gg.z + bb.z;
+      v[i].w = (v[i].w - mean) * rstd * gg.w + bb.w;
     }
+  }
+  if (out_f32) {
+#pragma unroll
+    for (int i = 0; i < MAXV; i++)
+      if (i * 32 + lane < nv) store4(y, row * ldy + 4LL * (i * 32 + lane), v[i], 1);
+  } else {
+#pragma unroll
+    for (int i = 0; i < MAXV; i++)
+      if (i * 32 + lane < nv) store4(y, row * ldy + 4LL * (i * 32 + lane), v[i], 0);
   }
 }
 

@@ -63,7 +63,20 @@ struct Epi {
   // all row-major outputs / the residual are 32-byte aligned with 32-byte multiple pitches: full chunks
   // use 256-bit accesses (set by the launcher)
   int wide;
+  // split-K (128 x 64 tiles only, ksplit > 1; set by the launcher when the caller passes a workspace): the
+  // K range of a tile is cut into ksplit slices computed by different CTAs.  Each adds its fp32 partial
+  // into sk_ws [M][sk_pitch] (red.add) and counts itself in sk_cnt [M][sk_pitch / 32] per 32-column
+  // chunk of a row; the slice that arrives last reads the sum, runs the epilogue above on it and puts the
+  // workspace back to zero for the next call.
+  float* sk_ws;
+  int* sk_cnt;
+  int sk_pitch;
+  int ksplit;
 };
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 
 // 32 consecutive 32-bit words at p: 256-bit accesses (one full 32-byte sector each, p 32-byte aligned) when
 // wide, else 128-bit ones.
@@ -415,6 +428,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int nN = (N + BN - 1) / BN;
   const int ntiles = ((M + BM - 1) / BM) * nN;
   const int nk = (K + BK - 1) / BK;
+  // work unit u = (tile u / ks_n, K slice u % ks_n); slice s covers k-blocks [nk*s/ks_n, nk*(s+1)/ks_n)
+  const int ks_n = ep.ksplit > 1 ? ep.ksplit : 1;
+  const int nunits = ntiles * ks_n;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -446,9 +462,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const int t = u / ks_n, ks = u % ks_n;
         const int mt = t / nN, nt = t % nN;
-        for (int kb = 0; kb < nk; kb++) {
+        const int kb1 = (int)((long long)nk * (ks + 1) / ks_n);
+        for (int kb = (int)((long long)nk * ks / ks_n); kb < kb1; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, ST_GEMM_PRODUCER)) {
             ok = false;
             break;
@@ -484,7 +502,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
+        const int ks = u % ks_n;
+        const int kb0 = (int)((long long)nk * ks / ks_n), kb1 = (int)((long long)nk * (ks + 1) / ks_n);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, ST_GEMM_MMA)) {
@@ -493,7 +513,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nk; kb++) {
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait(&full[stage], phase, abort_flag, ST_GEMM_MMA)) {
             ok = false;
             break;
@@ -503,7 +523,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + A_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
-            umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -524,7 +544,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr int CH = BN / 64;  // 32-column chunks per warp
     const int row = q * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
+      const int t = u / ks_n;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       const int mt = t / nN, nt = t % nN;
@@ -545,7 +566,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tb + (uint32_t)(c * 32), r);
         tmem_ld_wait();
-        if (m < M) epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
+        if (m >= M) continue;
+        if (ks_n > 1) {  // split-K: add this slice's partial; the slice that completes the sum runs the epilogue
+          float* w = ep.sk_ws + (size_t)m * ep.sk_pitch + n0;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(w + e, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                       __uint_as_float(r[e + 3]));
+          __threadfence();
+          int* cnt = ep.sk_cnt + (size_t)m * (ep.sk_pitch / 32) + n0 / 32;
+          if (atomicAdd(cnt, 1) != ks_n - 1) continue;
+          __threadfence();
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(w + e));
+            r[e] = __float_as_uint(v.x);
+            r[e + 1] = __float_as_uint(v.y);
+            r[e + 2] = __float_as_uint(v.z);
+            r[e + 3] = __float_as_uint(v.w);
+            __stcg(reinterpret_cast<float4*>(w + e), make_float4(0.f, 0.f, 0.f, 0.f));
+          }
+          *cnt = 0;
+        }
+        epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -970,9 +1013,30 @@ static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const 
   return check_launch("vt_gemm (CTA pair)");
 }
 
+// Split-K factor for a 128 x 64 tile launch with a workspace: 1 unless the tiles leave two thirds of the
+// SMs idle, else the s in 1..16 that minimises the k-blocks of the busiest CTA, ceil(tiles * s / SMs) *
+// ceil(nk / s), plus 2 k-blocks' worth for the partial-sum pass.  Measured on the text question (M 32):
+// a CTA of this kernel streams about one 8 KB weight block per 0.3 us, so the 32-tile proj / fc2 run
+// 13 -> 10 us and 39 -> 16 us split 4 ways, while the 96- / 128-tile qkv / fc1 got slower split (the
+// atomic partial sums of their wide outputs cost more than the idle third of the SMs).
+static int split_k(long long ntiles, int K) {
+  const int nk = (K + BK - 1) / BK, sms = sm_count();
+  if (ntiles * 3 > sms) return 1;
+  int best_s = 1;
+  long long best = -1;
+  for (int s = 1; s <= 16 && s <= nk; s++) {
+    const long long cost = (ntiles * s + sms - 1) / sms * ((nk + s - 1) / s) + (s > 1 ? 2 : 0);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
 template <int BN>
 static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
-                     int K, const Epi& ep) {
+                     int K, Epi ep) {
   CUtensorMap ta, tb;
   int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
   if (rc) return rc;
@@ -986,8 +1050,10 @@ static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const ui
     attr_done[dev] = true;
   }
   const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
-  const int grid = (int)(ntiles < sm_count() ? ntiles : sm_count());
+  ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K) : 1;
+  const long long units = ntiles * ep.ksplit;
+  if (units > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
+  const int grid = (int)(units < sm_count() ? units : sm_count());
   gemm_bf16_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
   return check_launch("vt_gemm");
 }
@@ -1053,6 +1119,12 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
 
 extern "C" {
 
+int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                     int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+                     long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
+                     const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D, void* ws,
+                     long long ws_bytes);
+
 // C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias, optionally GELU-tanh (after bf16 rounding).
 int vt_gemm_bf16(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
                  const float* bias, uint16_t* C, long long ldc, int M, int N, int K, int gelu) {
@@ -1079,6 +1151,25 @@ int vt_gemm_fused(cudaStream_t st, const uint16_t* A, long long lda, const uint1
                   int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
                   long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
                   const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D) {
+  return vt_gemm_fused_ws(st, A, lda, W, ldw, M, N, K, bias, out, ldo, out_f32, gelu, res, ldr, res_period, res_bf16,
+                          out2, ldo2, stats_out, ln_moments, ln_c, tiles_T, tiles_H, tiles_D, nullptr, 0);
+}
+
+// Workspace of vt_gemm_fused_ws for an M x N output: fp32 partial sums [M][P] and int arrival counters
+// [M][P/32], P = N rounded up to 32.
+long long vt_gemm_ws_bytes(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  const long long p = ((long long)N + 31) / 32 * 32;
+  return (long long)M * p * 4 + (long long)M * (p / 32) * 4;
+}
+
+// vt_gemm_fused with a zero-filled workspace (ws_bytes >= vt_gemm_ws_bytes(M, N)) that lets the small-tile
+// path split K across CTAs; every call leaves the workspace zero-filled again.  ws may be null.
+int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
+                     int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
+                     long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
+                     const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D, void* ws,
+                     long long ws_bytes) {
   using namespace vt;
   if (tiles_T > 0) {
     if (tiles_H <= 0 || tiles_D <= 0 || tiles_D % 8 || tiles_D > 80 || M % tiles_T || N != 3 * tiles_H * tiles_D ||
@@ -1089,6 +1180,15 @@ int vt_gemm_fused(cudaStream_t st, const uint16_t* A, long long lda, const uint1
                    tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
                    reinterpret_cast<const float2*>(ln_moments), ln_c, 0};
+  if (ws && M > 0 && N > 0) {
+    if (!aligned16(ws) || ws_bytes < vt_gemm_ws_bytes(M, N))
+      return set_error(E_SHAPE, "vt_gemm_fused_ws: workspace of %lld bytes (needs %lld, 16-byte aligned)", ws_bytes,
+                       vt_gemm_ws_bytes(M, N));
+    const int p = (N + 31) / 32 * 32;
+    ep.sk_ws = static_cast<float*>(ws);
+    ep.sk_cnt = reinterpret_cast<int*>(static_cast<char*>(ws) + (size_t)M * p * 4);
+    ep.sk_pitch = p;
+  }
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
 }
 

@@ -123,14 +123,25 @@ __global__ void __launch_bounds__(CT) attn_causal_kernel(const uint16_t* __restr
   float acc[QG][2];
 #pragma unroll
   for (int qi = 0; qi < QG; qi++) acc[qi][0] = acc[qi][1] = 0.f;
-  for (int j = warp; j < nk; j += 8) {
-    const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vc + ((size_t)h * ctx + j) * HD + 2 * lane);
-    const float vx = __uint_as_float(v2 << 16), vy = __uint_as_float(v2 & 0xffff0000u);
+  // 8 of this slice's keys per round: their V loads are issued together, then consumed
+  for (int j0 = warp; j0 < nk; j0 += 64) {
+    uint32_t v2[8];
 #pragma unroll
-    for (int qi = 0; qi < QG; qi++) {
-      const float p = ps[qi * nkp + j];
-      acc[qi][0] = fmaf(p, vx, acc[qi][0]);
-      acc[qi][1] = fmaf(p, vy, acc[qi][1]);
+    for (int u = 0; u < 8; u++) {
+      const int j = j0 + 8 * u;
+      v2[u] = j < nk ? *reinterpret_cast<const uint32_t*>(vc + ((size_t)h * ctx + j) * HD + 2 * lane) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int j = j0 + 8 * u;
+      if (j >= nk) break;
+      const float vx = __uint_as_float(v2[u] << 16), vy = __uint_as_float(v2[u] & 0xffff0000u);
+#pragma unroll
+      for (int qi = 0; qi < QG; qi++) {
+        const float p = ps[qi * nkp + j];
+        acc[qi][0] = fmaf(p, vx, acc[qi][0]);
+        acc[qi][1] = fmaf(p, vy, acc[qi][1]);
+      }
     }
   }
 #pragma unroll

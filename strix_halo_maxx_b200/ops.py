@@ -48,24 +48,30 @@ def as_gemm_operand(x2):
 
 
 def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=None, out_f32=False, out2=None,
-         stats_out=None, ln=None, tiles=None):
+         stats_out=None, ln=None, tiles=None, ws=None):
     """out[M, N] = x2 . w^T + bias (+ GELU) (+ res), see vt_gemm_fused in include/vt_b200.h.
     stats_out: [M, N/32, 2] fp32 row-chunk statistics of the (fp32) output; ln: (moments [M, 2], c) of a
-    LayerNorm folded into this GEMM; tiles: (T, H, D) to scatter into the attention-tile buffer `out`."""
+    LayerNorm folded into this GEMM; tiles: (T, H, D) to scatter into the attention-tile buffer `out`;
+    ws: a zero-filled workspace (gemm_workspace) that lets small GEMMs split K (vt_gemm_fused_ws)."""
     M = x2.shape[0]
     if out is None:
         out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :N]
     ln_mom, ln_c = ln if ln is not None else (None, None)
     tT, tH, tD = tiles if tiles is not None else (0, 0, 0)
-    rc = lib().vt_gemm_fused(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
-                             out.data_ptr(), out.stride(0) if tiles is None else 0,
-                             int(tiles is None and out.dtype == torch.float32), int(gelu), _ptr(res),
-                             0 if res is None else res.stride(0), int(res_period),
-                             int(res is not None and res.dtype == BF16), _ptr(out2),
-                             0 if out2 is None else out2.stride(0), _ptr(stats_out), _ptr(ln_mom), _ptr(ln_c),
-                             tT, tH, tD)
-    check(rc, "vt_gemm_fused")
+    rc = lib().vt_gemm_fused_ws(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
+                                out.data_ptr(), out.stride(0) if tiles is None else 0,
+                                int(tiles is None and out.dtype == torch.float32), int(gelu), _ptr(res),
+                                0 if res is None else res.stride(0), int(res_period),
+                                int(res is not None and res.dtype == BF16), _ptr(out2),
+                                0 if out2 is None else out2.stride(0), _ptr(stats_out), _ptr(ln_mom), _ptr(ln_c),
+                                tT, tH, tD, _ptr(ws), 0 if ws is None else ws.numel() * ws.element_size())
+    check(rc, "vt_gemm_fused_ws")
     return out
+
+
+def gemm_workspace(M, N, device):
+    """Zero-filled split-K workspace for GEMMs with outputs up to M x N (vt_gemm_ws_bytes)."""
+    return torch.zeros(max(lib().vt_gemm_ws_bytes(M, N), 16), dtype=torch.uint8, device=device)
 
 
 def row_stats(x2, stats, xb=None):

@@ -64,23 +64,26 @@ class TextDecoder:
         self.hl = torch.empty(1, D, dtype=BF16, device=dev)
         self.logits = torch.empty(1, 8, dtype=F32, device=dev)
         self.attn = ops.VtAttn(H, P, hd, dev)
+        # split-K workspace of the question's GEMMs (32 rows; the widest output is fc1's)
+        self.ws = ops.gemm_workspace(cfg.q_len, max(3 * D, cfg.ff), dev)
 
     def _layers(self, n, pos0, full):
         cfg = self.cfg
         D, H, hd, Fh = cfg.dim, cfg.heads, cfg.head_dim, cfg.ff
         x, h, qkv, a, f = self.x[:n], self.h[:n], self.qkv[:n], self.a[:n], self.f[:n]
         q = self.qflat[:H * n * hd].view(H, n, hd)
+        ws = None if full else self.ws  # the question's GEMMs are too small to fill the GPU: split K
         for i, b in enumerate(self.layers):
             ops.layer_norm(x, b["ln_w"], b["ln_b"], cfg.eps, out=h)
-            ops.gemm(h, b["qkv_w"], b["qkv_ld"], D, 3 * D, b["qkv_b"], out=qkv)
+            ops.gemm(h, b["qkv_w"], b["qkv_ld"], D, 3 * D, b["qkv_b"], out=qkv, ws=ws)
             ops.rope_qkv(qkv, pos0, self.cos, self.sin, q, self.kc[i], self.vc[i])
             if full:  # the prefix: no mask, its own n keys (md2fast.py:182-183)
                 self.attn(q[None], self.kc[i][None, :, pos0:pos0 + n], self.vc[i][None, :, pos0:pos0 + n], out=a[None])
             else:     # the question: causal over the cache (md2fast.py:184-185 with the query mask)
                 ops.attn_causal(q, self.kc[i], self.vc[i], pos0, a)
-            ops.gemm(a, b["proj_w"], b["proj_ld"], D, D, b["proj_b"], res=x, out=x)
-            ops.gemm(h, b["fc1_w"], b["fc1_ld"], D, Fh, b["fc1_b"], gelu=True, out=f)
-            ops.gemm(f, b["fc2_w"], b["fc2_ld"], Fh, D, b["fc2_b"], res=x, out=x)
+            ops.gemm(a, b["proj_w"], b["proj_ld"], D, D, b["proj_b"], res=x, out=x, ws=ws)
+            ops.gemm(h, b["fc1_w"], b["fc1_ld"], D, Fh, b["fc1_b"], gelu=True, out=f, ws=ws)
+            ops.gemm(f, b["fc2_w"], b["fc2_ld"], Fh, D, b["fc2_b"], res=x, out=x, ws=ws)
 
     def encode(self, emb, bos):
         """Image prefill (md2fast.py:201-206): emb [729, D] fp32 / bf16 on the device, bos id."""
@@ -96,5 +99,5 @@ class TextDecoder:
         self.x[:cfg.q_len].copy_(self.wte[ids])
         self._layers(cfg.q_len, cfg.prefix, False)
         ops.layer_norm(self.x[last:last + 1], self.post_w, self.post_b, cfg.eps, out=self.hl)
-        ops.gemm(self.hl, self.yn_w, self.yn_ld, cfg.dim, cfg.n_yn, self.yn_b, out=self.logits[:, :cfg.n_yn])
+        ops.gemm(self.hl, self.yn_w, self.yn_ld, cfg.dim, cfg.n_yn, self.yn_b, out=self.logits[:, :cfg.n_yn], ws=self.ws)
         return self.logits[0, :cfg.n_yn]

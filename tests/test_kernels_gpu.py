@@ -162,6 +162,56 @@ def test_gemm_empty_and_errors():
     assert lib().vt_gemm_bf16(0, bad.data_ptr(), 70, w.data_ptr(), 64, None, out.data_ptr(), 16, 8, 16, 64, 0) == -2
 
 
+SPLITK = [(32, 2048, 2048), (32, 8192, 2048), (32, 2048, 6144), (1, 2048, 4), (5, 4304, 1000), (100, 1152, 264)]
+
+
+@pytest.mark.parametrize("M,K,N", SPLITK)
+@pytest.mark.parametrize("epi", ["bf16", "gelu", "res_inplace"])
+def test_gemm_split_k_workspace(M, K, N, epi):
+    """vt_gemm_fused_ws: the small-tile path splits K across CTAs (fp32 partial sums in the workspace, the
+    last slice runs the epilogue); same result as the unsplit GEMM up to summation order, and the workspace
+    is zero-filled again after every call."""
+    x, w, b = _operands(M, K, N, 11)
+    ws = ops.gemm_workspace(M, N, DEV)
+    if epi == "res_inplace":
+        x0 = torch.randn(M, N, device=DEV)
+        NP = (N + 7) // 8 * 8  # fp32 output pitches are multiples of 8 elements
+        y_ws, y = torch.zeros(M, NP, device=DEV)[:, :N], torch.zeros(M, NP, device=DEV)[:, :N]
+        y_ws.copy_(x0)
+        y.copy_(x0)
+        ops.gemm(x, w, K, K, N, b, res=y_ws, out=y_ws, ws=ws)
+        ops.gemm(x, w, K, K, N, b, res=y, out=y)
+        ref = F.linear(x.float(), w.float(), b) + x0
+        assert rel(y_ws, ref) < 1e-4 and rel(y, ref) < 1e-4
+        assert torch.allclose(y_ws, y, rtol=1e-4, atol=1e-4)
+    else:
+        gelu = epi == "gelu"
+        o_ws = ops.gemm(x, w, K, K, N, b, gelu=gelu, ws=ws)
+        o = ops.gemm(x, w, K, K, N, b, gelu=gelu)
+        ref = F.linear(x.float(), w.float(), b)
+        if gelu:
+            ref = F.gelu(ref.to(BF).float(), approximate="tanh")
+        assert rel(o_ws, ref) < 5e-3
+        assert rel(o_ws, o) < 5e-3 and (o_ws.float() - o.float()).abs().max() <= 0.05 * o.float().abs().max()
+    torch.cuda.synchronize()
+    assert int(ws.count_nonzero()) == 0
+
+
+def test_gemm_split_k_workspace_reused_across_shapes_and_too_small():
+    """One workspace sized for the widest output serves GEMMs of other shapes back to back (the text
+    question's qkv / proj / fc1 / fc2), and a workspace below vt_gemm_ws_bytes is an error, not a fault."""
+    ws = ops.gemm_workspace(32, 8192, DEV)
+    for K, N in [(2048, 6144), (2048, 2048), (2048, 8192), (8192, 2048)]:
+        x, w, b = _operands(32, K, N, K + N)
+        out = ops.gemm(x, w, K, K, N, b, ws=ws)
+        assert rel(out, F.linear(x.float(), w.float(), b)) < 5e-3
+    torch.cuda.synchronize()
+    assert int(ws.count_nonzero()) == 0
+    x, w, b = _operands(32, 2048, 2048, 3)
+    with pytest.raises(VtError):
+        ops.gemm(x, w, 2048, 2048, 2048, b, ws=ops.gemm_workspace(8, 2048, DEV))
+
+
 def test_gemm_graph_replay_bit_exact():
     """test_hgemm.py:51-67: a captured launch replays bit-exactly like eager."""
     M, K, N = 729, 1152, 4304
