@@ -433,7 +433,9 @@ def frame_input_ms(dev, reps=20):
 
 def tapnext_frame_ms(dev, n_frames=16):
     """Config 3 (the BASELINE simplification) and the full TAPNext++ block: 12 blocks, 1280 tokens, the
-    state carried over n_frames frames of one video; mean ms per frame (CUDA events, 3 warm-up frames)."""
+    state carried over n_frames frames of one video; mean ms per frame (CUDA events, 4 warm-up frames, so
+    that every CUDA graph the engines replay -- one per history-ring position -- is captured before the
+    timed frames; a video's first frame always runs eagerly)."""
     from strix_halo_maxx_b200.config import TAPNEXT
     from strix_halo_maxx_b200.weights import tapnext_weights, tapnextpp_weights, tapnext_inputs
     from strix_halo_maxx_b200.tapnext import TapNextStep
@@ -443,7 +445,7 @@ def tapnext_frame_ms(dev, n_frames=16):
     out = {}
     for name, cls, wfn in (("config3", TapNextStep, tapnext_weights), ("tapnextpp", TapNextPPStep, tapnextpp_weights)):
         eng = cls(wfn(TAPNEXT, seed=9), TAPNEXT, device=dev)
-        for f in range(3):
+        for f in range(4):
             eng.step(fr[f], qs[f])
         eng.reset()
         torch.cuda.synchronize()

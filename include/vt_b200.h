@@ -74,11 +74,12 @@ int vt_gemm_fused(cudaStream_t stream, const uint16_t* A, long long lda, const u
 long long vt_gemm_ws_bytes(int M, int N);
 
 /* vt_gemm_fused with a caller-owned workspace (16-byte aligned, >= vt_gemm_ws_bytes(M, N) bytes, zero-filled
- * once when allocated; every call leaves it zero-filled again; calls sharing one workspace must not run
- * concurrently).  With it, a GEMM too small to occupy the GPU with 128 x 64 tiles -- few output columns or
- * a long K at small M, e.g. the text decoder's 32-token question -- splits K across CTAs: each adds its
- * fp32 partial sum into the workspace and the last one runs the epilogue on the total.  Results equal
- * vt_gemm_fused's up to fp32 summation order.  ws = NULL is vt_gemm_fused.
+ * once when allocated; one workspace sized for the largest M x N serves calls of every smaller shape, one
+ * at a time).  With it, a GEMM too small to occupy the GPU with 128 x 64 tiles -- few output columns at
+ * small M, e.g. the text decoder's 32-token question -- splits K across CTAs: each stores its fp32 partial
+ * sum in the workspace and the last to finish a row chunk adds them in slice order and runs the epilogue,
+ * so results are deterministic (equal to vt_gemm_fused's up to fp32 summation order).  ws = NULL is
+ * vt_gemm_fused.
  * Replaces: the same call sites as vt_gemm_fused (here the question prefill's linears, md2fast.py:192-199);
  * the reference's HIP GEMM has no split-K variant. */
 int vt_gemm_fused_ws(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M,

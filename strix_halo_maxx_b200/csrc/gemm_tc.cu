@@ -64,19 +64,19 @@ struct Epi {
   // use 256-bit accesses (set by the launcher)
   int wide;
   // split-K (128 x 64 tiles only, ksplit > 1; set by the launcher when the caller passes a workspace): the
-  // K range of a tile is cut into ksplit slices computed by different CTAs.  Each adds its fp32 partial
-  // into sk_ws [M][sk_pitch] (red.add) and counts itself in sk_cnt [M][sk_pitch / 32] per 32-column
-  // chunk of a row; the slice that arrives last reads the sum, runs the epilogue above on it and puts the
-  // workspace back to zero for the next call.
+  // K range of a tile is cut into ksplit slices computed by different CTAs.  Slice s stores its fp32
+  // partial into sk_ws + s * M * sk_pitch ([M][sk_pitch]) and counts itself in sk_cnt [M][sk_pitch / 32]
+  // per 32-column chunk of a row; the slice that arrives last adds the ksplit partials in slice order
+  // (so the result does not depend on which CTA finished first), runs the epilogue above on the sum and
+  // puts the counter back to zero for the next call.
   float* sk_ws;
   int* sk_cnt;
   int sk_pitch;
   int ksplit;
 };
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
+// Split-K slices of one launch (the workspace holds this many partial planes).
+constexpr int kMaxSplit = 16;
 
 // 32 consecutive 32-bit words at p: 256-bit accesses (one full 32-byte sector each, p 32-byte aligned) when
 // wide, else 128-bit ones.
@@ -567,25 +567,34 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(tb + (uint32_t)(c * 32), r);
         tmem_ld_wait();
         if (m >= M) continue;
-        if (ks_n > 1) {  // split-K: add this slice's partial; the slice that completes the sum runs the epilogue
+        if (ks_n > 1) {  // split-K: store this slice's partial; the slice that completes the row chunk sums them
+          const size_t plane = (size_t)M * ep.sk_pitch;
           float* w = ep.sk_ws + (size_t)m * ep.sk_pitch + n0;
+          const int ks = u % ks_n;
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
-            red_add_v4(w + e, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
-                       __uint_as_float(r[e + 3]));
+            __stcg(reinterpret_cast<float4*>(w + ks * plane + e),
+                   make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                               __uint_as_float(r[e + 3])));
           __threadfence();
           int* cnt = ep.sk_cnt + (size_t)m * (ep.sk_pitch / 32) + n0 / 32;
           if (atomicAdd(cnt, 1) != ks_n - 1) continue;
           __threadfence();
+          float acc[32];
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(w + e));
-            r[e] = __float_as_uint(v.x);
-            r[e + 1] = __float_as_uint(v.y);
-            r[e + 2] = __float_as_uint(v.z);
-            r[e + 3] = __float_as_uint(v.w);
-            __stcg(reinterpret_cast<float4*>(w + e), make_float4(0.f, 0.f, 0.f, 0.f));
+          for (int e = 0; e < 32; e++) acc[e] = 0.f;
+          for (int sl = 0; sl < ks_n; sl++) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(w + sl * plane + e));
+              acc[e] += v.x;
+              acc[e + 1] += v.y;
+              acc[e + 2] += v.z;
+              acc[e + 3] += v.w;
+            }
           }
+#pragma unroll
+          for (int e = 0; e < 32; e++) r[e] = __float_as_uint(acc[e]);
           *cnt = 0;
         }
         epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
@@ -1024,7 +1033,7 @@ static int split_k(long long ntiles, int K) {
   if (ntiles * 3 > sms) return 1;
   int best_s = 1;
   long long best = -1;
-  for (int s = 1; s <= 16 && s <= nk; s++) {
+  for (int s = 1; s <= kMaxSplit && s <= nk; s++) {
     const long long cost = (ntiles * s + sms - 1) / sms * ((nk + s - 1) / s) + (s > 1 ? 2 : 0);
     if (best < 0 || cost < best) {
       best = cost;
@@ -1050,7 +1059,7 @@ static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const ui
     attr_done[dev] = true;
   }
   const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K) : 1;
+  ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K) : 1;  // <= kMaxSplit
   const long long units = ntiles * ep.ksplit;
   if (units > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int grid = (int)(units < sm_count() ? units : sm_count());
@@ -1155,16 +1164,18 @@ int vt_gemm_fused(cudaStream_t st, const uint16_t* A, long long lda, const uint1
                           out2, ldo2, stats_out, ln_moments, ln_c, tiles_T, tiles_H, tiles_D, nullptr, 0);
 }
 
-// Workspace of vt_gemm_fused_ws for an M x N output: fp32 partial sums [M][P] and int arrival counters
-// [M][P/32], P = N rounded up to 32.
+// Workspace of vt_gemm_fused_ws for an M x N output: int arrival counters [M][P/32] at its start and up to
+// 16 fp32 partial-sum planes [M][P] at its end, P = N rounded up to 32.  Calls of other shapes sharing a
+// workspace sized for the largest keep the same two ends, so one call's partial sums never land on
+// another's counters (which must read zero when a call starts).
 long long vt_gemm_ws_bytes(int M, int N) {
   if (M <= 0 || N <= 0) return 0;
   const long long p = ((long long)N + 31) / 32 * 32;
-  return (long long)M * p * 4 + (long long)M * (p / 32) * 4;
+  return ((long long)M * (p / 32) * 4 + 15) / 16 * 16 + (long long)vt::gemm::kMaxSplit * M * p * 4;
 }
 
-// vt_gemm_fused with a zero-filled workspace (ws_bytes >= vt_gemm_ws_bytes(M, N)) that lets the small-tile
-// path split K across CTAs; every call leaves the workspace zero-filled again.  ws may be null.
+// vt_gemm_fused with a workspace (ws_bytes >= vt_gemm_ws_bytes(M, N), zero-filled when allocated) that lets
+// the small-tile path split K across CTAs; every call leaves the counters at zero again.  ws may be null.
 int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
                      int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
                      long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,
@@ -1185,8 +1196,9 @@ int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const ui
       return set_error(E_SHAPE, "vt_gemm_fused_ws: workspace of %lld bytes (needs %lld, 16-byte aligned)", ws_bytes,
                        vt_gemm_ws_bytes(M, N));
     const int p = (N + 31) / 32 * 32;
-    ep.sk_ws = static_cast<float*>(ws);
-    ep.sk_cnt = reinterpret_cast<int*>(static_cast<char*>(ws) + (size_t)M * p * 4);
+    const size_t planes = (size_t)gemm::kMaxSplit * M * p * 4;
+    ep.sk_cnt = static_cast<int*>(ws);
+    ep.sk_ws = reinterpret_cast<float*>(static_cast<char*>(ws) + ((size_t)ws_bytes / 16 * 16 - planes));
     ep.sk_pitch = p;
   }
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);

@@ -23,8 +23,11 @@ F32 = torch.float32
 
 
 class TapNextStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda"):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True):
         self.cfg = cfg
+        self.use_graphs = graphs
+        self._graph = None
+        self._frame_in = self._q_in = None
         dev = self.dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
             dev = self.dev = torch.device("cuda", torch.cuda.current_device())
@@ -65,7 +68,26 @@ class TapNextStep:
         self.first = True
 
     def step(self, frame, queries):
-        """frame [3, 256, 256] fp32/bf16 in [-1, 1], queries [256, 768] fp32 (device) -> [1280, 768] bf16."""
+        """frame [3, 256, 256] fp32/bf16 in [-1, 1], queries [256, 768] fp32 (device) -> [1280, 768] bf16.
+        With graphs=True every frame after a video's first replays one CUDA graph of the whole step (captured
+        the first time), after copying frame and queries into static input buffers: same kernels, same
+        buffers, bit-identical results, none of the ~110 launches' host time per frame."""
+        if not self.use_graphs or self.first:
+            self._run(frame, queries, self.first)
+        else:
+            if self._frame_in is None:
+                self._frame_in, self._q_in = torch.empty_like(frame), torch.empty_like(queries)
+            self._frame_in.copy_(frame)
+            self._q_in.copy_(queries)
+            if self._graph is None:
+                self._graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self._graph):
+                    self._run(self._frame_in, self._q_in, False)
+            self._graph.replay()
+        self.first = False
+        return self.out
+
+    def _run(self, frame, queries, first):
         cfg = self.cfg
         T, Wd, NI = cfg.ntok, cfg.width, cfg.n_img_tok
         ops.im2col(frame.reshape(1, *frame.shape[-3:]), cfg.patch, self.a_pe)
@@ -83,7 +105,5 @@ class TapNextStep:
             ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x)
             ops.rms_norm(self.x, blk["rms_w"], cfg.eps, out=self.t)
             ops.gemm(self.t, blk["gate_w"], blk["gate_ld"], Wd, 2 * Wd, blk["gate_b"], out=self.G)
-            ops.rglru(self.G, blk["a_param"], self.t, self.state[i], self.x, cfg.lru_c, self.first)
+            ops.rglru(self.G, blk["a_param"], self.t, self.state[i], self.x, cfg.lru_c, first)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
-        self.first = False
-        return self.out

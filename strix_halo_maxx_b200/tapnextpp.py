@@ -13,6 +13,12 @@ Per block, in the reference's order:
     x  += gelu_erf(LN_2(x) W0^T + b0) W3^T + b3        vt_gemm, vt_gelu_erf, vt_gemm + residual
 and the encoder LayerNorm after the last block.  The recurrent state (h fp32 and the last three xx of every
 block) lives on the device, owned by this object; reset() starts a new video.
+
+A frame is ~200 kernel launches, more host time than the B200 needs to run them, so with graphs=True
+(default) every frame after a video's first replays a CUDA graph of the whole step, one per position of the
+history ring (frame % 3), captured the first time that position comes up; the frame and the queries are
+copied into static input buffers first.  The graphs launch the same kernels on the same buffers as the
+eager step, so the results are bit-identical (tests/test_tapnextpp_gpu.py).
 """
 import torch
 import torch.nn.functional as F
@@ -26,8 +32,11 @@ F32 = torch.float32
 
 
 class TapNextPPStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda"):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True):
         self.cfg = cfg
+        self.use_graphs = graphs
+        self._graphs = {}
+        self._frame_in = self._q_in = None
         dev = self.dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
             dev = self.dev = torch.device("cuda", torch.cuda.current_device())
@@ -79,14 +88,30 @@ class TapNextPPStep:
 
     def step(self, frame, queries):
         """frame [3, 256, 256] in [-1, 1], queries [n_queries, 768] fp32 (device) -> [ntok, 768] bf16."""
+        k = self.frame % 3  # history roles: x_(t-3) = slot k, x_(t-2) = k+1, x_(t-1) = k+2 (mod 3)
+        if not self.use_graphs or self.frame == 0:
+            self._run(frame, queries, k, self.frame == 0)
+        else:
+            if self._frame_in is None:
+                self._frame_in, self._q_in = torch.empty_like(frame), torch.empty_like(queries)
+            self._frame_in.copy_(frame)
+            self._q_in.copy_(queries)
+            g = self._graphs.get(k)
+            if g is None:
+                g = self._graphs[k] = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._run(self._frame_in, self._q_in, k, False)
+            g.replay()
+        self.frame += 1
+        return self.out
+
+    def _run(self, frame, queries, k, first):
         cfg = self.cfg
         T, Wd, NI, Fh = cfg.ntok, cfg.width, cfg.n_img_tok, cfg.ff
         ops.im2col(frame.reshape(1, *frame.shape[-3:]), cfg.patch, self.a_pe)
         ops.gemm(self.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
                  res=self.pos, res_period=NI, out=self.x[:NI])
         self.x[NI:].copy_(queries)
-        k = self.frame % 3  # history roles: x_(t-3) = slot k, x_(t-2) = k+1, x_(t-1) = k+2 (mod 3)
-        first = self.frame == 0
         for i, b in enumerate(self.blocks):
             hist = (self.hist[i, k], self.hist[i, (k + 1) % 3], self.hist[i, (k + 2) % 3])
             # recurrent block (step8.py:474-481)
@@ -111,5 +136,3 @@ class TapNextPPStep:
             ops.gelu_erf(self.f)
             ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
-        self.frame += 1
-        return self.out

@@ -26,3 +26,14 @@ def test_tapnext_stream(n_blocks, n_frames, affine):
         out = eng.step(torch.from_numpy(frames[f]).cuda(), torch.from_numpy(queries[f]).cuda())
         assert_tokens_close(out.float().cpu(), ref, what=f"frame {f}")
     assert device_status(clear=True) == 0
+
+
+def test_tapnext_graph_replay_matches_eager():
+    """Frames after the first replay one captured CUDA graph: bit-identical to launching eagerly."""
+    W = wg.tapnext_weights(CFG, seed=8, n_blocks=3, affine="random")
+    frames, queries = wg.tapnext_inputs(CFG, 5, seed=4)
+    eg, ee = TapNextStep(W, CFG, device="cuda"), TapNextStep(W, CFG, device="cuda", graphs=False)
+    for f in range(5):
+        fr, q = torch.from_numpy(frames[f]).cuda(), torch.from_numpy(queries[f]).cuda()
+        assert torch.equal(eg.step(fr, q), ee.step(fr, q)), f"frame {f}"
+    assert eg._graph is not None

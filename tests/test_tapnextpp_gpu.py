@@ -85,3 +85,19 @@ def test_tapnextpp_stream(n_blocks, n_frames, affine):
         out = eng.step(torch.from_numpy(frames[f]).to(DEV), torch.from_numpy(queries[f]).to(DEV))
         assert_tokens_close(out.float().cpu(), ref, what=f"frame {f}")
     assert device_status(clear=True) == 0
+
+
+def test_tapnextpp_graph_replay_matches_eager():
+    """Frames after the first replay the graph of their history-ring position (three graphs): bit-identical
+    to launching eagerly, across a reset to a new video."""
+    W = wg.tapnextpp_weights(CFG, seed=9, n_blocks=2, affine="random")
+    frames, queries = wg.tapnext_inputs(CFG, 6, seed=4)
+    eg, ee = TapNextPPStep(W, CFG, device=DEV), TapNextPPStep(W, CFG, device=DEV, graphs=False)
+    for f in list(range(5)) + ["reset"] + list(range(3)):
+        if f == "reset":
+            eg.reset()
+            ee.reset()
+            continue
+        fr, q = torch.from_numpy(frames[f]).to(DEV), torch.from_numpy(queries[f]).to(DEV)
+        assert torch.equal(eg.step(fr, q), ee.step(fr, q)), f"frame {f}"
+    assert sorted(eg._graphs) == [0, 1, 2]

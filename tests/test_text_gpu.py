@@ -66,3 +66,20 @@ def test_text_decoder_prefill_and_question(n_layers, affine):
     logits = dec.query(torch.from_numpy(ids).to(DEV), last).float().cpu()
     assert rel(logits, logits_ref) < 3e-2, (logits, logits_ref)
     assert device_status(clear=True) == 0
+
+
+def test_text_question_graph_replay_matches_eager():
+    """Questions after the first replay one captured graph (ids and the last-token index in static device
+    buffers): logits bit-identical to the eager path for different questions."""
+    W = wg.text_weights(TEXT, seed=3, n_layers=2, affine="random")
+    emb, bos, ids, last = wg.text_inputs(TEXT, seed=5)
+    dg, de = TextDecoder(W, TEXT, device=DEV), TextDecoder(W, TEXT, device=DEV, graphs=False)
+    e = torch.from_numpy(emb).to(DEV)
+    dg.encode(e, bos)
+    de.encode(e, bos)
+    g = torch.Generator().manual_seed(1)
+    for r in range(3):
+        q = torch.from_numpy(ids).to(DEV) if r == 0 else torch.randint(1, TEXT.vocab, (TEXT.q_len,), generator=g).to(DEV)
+        lst = last if r == 0 else TEXT.q_len - 1 - 3 * r
+        assert torch.equal(dg.query(q, lst), de.query(q, lst)), f"question {r}"
+    assert dg._qgraph is not None
