@@ -109,7 +109,8 @@ int vt_gemm_qkv_tiles(cudaStream_t stream, const uint16_t* A, long long lda, con
                       const float* bias, uint16_t* tiles, int M, int K, int T, int H, int D);
 
 /* Size in bytes of the attention-tile buffer for B crops x H heads x T tokens of head_dim D:
- * layout [B][q|k|v][H][ceil(T/128)][DP/8][128][8] bf16, DP = 64 (D <= 64) or 80.  0 if unsupported. */
+ * layout [B][q|k|v][H][ceil(T/128)][tile] bf16 with a Q tile [DP/8][128][8] and a K or V tile
+ * [2][DP/8][64][8] (two 64-token halves), DP = 64 (D <= 64) or 80.  0 if unsupported. */
 long long vt_attn_tiles_bytes(int B, int T, int H, int D);
 
 /* Strided Q/K/V (element (b,t,h,d) at X + b*sx_b + t*sx_t + h*sx_h + d) -> attention tiles (zero-filled
@@ -119,8 +120,8 @@ int vt_attn_pack(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, cons
                  int B, int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b,
                  long long sk_t, long long sk_h, long long sv_b, long long sv_t, long long sv_h);
 
-/* tcgen05 flash attention from attention tiles: O[b,t,h,:D] = softmax(Q K^T * scale) V, S and O in TMEM,
- * P through shared memory; O element (b,t,h,d) at O + b*so_b + t*so_t + h*so_h + d (strides multiples of 8).
+/* tcgen05 flash attention from attention tiles: O[b,t,h,:D] = softmax(Q K^T * scale) V, S, P and O in TMEM;
+ * O element (b,t,h,d) at O + b*so_b + t*so_t + h*so_h + d (strides multiples of 8).
  * Replaces: attn_fwd2, moondream/gpu/hip/attn.hip:442 (hattn.Attn.__call__, hattn.py:26-37). */
 int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
                       long long so_b, long long so_t, long long so_h, float scale);

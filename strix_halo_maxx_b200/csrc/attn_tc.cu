@@ -2,13 +2,14 @@
 // reference's attn_fwd2 (moondream/gpu/hip/attn.hip:142-272, 442) and its V^T copy (vtranspose,
 // attn.hip:275-288) behind hattn.Attn (moondream/gpu/hattn.py:17-37).
 //
-// Operand layout ("attention tiles"): for crop b, operand w (0 q, 1 k, 2 v), head h, 128-token tile tt,
-// 8-element d chunk c, row r:   tiles[((((b*3 + w)*H + h)*Tt + tt)*NC + c)*1024 + r*8 + e]
-// with Tt = ceil(T/128), NC = DP/8, DP = 64 or 80 (head_dim padded to the tensor-core K granularity).
-// One 128-token tile of one operand is NC*2 KB contiguous, in exactly the canonical no-swizzle layout
-// tcgen05 reads (8-row x 16-byte core matrices), so it arrives with one cp.async.bulk.  Rows t >= T and
-// lanes d >= D are zero (the buffer is zeroed once at allocation and never written there).  The tower's
-// QKV GEMM writes this layout from its epilogue; vt_attn_pack builds it from any strided Q/K/V.
+// Operand layout ("attention tiles"): for crop b, operand w (0 q, 1 k, 2 v), head h, token t, 8-element d
+// chunk c:  tiles[((b*3 + w)*H + h)*Tt*NC*1024 + attn_tile_off(w, t, c, NC) + e]  (vt_common.cuh), with
+// Tt = ceil(T/128), NC = DP/8, DP = 64 or 80 (head_dim padded to the tensor-core K granularity).  A
+// 128-token Q tile is [c][128][8] and each 64-token half of a K or V tile [c][64][8], NC*2 KB and NC KB
+// contiguous in exactly the canonical no-swizzle layout tcgen05 reads (8-row x 16-byte core matrices), so
+// each arrives with one cp.async.bulk.  Rows t >= T and lanes d >= D are zero (the buffer is zeroed once at
+// allocation and never written there).  The tower's QKV GEMM writes this layout from its epilogue;
+// vt_attn_pack builds it from any strided Q/K/V.
 //
 // CTA = one 128-query tile of one (crop, head), 2 CTAs per SM; 6 warps:
 //   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, KVS-stage rings);
@@ -111,16 +112,16 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
 
   if (warp == 4) {
     if (lane == 0) {
-      // ---------------- bulk loads: Q once (20 KB); per 64-key tile NC pieces of 1 KB for K and for V.
+      // ---------------- bulk loads: Q once (NC * 2 KB); per 64-key tile one NC KB copy each for K and V.
       // The MMA thread needs K_(j+1) (for S_(j+1)) before V_j (for PV_j), and K_(j+1)'s stage frees when
       // S_(j+1-KVS) completes while V_j's frees only when PV_(j-KVS) does: so K is issued one tile ahead
       // of V and never queues behind a V wait.
       bool ok = true;
       int last_k = 0, last_v = -1;  // last key tiles whose K / V copies were issued
       auto load_kv = [&](uint64_t* full, const uint16_t* base, int j, int off) {
-        const uint16_t* src = base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * 64 * 8;
+        const uint16_t* src = base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * NC * 512;
         mbar_arrive_expect_tx(full, L::KT);
-        for (int c = 0; c < NC; c++) bulk_load(sm + off + (j % KVS) * L::KT + c * 1024, src + (size_t)c * 1024, 1024, full);
+        bulk_load(sm + off + (j % KVS) * L::KT, src, L::KT, full);
       };
       mbar_arrive_expect_tx(q_full, L::QT);
       bulk_load(sm + L::Q, q_src, L::QT, q_full);
@@ -333,8 +334,7 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ 
     const uint16_t* src = w == 0 ? q + bb * sq_b + t * sq_t + hh * sq_h
                         : w == 1 ? k + bb * sk_b + t * sk_t + hh * sk_h
                                  : v + bb * sv_b + t * sv_t + hh * sv_h;
-    const size_t dst = ((((size_t)bb * 3 + w) * H + hh) * Tt + t / 128) * ((size_t)NC * 1024) + (size_t)c * 1024 +
-                       (size_t)(t % 128) * 8;
+    const size_t dst = (((size_t)bb * 3 + w) * H + hh) * Tt * ((size_t)NC * 1024) + attn_tile_off(w, t, c, NC);
     *reinterpret_cast<uint4*>(tiles + dst) = *reinterpret_cast<const uint4*>(src + c * 8);
   }
 }

@@ -50,7 +50,8 @@ struct Epi {
   uint16_t* out2;     // optional bf16 copy of an fp32 output, [M][ldo2]
   long long ldo2;
   // attention-tile output (pk_T > 0): the bf16 result [M = crops*T][3*H*D] is scattered into the tile
-  // layout vt_attn_tiles_fwd reads, ((((b*3 + w)*H + h)*Tt + t/128)*NC + d/8)*1024 + (t%128)*8 + d%8
+  // layout vt_attn_tiles_fwd reads: element (b, w, h, t, d) at ((b*3 + w)*H + h)*Tt*NC*1024 +
+  // attn_tile_off(w, t, d/8, NC) + d%8
   int pk_T, pk_H, pk_D, pk_NC, pk_Tt;
   // row statistics of an fp32 output (stats_out != null, N % 32 == 0): for every 32-column chunk j of
   // row m, stats_out[m * N/32 + j] = (chunk mean, chunk sum of squared deviations)
@@ -233,8 +234,8 @@ __device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], 
       const int n = n0 + 8 * j;
       if (n < N) {
         const int w = n / HD, rem = n % HD, hh = rem / ep.pk_D, d = rem % ep.pk_D;
-        const size_t off = ((((size_t)crop * 3 + w) * ep.pk_H + hh) * ep.pk_Tt + t / 128) * tile_elems +
-                           (size_t)(d / 8) * 1024 + (size_t)(t % 128) * 8;
+        const size_t off = (((size_t)crop * 3 + w) * ep.pk_H + hh) * ep.pk_Tt * tile_elems +
+                           attn_tile_off(w, t, d / 8, ep.pk_NC);
         *reinterpret_cast<uint4*>(base + off) =
             make_uint4(pack_bf2(v[8 * j], v[8 * j + 1]), pack_bf2(v[8 * j + 2], v[8 * j + 3]),
                        pack_bf2(v[8 * j + 4], v[8 * j + 5]), pack_bf2(v[8 * j + 6], v[8 * j + 7]));
@@ -383,12 +384,11 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
     const int rem = n0 - wsel * HD;
     int hh = rem / ep.pk_D, d = rem - hh * ep.pk_D;
     const size_t tile_elems = (size_t)ep.pk_NC * 1024;
-    const size_t row_off = (size_t)(t >> 7) * tile_elems + (size_t)(t & 127) * 8;
     uint16_t* base = reinterpret_cast<uint16_t*>(ep.out);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const size_t off = (((size_t)crop * 3 + wsel) * ep.pk_H + hh) * (size_t)ep.pk_Tt * tile_elems + row_off +
-                         (size_t)(d >> 3) * 1024;
+      const size_t off = (((size_t)crop * 3 + wsel) * ep.pk_H + hh) * (size_t)ep.pk_Tt * tile_elems +
+                         attn_tile_off(wsel, t, d >> 3, ep.pk_NC);
       *reinterpret_cast<uint4*>(base + off) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
       d += 8;
       if (d >= ep.pk_D) {

@@ -98,6 +98,17 @@ __device__ __forceinline__ unsigned long long gelu_tanh2(unsigned long long x) {
   return f2_fma(h, f2_pack(tanh_approx(u0), tanh_approx(u1)), h);
 }
 
+// Attention-tile layout: offset (bf16 elements) of row t, 8-element d chunk c of operand w (0 q, 1 k, 2 v)
+// within one (crop, operand, head) block of ceil(T/128) tiles of NC * 1024 elements.  A Q tile is
+// [c][128 rows][8]; a K or V tile is two 64-row halves [half][c][64 rows][8], so each 64-key tile the
+// attention kernel streams is one contiguous NC KB copy.  Both are the canonical no-swizzle layout of
+// 8-row x 16-byte core matrices that tcgen05 descriptors address.
+__device__ __forceinline__ size_t attn_tile_off(int w, int t, int c, int NC) {
+  const size_t tile = (size_t)(t >> 7) * NC * 1024;
+  if (w == 0) return tile + (size_t)c * 1024 + (size_t)(t & 127) * 8;
+  return tile + (size_t)((t >> 6) & 1) * NC * 512 + (size_t)c * 512 + (size_t)(t & 63) * 8;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
