@@ -39,7 +39,6 @@ template <int NC>
 struct Smem {
   static constexpr int QT = NC * 2048;  // bytes of the 128-row Q tile
   static constexpr int KT = NC * 1024;  // bytes of a 64-row K or V tile
-  static constexpr int PT = 8 * 2048;   // bytes of a P tile: 8 chunks (64 keys) of 128 rows x 16 B
   static constexpr int Q = 0;
   static constexpr int K = QT;                      // KVS stages
   static constexpr int V = QT + KVS * KT;           // KVS stages
