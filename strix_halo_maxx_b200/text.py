@@ -35,7 +35,7 @@ class TextDecoder:
     def __init__(self, weights, cfg: TextConfig = TEXT, device="cuda", graphs=True):
         self.cfg = cfg
         self.use_graphs = graphs
-        self._qgraph = None
+        self._qgraph = self._egraph = None
         dev = self.dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
             dev = self.dev = torch.device("cuda", torch.cuda.current_device())
@@ -67,6 +67,8 @@ class TextDecoder:
         self.xl = torch.empty(1, D, dtype=F32, device=dev)
         self._ids = torch.zeros(cfg.q_len, dtype=torch.int64, device=dev)
         self._last = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._bos = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._emb = torch.zeros(P - 1, D, dtype=F32, device=dev)
         self.logits = torch.empty(1, 8, dtype=F32, device=dev)
         self.attn = ops.VtAttn(H, P, hd, dev)
         # split-K workspace of the question's GEMMs (32 rows; the widest output is fc1's)
@@ -91,11 +93,26 @@ class TextDecoder:
             ops.gemm(f, b["fc2_w"], b["fc2_ld"], Fh, D, b["fc2_b"], res=x, out=x, ws=ws)
 
     def encode(self, emb, bos):
-        """Image prefill (md2fast.py:201-206): emb [729, D] fp32 / bf16 on the device, bos id."""
-        self.x[0].copy_(self.wte[bos])
-        self.x[1:self.cfg.prefix].copy_(emb)
-        self._layers(self.cfg.prefix, 0, True)
+        """Image prefill (md2fast.py:201-206): emb [729, D] fp32 / bf16 on the device, bos id.  The image
+        features and the bos id go into static device buffers, so with graphs=True every prefill after the
+        first replays one CUDA graph of its ~190 launches (same kernels and buffers as the eager path)."""
+        self._emb.copy_(emb)
+        self._bos.fill_(int(bos))
+        if not self.use_graphs:
+            self._encode()
+        elif self._egraph is None:
+            self._encode()  # first prefill eagerly (one-time library and buffer set-up), then capture
+            self._egraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self._egraph):
+                self._encode()
+        else:
+            self._egraph.replay()
         return self.x
+
+    def _encode(self):
+        torch.index_select(self.wte, 0, self._bos, out=self.x[:1])
+        self.x[1:self.cfg.prefix].copy_(self._emb)
+        self._layers(self.cfg.prefix, 0, True)
 
     def query(self, ids, last):
         """Question prefill (md2fast.py:208-212): ids [q_len] int64 on the device, `last` the index of the

@@ -83,3 +83,19 @@ def test_text_question_graph_replay_matches_eager():
         lst = last if r == 0 else TEXT.q_len - 1 - 3 * r
         assert torch.equal(dg.query(q, lst), de.query(q, lst)), f"question {r}"
     assert dg._qgraph is not None
+
+
+def test_text_prefill_graph_replay_matches_eager():
+    """Image prefills after the first replay one captured graph (features and bos in static buffers):
+    hidden states bit-identical to the eager path, and the question after it too."""
+    W = wg.text_weights(TEXT, seed=3, n_layers=2, affine="random")
+    emb, bos, ids, last = wg.text_inputs(TEXT, seed=5)
+    dg, de = TextDecoder(W, TEXT, device=DEV), TextDecoder(W, TEXT, device=DEV, graphs=False)
+    g = torch.Generator().manual_seed(2)
+    for r in range(3):
+        e = torch.from_numpy(emb).to(DEV) if r == 0 else torch.randn(TEXT.prefix - 1, TEXT.dim, generator=g).to(DEV)
+        b = bos if r == 0 else r
+        assert torch.equal(dg.encode(e, b), de.encode(e, b)), f"prefill {r}"
+        q = torch.from_numpy(ids).to(DEV)
+        assert torch.equal(dg.query(q, last), de.query(q, last)), f"question after prefill {r}"
+    assert dg._egraph is not None
