@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_o = tmem + 128;
+  griddep_wait();  // programmatic dependent launch: the tiles' producer has completed
+  griddep_launch();
 
   if (warp == 4) {
     if (lane == 0) {
@@ -320,6 +322,8 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ 
                                                    int T, int H, int D, int NC, int Tt, long long sq_b, long long sq_t,
                                                    long long sq_h, long long sk_b, long long sk_t, long long sk_h,
                                                    long long sv_b, long long sv_t, long long sv_h) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int dch = D / 8;
   const long long per_tok = 3LL * H * dch;
   const long long total = (long long)B * T * per_tok;
@@ -352,7 +356,7 @@ static int launch_nc(cudaStream_t st, Args a, int B) {
   for (int b0 = 0; b0 < B; b0 += 65535) {
     a.b0 = b0;
     const int nb = (B - b0) < 65535 ? (B - b0) : 65535;
-    attn_tc_kernel<NC><<<dim3(a.Tt, a.H, nb), THREADS, Smem<NC>::BYTES, st>>>(a);
+    launch_k(attn_tc_kernel<NC>, dim3(a.Tt, a.H, nb), THREADS, Smem<NC>::BYTES, st, a);
     int rc = check_launch("vt_attn_tiles_fwd");
     if (rc) return rc;
   }
@@ -391,7 +395,7 @@ int vt_attn_pack(cudaStream_t st, const uint16_t* Q, const uint16_t* K, const ui
   const long long total = (long long)B * T * 3 * H * (D / 8);
   long long g = (total + 255) / 256;
   const long long cap = (long long)sm_count() * 16;
-  attn_tc::pack_kernel<<<(int)(g < cap ? (g < 1 ? 1 : g) : cap), 256, 0, st>>>(Q, K, V, tiles, B, T, H, D, NC, Tt, sq_b,
+  launch_k(attn_tc::pack_kernel, (int)(g < cap ? (g < 1 ? 1 : g) : cap), 256, 0, st, Q, K, V, tiles, B, T, H, D, NC, Tt, sq_b,
                                                                                sq_t, sq_h, sk_b, sk_t, sk_h, sv_b,
                                                                                sv_t, sv_h);
   return check_launch("vt_attn_pack");

@@ -37,6 +37,8 @@ template <int MAXV, bool RMS>
 __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long ldx, int in_bf16, const float* g,
                                                         const float* bta, void* y, long long ldy, int out_f32, int M,
                                                         int N, float eps) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * 8 + warp;
   if (row >= M) return;
@@ -98,6 +100,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
 __global__ void __launch_bounds__(256) rowstats_kernel(const float* __restrict__ x, long long ldx,
                                                        uint16_t* __restrict__ xb, long long ldxb,
                                                        float2* __restrict__ stats, int M, int N) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * 8 + warp;
   if (row >= M) return;
@@ -132,6 +136,8 @@ __global__ void __launch_bounds__(256) rowstats_kernel(const float* __restrict__
 // Chan's parallel formula (equal chunk counts): one thread per row.
 __global__ void __launch_bounds__(256) row_moments_kernel(const float2* __restrict__ stats, int nchunk, int M,
                                                           float eps, float2* __restrict__ out) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   for (long long m = (long long)blockIdx.x * blockDim.x + threadIdx.x; m < M; m += (long long)gridDim.x * blockDim.x) {
     const float2* st = stats + m * nchunk;
     float s = 0.f;
@@ -152,6 +158,8 @@ __global__ void __launch_bounds__(256) row_moments_kernel(const float2* __restri
 // 2: uint8 NHWC 0..255 normalised by (u/255 - 0.5)/0.5 (md2fast.py:148).  One thread per P-pixel run.
 __global__ void __launch_bounds__(256) im2col_kernel(const void* pix, int kind, int B, int C, int S, int P,
                                                      uint16_t* out, long long ldo) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int g = S / P;
   const long long total = (long long)B * g * g * C * P;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -183,6 +191,8 @@ __global__ void __launch_bounds__(256) im2col_kernel(const void* pix, int kind, 
 // Multi-crop combine: out[t, :W] = f[0, t], out[t, W:2W] = mean_{i=1..n-1} f[i, t] (fp32 sum), bf16.
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* f, long long crop_stride, long long ldf,
                                                       int n_crops, int T, int W, uint16_t* out, long long ldo) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int nch = W / 8;
   const long long total = (long long)T * nch;
   const float inv = 1.0f / (float)(n_crops - 1);
@@ -217,6 +227,8 @@ __device__ __forceinline__ float softplusf_(float z) { return z > 20.f ? z : log
 __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param,
                                                     const uint16_t* u, long long ldu, float* state, long long lds,
                                                     float* x, long long ldx, int M, int W, float c, int first) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int nv = W / 4;
   const long long total = (long long)M * nv;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -271,7 +283,7 @@ static int norm_launch(const char* what, cudaStream_t st, const void* x, long lo
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
   const int per_lane = (N / 4 + 31) / 32;
-#define VT_LN(V) layernorm_kernel<V, RMS><<<(unsigned)blocks, 256, 0, st>>>(x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps)
+#define VT_LN(V) launch_k(layernorm_kernel<V, RMS>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps)
   if (per_lane <= 4) VT_LN(4);
   else if (per_lane <= 8) VT_LN(8);
   else if (per_lane <= 12) VT_LN(12);
@@ -310,7 +322,7 @@ int vt_rowstats(cudaStream_t st, const float* x, long long ldx, uint16_t* xb, lo
     return set_error(E_SHAPE, "vt_rowstats: pitches / alignment invalid");
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "vt_rowstats: M too large");
-  ew::rowstats_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, ldx, xb, ldxb, reinterpret_cast<float2*>(stats), M, N);
+  launch_k(ew::rowstats_kernel, (unsigned)blocks, 256, 0, st, x, ldx, xb, ldxb, reinterpret_cast<float2*>(stats), M, N);
   return check_launch("vt_rowstats");
 }
 
@@ -322,7 +334,7 @@ int vt_row_moments(cudaStream_t st, const float* stats, int M, int nchunk, float
   if (M == 0) return OK;
   if (!stats || !moments || (reinterpret_cast<uintptr_t>(stats) & 7) || (reinterpret_cast<uintptr_t>(moments) & 7))
     return set_error(E_SHAPE, "vt_row_moments: pointers must be 8-byte aligned");
-  ew::row_moments_kernel<<<ew::grid_for(M, 256), 256, 0, st>>>(reinterpret_cast<const float2*>(stats), nchunk, M, eps,
+  launch_k(ew::row_moments_kernel, ew::grid_for(M, 256), 256, 0, st, reinterpret_cast<const float2*>(stats), nchunk, M, eps,
                                                                reinterpret_cast<float2*>(moments));
   return check_launch("vt_row_moments");
 }
@@ -336,7 +348,7 @@ int vt_im2col(cudaStream_t st, const void* pix, int kind, int B, int C, int S, i
   if (B == 0) return OK;
   if (!pix || !out || ldo < (long long)C * P * P) return set_error(E_SHAPE, "vt_im2col: bad output");
   const int g = S / P;
-  ew::im2col_kernel<<<ew::grid_for((long long)B * g * g * C * P, 256), 256, 0, st>>>(pix, kind, B, C, S, P, out, ldo);
+  launch_k(ew::im2col_kernel, ew::grid_for((long long)B * g * g * C * P, 256), 256, 0, st, pix, kind, B, C, S, P, out, ldo);
   return check_launch("vt_im2col");
 }
 
@@ -349,7 +361,7 @@ int vt_crop_combine(cudaStream_t st, const uint16_t* f, long long crop_stride, l
   if (T == 0) return OK;
   if (!f || !out || ldf < W || ldo < 2LL * W || ldf % 8 || ldo % 8 || crop_stride % 8 || !aligned16(f) || !aligned16(out))
     return set_error(E_SHAPE, "vt_crop_combine: pitches / alignment invalid");
-  ew::combine_kernel<<<ew::grid_for((long long)T * (W / 8), 256), 256, 0, st>>>(f, crop_stride, ldf, n_crops, T, W, out, ldo);
+  launch_k(ew::combine_kernel, ew::grid_for((long long)T * (W / 8), 256), 256, 0, st, f, crop_stride, ldf, n_crops, T, W, out, ldo);
   return check_launch("vt_crop_combine");
 }
 
@@ -364,7 +376,7 @@ int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_para
       lds % 4 || ldx % 4 || !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(a_param) ||
       (reinterpret_cast<uintptr_t>(u) & 7))
     return set_error(E_SHAPE, "vt_rglru: pitches / alignment invalid");
-  ew::rglru_kernel<<<ew::grid_for((long long)M * (W / 4), 256), 256, 0, st>>>(G, ldg, a_param, u, ldu, state, lds, x,
+  launch_k(ew::rglru_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, a_param, u, ldu, state, lds, x,
                                                                              ldx, M, W, c, first);
   return check_launch("vt_rglru");
 }

@@ -455,6 +455,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // programmatic dependent launch: the operands' producer has completed
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -697,6 +699,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // programmatic dependent launch: the operands' producer has completed
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1011,13 +1015,13 @@ static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const 
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
   if (mode == 2) {
     pair_attr<2>(dev);
-    gemm_bf16_tc_pair_kernel<2><<<2 * clusters, THREADS, PairCfg<2>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+    launch_k(gemm_bf16_tc_pair_kernel<2>, 2 * clusters, THREADS, PairCfg<2>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
   } else if (mode == 1) {
     pair_attr<1>(dev);
-    gemm_bf16_tc_pair_kernel<1><<<2 * clusters, THREADS, PairCfg<1>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+    launch_k(gemm_bf16_tc_pair_kernel<1>, 2 * clusters, THREADS, PairCfg<1>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
   } else {
     pair_attr<0>(dev);
-    gemm_bf16_tc_pair_kernel<0><<<2 * clusters, THREADS, PairCfg<0>::SMEM_BYTES, st>>>(ta, tb, tr, to, to2, M, N, K, ep);
+    launch_k(gemm_bf16_tc_pair_kernel<0>, 2 * clusters, THREADS, PairCfg<0>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
   }
   return check_launch("vt_gemm (CTA pair)");
 }
@@ -1063,7 +1067,7 @@ static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const ui
   const long long units = ntiles * ep.ksplit;
   if (units > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  gemm_bf16_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM_BYTES, st>>>(ta, tb, M, N, K, ep);
+  launch_k(gemm_bf16_tc_kernel<BN>, grid, THREADS, Cfg<BN>::SMEM_BYTES, st, ta, tb, M, N, K, ep);
   return check_launch("vt_gemm");
 }
 

@@ -1,6 +1,7 @@
 // Host helpers of libvt_b200.so: error strings, the device status word, SM count and the
 // cuTensorMapEncodeTiled entry point (fetched through the runtime, so no libcuda link is needed).
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -40,6 +41,14 @@ int sm_count() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("VT_PDL");
+    return e ? atoi(e) != 0 : true;
+  }();
+  return on;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,

@@ -16,6 +16,8 @@ constexpr int PREC = 22;
 __global__ void resize_pass_kernel(const uint8_t* __restrict__ in, long long sa, long long sb, long long sc,
                                    uint8_t* __restrict__ out, long long oa, long long ob, long long oc, int n_out,
                                    int n_other, const int* __restrict__ bounds, const int* __restrict__ w, int ksize) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (t >= (long long)n_out * n_other * 3) return;
   const int c = (int)(t % 3);
@@ -44,7 +46,7 @@ int vt_resize_pass_u8(cudaStream_t st, const uint8_t* in, long long sa, long lon
   if ((long long)n_out * n_other == 0) return OK;
   if (!in || !out || !bounds || !weights) return set_error(E_SHAPE, "vt_resize_pass_u8: null pointer");
   const long long n = (long long)n_out * n_other * 3;
-  rsz::resize_pass_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, sa, sb, sc, out, oa, ob, oc, n_out, n_other,
+  launch_k(rsz::resize_pass_kernel, (unsigned)((n + 255) / 256), 256, 0, st, in, sa, sb, sc, out, oa, ob, oc, n_out, n_other,
                                                                       bounds, weights, ksize);
   return check_launch("vt_resize_pass_u8");
 }

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
     const float* __restrict__ conv_w, const float* __restrict__ conv_b, const float* __restrict__ sp,
     const float* __restrict__ wx, const float* __restrict__ bx, const float* __restrict__ wa,
     const float* __restrict__ ba, uint16_t* __restrict__ z, long long ldz, int R, int W, int first) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   __shared__ float xcs[RB][HD + 1];
   __shared__ float wxs[HD][HD], was[HD][HD];
   const int q = blockIdx.y, r0 = blockIdx.x * RB, tid = threadIdx.x;
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
 // out[r, j] = bf16(bf16(gelu_tanh(G[r, j])) * G[r, F + j]) for j < F: G = [gate | up] (bf16 linear outputs)
 __global__ void gated_gelu_mul_kernel(const uint16_t* __restrict__ G, long long ldg, uint16_t* __restrict__ out,
                                       long long ldo, int R, int F) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int nv = F / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)R * nv;
        i += (long long)gridDim.x * blockDim.x) {
@@ -110,6 +114,8 @@ __global__ void gated_gelu_mul_kernel(const uint16_t* __restrict__ G, long long 
 
 // x = bf16(0.5 x (1 + erf(x / sqrt 2))) in place on a bf16 [R][N] matrix (N % 8 == 0)
 __global__ void gelu_erf_kernel(uint16_t* __restrict__ x, long long ld, int R, int N) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const int nv = N / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)R * nv;
        i += (long long)gridDim.x * blockDim.x) {
@@ -147,7 +153,7 @@ int vt_ssm_step(cudaStream_t st, const uint16_t* yg, const uint16_t* xx, long lo
       !ba || !z || ldi < W || ldh < W || ldhs < W || ldz < W)
     return set_error(E_SHAPE, "vt_ssm_step: null pointer or row pitch below W");
   const dim3 grid((R + ssm::RB - 1) / ssm::RB, W / ssm::HD);
-  ssm::ssm_step_kernel<<<grid, ssm::THREADS, 0, st>>>(yg, xx, ldi, hist_old, hist_mid, hist_new, ldh, h, ldhs, conv_w,
+  launch_k(ssm::ssm_step_kernel, grid, ssm::THREADS, 0, st, yg, xx, ldi, hist_old, hist_mid, hist_new, ldh, h, ldhs, conv_w,
                                                       conv_b, softplus_a, wx, bx, wa, ba, z, ldz, R, W, first);
   return check_launch("vt_ssm_step");
 }
@@ -158,7 +164,7 @@ int vt_gated_gelu_mul(cudaStream_t st, const uint16_t* G, long long ldg, uint16_
   if (R == 0) return OK;
   if (!G || !out || ldg < 2LL * F || ldo < F || ldg % 8 || ldo % 8 || !aligned16(G) || !aligned16(out))
     return set_error(E_SHAPE, "vt_gated_gelu_mul: pitches / alignment invalid");
-  ssm::gated_gelu_mul_kernel<<<ssm::grid_for((long long)R * (F / 8), 256), 256, 0, st>>>(G, ldg, out, ldo, R, F);
+  launch_k(ssm::gated_gelu_mul_kernel, ssm::grid_for((long long)R * (F / 8), 256), 256, 0, st, G, ldg, out, ldo, R, F);
   return check_launch("vt_gated_gelu_mul");
 }
 
@@ -167,7 +173,7 @@ int vt_gelu_erf(cudaStream_t st, uint16_t* x, long long ld, int R, int N) {
   if (R < 0 || N <= 0 || N % 8) return set_error(E_SHAPE, "vt_gelu_erf: N must be a positive multiple of 8");
   if (R == 0) return OK;
   if (!x || ld < N || ld % 8 || !aligned16(x)) return set_error(E_SHAPE, "vt_gelu_erf: pitch / alignment invalid");
-  ssm::gelu_erf_kernel<<<ssm::grid_for((long long)R * (N / 8), 256), 256, 0, st>>>(x, ld, R, N);
+  launch_k(ssm::gelu_erf_kernel, ssm::grid_for((long long)R * (N / 8), 256), 256, 0, st, x, ld, R, N);
   return check_launch("vt_gelu_erf");
 }
 

@@ -18,6 +18,8 @@ constexpr int HD = 64, ROT = 32, MAX_CTX = 2048;  // moondream2 context: 2048 po
 __global__ void rope_qkv_kernel(const uint16_t* __restrict__ qkv, long long ld, int n, int H, int pos0,
                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t, uint16_t* __restrict__ qo,
                                 uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int ctx) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (t >= (long long)n * H * 32) return;
   const int i = (int)(t % 32), h = (int)((t / 32) % H), r = (int)(t / (32LL * H));
@@ -54,6 +56,8 @@ __global__ void __launch_bounds__(CT) attn_causal_kernel(const uint16_t* __restr
                                                          const uint16_t* __restrict__ vc, int n, int H, int pos0, int ctx,
                                                          int nkp, float scale, uint16_t* __restrict__ out,
                                                          long long ldo) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
   extern __shared__ float smf[];
   const int h = blockIdx.x, g0 = blockIdx.y * QG;
   const int nq = min(QG, n - g0);
@@ -178,7 +182,7 @@ int vt_rope_qkv(cudaStream_t st, const uint16_t* qkv, long long ld, int n, int H
       (reinterpret_cast<uintptr_t>(kc) & 3) || (reinterpret_cast<uintptr_t>(vc) & 3))
     return set_error(E_SHAPE, "vt_rope_qkv: null pointer, pitch or alignment invalid");
   const long long threads = (long long)n * H * 32;
-  text::rope_qkv_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(qkv, ld, n, H, pos0, cos_t, sin_t, q, kc,
+  launch_k(text::rope_qkv_kernel, (unsigned)((threads + 255) / 256), 256, 0, st, qkv, ld, n, H, pos0, cos_t, sin_t, q, kc,
                                                                           vc, ctx);
   return check_launch("vt_rope_qkv");
 }
@@ -203,7 +207,7 @@ int vt_attn_causal(cudaStream_t st, const uint16_t* q, const uint16_t* kc, const
     attr_done[dev] = true;
   }
   const int nkp = (pos0 + n + 3) & ~3;  // row pitch of the score rows (floats), 16-byte multiple
-  text::attn_causal_kernel<<<dim3(H, (n + text::QG - 1) / text::QG), text::CT, text::causal_smem_floats(nkp) * 4, st>>>(
+  launch_k(text::attn_causal_kernel, dim3(H, (n + text::QG - 1) / text::QG), text::CT, text::causal_smem_floats(nkp) * 4, st, 
       q, kc, vc, n, H, pos0, ctx, nkp, scale, out, ldo);
   return check_launch("vt_attn_causal");
 }

@@ -109,6 +109,12 @@ __device__ __forceinline__ size_t attn_tile_off(int w, int t, int c, int NC) {
   return tile + (size_t)((t >> 6) & 1) * NC * 512 + (size_t)c * 512 + (size_t)(t & 63) * 8;
 }
 
+// Programmatic dependent launch (see launch_k in vt_host.h): griddep_wait blocks until the previous kernel
+// in the stream has completed and its memory is visible (a no-op when launched without the attribute);
+// griddep_launch lets the next kernel start launching once every CTA of this one has called it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }

@@ -12,6 +12,26 @@ namespace vt {
 enum : int { OK = 0, E_VARIANT = -1, E_SHAPE = -2, E_LAUNCH = -3, E_LAYOUT = -4, E_TMAP = -5 };
 
 int set_error(int code, const char* fmt, ...);   // records the message for vt_last_error_string()
+
+// Programmatic dependent launch: every kernel of the library is launched with the attribute that lets it
+// start (prologue: barriers, TMEM, descriptor prefetch) while the previous kernel in the stream finishes;
+// each kernel executes griddepcontrol.wait (griddep_wait) before its first global-memory access, so no
+// kernel reads or writes memory before its predecessor has completed.  VT_PDL=0 turns the attribute off.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
 int check_launch(const char* what);              // maps cudaGetLastError() to E_LAUNCH
 int sm_count();                                  // SMs of the current device (cached per device)
 bool aligned16(const void* p);
