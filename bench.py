@@ -382,24 +382,31 @@ def text_ms(dev, reps=10):
             W[name] = torch.zeros(shape, device=dev)
         else:
             W[name] = torch.randn(shape, device=dev, generator=g) * (1.0 if kind == "normal1" else 0.02)
-    dec = TextDecoder(W, TEXT, device=dev)
-    del W
     emb = torch.randn(TEXT.prefix - 1, TEXT.dim, device=dev, generator=g)
     ids = torch.randint(1, TEXT.vocab, (TEXT.q_len,), device=dev, generator=g)
-    out = {}
-    for name, fn in (("prefill_ms", lambda: dec.encode(emb, 0)), ("question_ms", lambda: dec.query(ids, TEXT.q_len - 1))):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        out[name] = e0.elapsed_time(e1) / reps
+
+    def timed(dec):
+        res = {}
+        for name, fn in (("prefill_ms", lambda: dec.encode(emb, 0)), ("question_ms", lambda: dec.query(ids, TEXT.q_len - 1))):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = e0.elapsed_time(e1) / reps
+        return res
+
+    # bf16 linears (tlin_cls=HLin), then the W8A8 int8 ones (tlin_cls=HI8Lin, the reference's default)
+    out = timed(TextDecoder(W, TEXT, device=dev))
     out["prefill_gemm_tflops"] = TEXT.flops(TEXT.prefix) / (out["prefill_ms"] / 1000) / 1e12
-    del dec
+    i8 = timed(TextDecoder(W, TEXT, device=dev, int8=True))
+    i8["prefill_gemm_tops"] = TEXT.flops(TEXT.prefix) / (i8["prefill_ms"] / 1000) / 1e12
+    out["int8"] = i8
+    del W
     return out
 
 

@@ -88,6 +88,37 @@ int vt_gemm_fused_ws(cudaStream_t stream, const uint16_t* A, long long lda, cons
                      const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D, void* ws,
                      long long ws_bytes);
 
+/* Per-token int8 quantisation of the activation rows of a W8A8 GEMM: s[m] = max(max_k |x[m,k]|, 1e-5) / 127
+ * and q[m,k] = trunc(x[m,k] / s[m] +- 0.5) (round half away from zero, IEEE fp32 division and addition),
+ * from x bf16 [M, K] (pitch ldx elements, 16-byte aligned) into q int8 (pitch ldq bytes, 8-byte aligned);
+ * K % 8 == 0, K <= 16384.
+ * Replaces: quant_rows, moondream/gpu/hgemm.py:10-16 (its Triton kernel _quant_rows, tgemm.py:81-91), as
+ * HI8Lin.quant (hgemm.py:116-117) and the shared quantisation of the LN output (md2fast.py:174) call it. */
+int vt_quant_rows(cudaStream_t stream, const uint16_t* x, long long ldx, int M, int K, int8_t* q, long long ldq,
+                  float* s);
+
+/* vt_layernorm fused with vt_quant_rows of its bf16 output: the same q[M, N] (pitch ldq bytes, a multiple of
+ * 4) and s[M], without the bf16 round trip through memory; y (bf16, pitch ldy) also receives the LayerNorm
+ * output when not NULL.  N % 4 == 0, N <= 4096.
+ * Replaces: _ln followed by HI8Lin.quant on its output, the shared activation of qkv and fc1
+ * (moondream/gpu/md2fast.py:173-174). */
+int vt_layernorm_quant(cudaStream_t stream, const void* x, long long ldx, int in_bf16, const float* gamma,
+                       const float* beta, int M, int N, float eps, int8_t* q, long long ldq, float* s, uint16_t* y,
+                       long long ldy);
+
+/* W8A8 int8 GEMM on the tensor cores (tcgen05 kind::i8, exact int32 accumulation):
+ *   out[m, n] = ((float)(A[m,:] . W[n,:]) * sa[m]) * sw[n] + bias[n],
+ * GELU-tanh applied to that fp32 value when gelu != 0, then bf16 output (fp32 with out_f32, no GELU), plus
+ * res (fp32, or bf16 with res_bf16; may alias out) when res != NULL.  A [M, K] and W [N, K] signed int8 with
+ * pitches lda / ldw in bytes (multiples of 16, 16-byte aligned bases); sa [M] the activation scales
+ * (vt_quant_rows), sw [N] the per-channel weight scales (16-byte aligned), bias [N] fp32 or NULL.  ws / ws_bytes
+ * as for vt_gemm_fused_ws (the split-K partial sums are int32, so the result does not depend on the split).
+ * Replaces: i8gemm_launch / i8gemm_small_launch, moondream/gpu/hip/i8gemm.hip:480-533 and 555-593 (the
+ * kernel epilogue i8gemm.hip:183-197), as HI8Lin.__call__ runs them (moondream/gpu/hgemm.py:119-137). */
+int vt_gemm_i8(cudaStream_t stream, const int8_t* A, long long lda, const int8_t* W, long long ldw, const float* sa,
+               const float* sw, int M, int N, int K, const float* bias, void* out, long long ldo, int out_f32,
+               int gelu, const void* res, long long ldr, int res_bf16, void* ws, long long ws_bytes);
+
 /* Row statistics of x[M, N] fp32 (N % 32 == 0) in the stats_out format of vt_gemm_fused, and optionally the
  * bf16 copy xb: the LayerNorm inputs for a residual stream that no vt_gemm_fused epilogue produced.
  * Replaces: the statistics half of _ln, md2fast.py:43-44. */

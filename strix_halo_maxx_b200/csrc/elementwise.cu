@@ -33,10 +33,13 @@ __device__ __forceinline__ void store4(void* base, long long idx, float4 v, int 
 // Follows F.layer_norm as md2fast.py:43-44 calls it.
 // RMS = true gives RMSNorm instead: y = x * rsqrt(mean(x^2) + eps) * gamma (+ beta when given).
 constexpr int LN_MAXV = 32;  // float4 per lane, upper bound (N <= 4096)
-template <int MAXV, bool RMS>
+// QUANT = true: the row is also quantised per token for the int8 GEMM (vt_layernorm_quant): y rounded to bf16
+// (as vt_layernorm's bf16 output), s = max(max |y|, 1e-5) / 127, q = trunc(y / s +- 0.5) -- the same numbers
+// vt_quant_rows makes from vt_layernorm's output; y itself is stored only when y != null.
+template <int MAXV, bool RMS, bool QUANT = false>
 __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long ldx, int in_bf16, const float* g,
                                                         const float* bta, void* y, long long ldy, int out_f32, int M,
-                                                        int N, float eps) {
+                                                        int N, float eps, int8_t* qout, long long ldq, float* qs) {
   griddep_wait();  // programmatic dependent launch: the previous kernel has completed
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,6 +85,36 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
       v[i].z = (v[i].z - mean) * rstd * gg.z + bb.z;
       v[i].w = (v[i].w - mean) * rstd * gg.w + bb.w;
     }
+  }
+  if constexpr (QUANT) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+      if (i * 32 + lane < nv) {
+        v[i] = make_float4(bfround(v[i].x), bfround(v[i].y), bfround(v[i].z), bfround(v[i].w));
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(fmaxf(amax, 1e-5f), 127.f);
+    auto q8 = [sc](float xv) -> uint32_t {
+      const float t = __fdiv_rn(xv, sc);
+      int qi = __float2int_rz(__fadd_rn(t, t >= 0.f ? 0.5f : -0.5f));
+      qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+      return (uint32_t)qi & 0xffu;
+    };
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+      const int c = i * 32 + lane;
+      if (c < nv) {
+        *reinterpret_cast<uint32_t*>(qout + row * ldq + 4LL * c) =
+            q8(v[i].x) | (q8(v[i].y) << 8) | (q8(v[i].z) << 16) | (q8(v[i].w) << 24);
+        if (y) store4(y, row * ldy + 4LL * c, v[i], 0);
+      }
+    }
+    if (lane == 0) qs[row] = sc;
+    return;
   }
   if (out_f32) {
 #pragma unroll
@@ -283,13 +316,40 @@ static int norm_launch(const char* what, cudaStream_t st, const void* x, long lo
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
   const int per_lane = (N / 4 + 31) / 32;
-#define VT_LN(V) launch_k(layernorm_kernel<V, RMS>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps)
+#define VT_LN(V)                                                                                                  \
+  launch_k(layernorm_kernel<V, RMS>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, \
+           eps, (int8_t*)nullptr, 0LL, (float*)nullptr)
   if (per_lane <= 4) VT_LN(4);
   else if (per_lane <= 8) VT_LN(8);
   else if (per_lane <= 12) VT_LN(12);
   else if (per_lane <= 16) VT_LN(16);
   else VT_LN(32);
 #undef VT_LN
+  return check_launch(what);
+}
+
+static int ln_quant_launch(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma,
+                           const float* beta, int M, int N, float eps, int8_t* q, long long ldq, float* s, void* y,
+                           long long ldy) {
+  const char* what = "vt_layernorm_quant";
+  if (M < 0 || N < 0) return set_error(E_SHAPE, "%s: negative shape", what);
+  if (M == 0) return OK;
+  if (N == 0 || N % 4 || N > 4 * 32 * LN_MAXV) return set_error(E_SHAPE, "%s: N=%d unsupported", what, N);
+  if (!x || !q || !s || !gamma || !beta) return set_error(E_SHAPE, "%s: null pointer", what);
+  if (ldx < N || ldx % 4 || ldq < N || ldq % 4 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
+      (reinterpret_cast<uintptr_t>(q) & 3) || (y && (ldy < N || ldy % 4 || !aligned16(y))))
+    return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
+  const long long blocks = ((long long)M + 7) / 8;
+  if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
+  const int per_lane = (N / 4 + 31) / 32;
+#define VT_LNQ(V)                                                                                                \
+  launch_k(layernorm_kernel<V, false, true>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, 0, \
+           M, N, eps, q, ldq, s)
+  if (per_lane <= 4) VT_LNQ(4);
+  else if (per_lane <= 8) VT_LNQ(8);
+  else if (per_lane <= 16) VT_LNQ(16);
+  else VT_LNQ(32);
+#undef VT_LNQ
   return check_launch(what);
 }
 }  // namespace ew
@@ -302,6 +362,14 @@ extern "C" {
 int vt_layernorm(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma, const float* beta,
                  void* y, long long ldy, int out_f32, int M, int N, float eps) {
   return vt::ew::norm_launch<false>("vt_layernorm", st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, eps);
+}
+
+// LayerNorm fused with the per-token int8 quantisation of its bf16 output (vt_quant_rows' numbers): q[M, N]
+// int8 (pitch ldq bytes, a multiple of 4), s[M]; y (bf16, pitch ldy) receives the bf16 output when not null.
+int vt_layernorm_quant(cudaStream_t st, const void* x, long long ldx, int in_bf16, const float* gamma,
+                       const float* beta, int M, int N, float eps, int8_t* q, long long ldq, float* s, uint16_t* y,
+                       long long ldy) {
+  return vt::ew::ln_quant_launch(st, x, ldx, in_bf16, gamma, beta, M, N, eps, q, ldq, s, y, ldy);
 }
 
 // y = x * rsqrt(mean(x^2) + eps) * gamma (RMSNorm), same layout rules as vt_layernorm.

@@ -74,6 +74,13 @@ struct Epi {
   int* sk_cnt;
   int sk_pitch;
   int ksplit;
+  // W8A8 int8 operands (the I8 kernel instantiations, vt_gemm_i8): the accumulator is the exact int32 dot
+  // product of the int8 rows, scaled as ((float)acc * i8_sa[m]) * i8_sw[n] before the bias, the order of
+  // the reference's int8 epilogue (moondream/gpu/hip/i8gemm.hip:183-197); gelu = 2 there applies GELU-tanh to
+  // the fp32 value in the sigmoid form (gelu_sigmoid; gelu = 1: tanh.approx on the bf16-rounded value, the
+  // bf16 GEMM's rule)
+  const float* i8_sa;
+  const float* i8_sw;
 };
 
 // Split-K slices of one launch (the workspace holds this many partial planes).
@@ -122,6 +129,11 @@ __device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], 
 #pragma unroll
   for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
   const bool full = (n0 + 32 <= N);
+  if (ep.i8_sw) {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      if (n0 + j < N) v[j] = __fmul_rn(v[j], ep.i8_sw[n0 + j]);
+  }
   if (ep.ln_moments) {
     if (full) {
       const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
@@ -242,9 +254,12 @@ __device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], 
       }
     }
   } else {
-    if (ep.gelu) {
+    if (ep.gelu == 1) {
 #pragma unroll
       for (int j = 0; j < 32; j++) v[j] = gelu_tanh(bfround(v[j]));
+    } else if (ep.gelu == 2) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = gelu_sigmoid(v[j]);
     }
     uint16_t* op = reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0;
     if (full) {
@@ -292,6 +307,15 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
   unsigned long long v[16];
 #pragma unroll
   for (int j = 0; j < 16; j++) v[j] = f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+  if (ep.i8_sw) {  // int8 path: the column scale (the row scale is already in)
+    const float4* s4 = reinterpret_cast<const float4*>(ep.i8_sw + n0);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float4 sw = __ldg(s4 + j);
+      v[2 * j] = f2_mul(v[2 * j], f2_pack(sw.x, sw.y));
+      v[2 * j + 1] = f2_mul(v[2 * j + 1], f2_pack(sw.z, sw.w));
+    }
+  }
   if (ep.ln_moments) {  // rstd * (acc - mean * c) + bias = rstd * acc + (bias - rstd * mean * c)
     const unsigned long long rs = f2_pack(rstd, rstd), nrm = f2_pack(-rstd * mu, -rstd * mu);
     const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
@@ -360,14 +384,23 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
     }
     return;
   }
-  // bf16 outputs: round to bf16 first (GELU is applied to the bf16 linear output)
+  // bf16 outputs: round to bf16 first (GELU is applied to the bf16 linear output), except for the int8
+  // epilogue's GELU on the fp32 value
+  if (ep.gelu == 2) {
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      float g0, g1;
+      f2_unpack(v[j], g0, g1);
+      v[j] = f2_pack(gelu_sigmoid(g0), gelu_sigmoid(g1));
+    }
+  }
 #pragma unroll
   for (int j = 0; j < 16; j++) {
     float x0, x1;
     f2_unpack(v[j], x0, x1);
     w[j] = pack_bf2(x0, x1);
   }
-  if (ep.gelu) {
+  if (ep.gelu == 1) {
 #pragma unroll
     for (int j = 0; j < 16; j++) {
       float g0, g1;
@@ -401,13 +434,21 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
   st_words<16>(reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0, w, ep.wide != 0);
 }
 
+// int8 path: the s32 accumulator words of a chunk become fp32 (float)acc * sa, sa the row's activation scale.
+__device__ __forceinline__ void i8_row_scale(uint32_t (&r)[32], float sa) {
+#pragma unroll
+  for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fmul_rn(__int2float_rn((int)r[j]), sa));
+}
+
 // The same with the residual loaded where it is added.
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int M, int n0, int N, const Epi& ep,
                                                float mu, float rstd) {
   epilogue_chunk_rw<false>(r, r, m, M, n0, N, ep, mu, rstd);
 }
 
-template <int BN>
+// I8: signed int8 operands (kind::i8, 128-element k-blocks: the same 128-byte swizzled rows), s32
+// accumulators converted in the epilogue (Epi::i8_sa / i8_sw).
+template <int BN, bool I8>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                         int K, Epi ep) {
@@ -427,7 +468,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nN = (N + BN - 1) / BN;
   const int ntiles = ((M + BM - 1) / BM) * nN;
-  const int nk = (K + BK - 1) / BK;
+  constexpr int BKE = I8 ? 2 * BK : BK;  // k-block width in elements (128 bytes)
+  const int nk = (K + BKE - 1) / BKE;
   // work unit u = (tile u / ks_n, K slice u % ks_n); slice s covers k-blocks [nk*s/ks_n, nk*(s+1)/ks_n)
   const int ks_n = ep.ksplit > 1 ? ep.ksplit : 1;
   const int nunits = ntiles * ks_n;
@@ -475,8 +517,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* sa = smem + stage * STAGE_BYTES;
-          tma_load_2d(&tmA, &full[stage], sa, kb * BK, mt * BM);
-          tma_load_2d(&tmB, &full[stage], sa + A_BYTES, kb * BK, nt * BN);
+          tma_load_2d(&tmA, &full[stage], sa, kb * BKE, mt * BM);
+          tma_load_2d(&tmB, &full[stage], sa + A_BYTES, kb * BKE, nt * BN);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -500,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+      constexpr uint32_t IDESC = I8 ? idesc_i8(BM, BN) : idesc_bf16(BM, BN);
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
@@ -524,8 +566,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; k++)
-            umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; k++) {  // 32 bytes of K per instruction (16 bf16 / 32 int8)
+            if constexpr (I8)
+              umma_i8(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+            else
+              umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+          }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -552,12 +598,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t acc_phase = (it >> 1) & 1;
       const int mt = t / nN, nt = t % nN;
       const int m = mt * BM + row;
-      float mu = 0.f, rstd = 1.f;
+      float mu = 0.f, rstd = 1.f, sa = 1.f;
       if (ep.ln_moments && m < M) {  // issued before the wait: the load overlaps the tile's MMAs
         const float2 mr = ep.ln_moments[m];
         mu = mr.x;
         rstd = mr.y;
       }
+      if (I8 && m < M) sa = ep.i8_sa[m];
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -582,23 +629,42 @@ __global__ void __launch_bounds__(THREADS, 1)
           int* cnt = ep.sk_cnt + (size_t)m * (ep.sk_pitch / 32) + n0 / 32;
           if (atomicAdd(cnt, 1) != ks_n - 1) continue;
           __threadfence();
-          float acc[32];
+          if constexpr (I8) {  // int32 partials: the sum is exact in any order
+            int acc[32];
 #pragma unroll
-          for (int e = 0; e < 32; e++) acc[e] = 0.f;
-          for (int sl = 0; sl < ks_n; sl++) {
+            for (int e = 0; e < 32; e++) acc[e] = 0;
+            for (int sl = 0; sl < ks_n; sl++) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(w + sl * plane + e));
-              acc[e] += v.x;
-              acc[e + 1] += v.y;
-              acc[e + 2] += v.z;
-              acc[e + 3] += v.w;
+              for (int e = 0; e < 32; e += 4) {
+                const int4 v = __ldcg(reinterpret_cast<const int4*>(w + sl * plane + e));
+                acc[e] += v.x;
+                acc[e + 1] += v.y;
+                acc[e + 2] += v.z;
+                acc[e + 3] += v.w;
+              }
             }
-          }
 #pragma unroll
-          for (int e = 0; e < 32; e++) r[e] = __float_as_uint(acc[e]);
+            for (int e = 0; e < 32; e++) r[e] = (uint32_t)acc[e];
+          } else {
+            float acc[32];
+#pragma unroll
+            for (int e = 0; e < 32; e++) acc[e] = 0.f;
+            for (int sl = 0; sl < ks_n; sl++) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(w + sl * plane + e));
+                acc[e] += v.x;
+                acc[e + 1] += v.y;
+                acc[e + 2] += v.z;
+                acc[e + 3] += v.w;
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 32; e++) r[e] = __float_as_uint(acc[e]);
+          }
           *cnt = 0;
         }
+        if constexpr (I8) i8_row_scale(r, sa);
         epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
       }
       tc_fence_before();
@@ -643,11 +709,12 @@ struct PairCfg {
 };
 constexpr int P_A_BYTES = 128 * BK * 2;
 
-template <int MODE>
+template <int MODE, bool I8>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
                              const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epi ep) {
+  static_assert(!(I8 && MODE == 2), "the staged fp32-residual epilogue has no int8 form");
   using C = PairCfg<MODE>;
   constexpr int P_STAGES = C::STAGES, P_STAGE_BYTES = C::STAGE_BYTES;
   constexpr int BN = 256;
@@ -668,7 +735,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const int nN = (N + BN - 1) / BN;
   const int ntiles = ((M + 255) / 256) * nN;
-  const int nk = (K + BK - 1) / BK;
+  constexpr int BKE = I8 ? 2 * BK : BK;  // k-block width in elements (128 bytes)
+  const int nk = (K + BKE - 1) / BKE;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -720,8 +788,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           const uint32_t fb = full_leader0 + stage * 8;
-          tma_load_2d_pair(&tmA, fb, sa, kb * BK, mt * 256 + (int)rank * 128);
-          tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BK, nt * BN + (int)rank * bhalf);
+          tma_load_2d_pair(&tmA, fb, sa, kb * BKE, mt * 256 + (int)rank * 128);
+          tma_load_2d_pair(&tmB, fb, sa + P_A_BYTES, kb * BKE, nt * BN + (int)rank * bhalf);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -739,7 +807,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader CTA only)
-      constexpr uint32_t IDESC = idesc_bf16(256, BN), IDESC_HALF = idesc_bf16(256, BN / 2);
+      constexpr uint32_t IDESC = I8 ? idesc_i8(256, BN) : idesc_bf16(256, BN);
+      constexpr uint32_t IDESC_HALF = I8 ? idesc_i8(256, BN / 2) : idesc_bf16(256, BN / 2);
       const uint32_t empty0_self = smem_u32(&empty[0]), empty0_peer = mapa_shared(smem_u32(&empty[0]), 1);
       const uint32_t tfull0_self = smem_u32(&tfull[0]), tfull0_peer = mapa_shared(smem_u32(&tfull[0]), 1);
       uint32_t stage = 0, phase = 0;
@@ -764,8 +833,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
           const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + P_A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; k++)
-            umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < BK / 16; k++) {  // 32 bytes of K per instruction (16 bf16 / 32 int8)
+            if constexpr (I8)
+              umma_i8_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
           umma_commit_pair(empty0_self + stage * 8);
           umma_commit_pair(empty0_peer + stage * 8);
           if (++stage == P_STAGES) {
@@ -806,12 +879,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint32_t acc_phase = (it >> 1) & 1;
       const int mt = t / nN, nt = t % nN;
       const int m = mt * 256 + (int)rank * 128 + row;
-      float mu = 0.f, rstd = 1.f;
+      float mu = 0.f, rstd = 1.f, sa = 1.f;
       if (ep.ln_moments && m < M) {
         const float2 mr = ep.ln_moments[m];
         mu = mr.x;
         rstd = mr.y;
       }
+      if (I8 && m < M) sa = ep.i8_sa[m];
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * CH * 32);
       const int nbase = nt * BN + half * CH * 32;
       if constexpr (MODE == 2) {
@@ -925,6 +999,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tb + (uint32_t)(i * 32), r);
           tmem_ld_wait();
+          if constexpr (I8) i8_row_scale(r, sa);
           if (m < M) epilogue_chunk_rw<true>(r, rw[i & 1], m, M, n0, N, ep, mu, rstd);
         }
       } else {
@@ -937,6 +1012,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tb + (uint32_t)(i * 32), r);
           tmem_ld_wait();
+          if constexpr (I8) i8_row_scale(r, sa);
           if (m < M) epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
         }
       }
@@ -980,65 +1056,87 @@ static bool pair_mode2_ok(const Epi& ep, int N, int K) {
          (!ep.out2 || ep.ldo2 % 8 == 0);
 }
 
-template <int MODE>
+template <int MODE, bool I8>
 static void pair_attr(int dev) {
   static bool done[64] = {false};
   if (dev >= 0 && dev < 64 && !done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          PairCfg<MODE>::SMEM_BYTES);
     done[dev] = true;
   }
 }
 
-static int launch_pair(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
-                       int K, const Epi& ep) {
+// K-major operand tensor maps: bf16 with 64-element boxes, or int8 with 128-element ones (128 bytes either way).
+static int make_tmap_op(CUtensorMap* m, const void* p, int K, int rows, long long ld, int box_rows, bool i8) {
+  return i8 ? make_tmap_i8(m, p, (uint64_t)K, (uint64_t)rows, (uint64_t)ld, 2 * BK, box_rows)
+            : make_tmap_bf16(m, p, (uint64_t)K, (uint64_t)rows, (uint64_t)ld, BK, box_rows);
+}
+
+template <int MODE, bool I8>
+static void launch_pair_mode(cudaStream_t st, int clusters, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const CUtensorMap& tr, const CUtensorMap& to, const CUtensorMap& to2, int M, int N, int K,
+                             const Epi& ep) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  pair_attr<MODE, I8>(dev);
+  launch_k(gemm_bf16_tc_pair_kernel<MODE, I8>, 2 * clusters, THREADS, PairCfg<MODE>::SMEM_BYTES, st, ta, tb, tr, to, to2,
+           M, N, K, ep);
+}
+
+static int launch_pair(cudaStream_t st, const void* A, long long lda, const void* W, long long ldw, int M, int N,
+                       int K, const Epi& ep, bool i8) {
   CUtensorMap ta, tb, tr, to, to2;
   memset(&tr, 0, sizeof(tr));
   memset(&to, 0, sizeof(to));
   memset(&to2, 0, sizeof(to2));
-  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128);
+  int rc = make_tmap_op(&ta, A, K, M, lda, 128, i8);
   if (rc) return rc;
-  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, 128);
+  rc = make_tmap_op(&tb, W, K, N, ldw, 128, i8);
   if (rc) return rc;
-  const int mode = !ep.res ? 0 : pair_mode2_ok(ep, N, K) ? 2 : 1;
+  const int mode = !ep.res ? 0 : (!i8 && pair_mode2_ok(ep, N, K)) ? 2 : 1;
   if (mode == 2) {
     rc = make_tmap_epi(&tr, ep.res, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldr, 32, 32, 128);
     if (!rc) rc = make_tmap_epi(&to, ep.out, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo, 32, 32, 128);
     if (!rc && ep.out2) rc = make_tmap_epi(&to2, ep.out2, 2, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo2, 32, 32, 64);
     if (rc) return rc;
   }
-  int dev = 0;
-  cudaGetDevice(&dev);
   const long long ntiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int max_clusters = sm_count() / 2;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
-  if (mode == 2) {
-    pair_attr<2>(dev);
-    launch_k(gemm_bf16_tc_pair_kernel<2>, 2 * clusters, THREADS, PairCfg<2>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
+  if (i8) {
+    if (mode == 1) launch_pair_mode<1, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    else launch_pair_mode<0, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+  } else if (mode == 2) {
+    launch_pair_mode<2, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   } else if (mode == 1) {
-    pair_attr<1>(dev);
-    launch_k(gemm_bf16_tc_pair_kernel<1>, 2 * clusters, THREADS, PairCfg<1>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
+    launch_pair_mode<1, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   } else {
-    pair_attr<0>(dev);
-    launch_k(gemm_bf16_tc_pair_kernel<0>, 2 * clusters, THREADS, PairCfg<0>::SMEM_BYTES, st, ta, tb, tr, to, to2, M, N, K, ep);
+    launch_pair_mode<0, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   }
   return check_launch("vt_gemm (CTA pair)");
 }
 
 // Split-K factor for a 128 x 64 tile launch with a workspace: 1 unless the tiles leave two thirds of the
-// SMs idle, else the s in 1..16 that minimises the k-blocks of the busiest CTA, ceil(tiles * s / SMs) *
-// ceil(nk / s), plus 2 k-blocks' worth for the partial-sum pass.  Measured on the text question (M 32):
-// a CTA of this kernel streams about one 8 KB weight block per 0.3 us, so the 32-tile proj / fc2 run
-// 13 -> 10 us and 39 -> 16 us split 4 ways, while the 96- / 128-tile qkv / fc1 got slower split (the
-// atomic partial sums of their wide outputs cost more than the idle third of the SMs).
-static int split_k(long long ntiles, int K) {
-  const int nk = (K + BK - 1) / BK, sms = sm_count();
+// SMs idle, else the s in 1..16 that minimises the busiest CTA's work, ceil(tiles * s / SMs) work units of
+// ceil(nk / s) k-blocks plus a fixed cost of 2 k-blocks each (accumulator hand-off, partial store), plus 2
+// k-blocks' worth for the partial-sum pass.  Measured on the text question (M 32): a CTA of this kernel
+// streams about one 8 KB weight block per 0.3 us, so the 32-tile proj / fc2 run 13 -> 10 us and
+// 39 -> 16 us split 4 ways, while the 96- / 128-tile qkv / fc1 got slower split (the atomic partial sums of
+// their wide outputs cost more than the idle third of the SMs).  Without the per-unit cost fc2 chose 9
+// (bf16) or 13 (int8) slices, several units per CTA: the whole question took 2.48 / 2.91 ms instead of
+// 2.32 / 2.34 ms.  VT_SPLITK_UNIT overrides the per-unit cost (tuning switch).
+static int split_k(long long ntiles, int K, int bke) {
+  static const int unit = [] {
+    const char* e = getenv("VT_SPLITK_UNIT");
+    return e ? atoi(e) : 2;
+  }();
+  const int nk = (K + bke - 1) / bke, sms = sm_count();
   if (ntiles * 3 > sms) return 1;
   int best_s = 1;
   long long best = -1;
   for (int s = 1; s <= kMaxSplit && s <= nk; s++) {
-    const long long cost = (ntiles * s + sms - 1) / sms * ((nk + s - 1) / s) + (s > 1 ? 2 : 0);
+    const long long cost = (ntiles * s + sms - 1) / sms * ((nk + s - 1) / s + unit) + (s > 1 ? 2 : 0);
     if (best < 0 || cost < best) {
       best = cost;
       best_s = s;
@@ -1047,37 +1145,40 @@ static int split_k(long long ntiles, int K) {
   return best_s;
 }
 
-template <int BN>
-static int launch_bn(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
-                     int K, Epi ep) {
+template <int BN, bool I8>
+static int launch_bn(cudaStream_t st, const void* A, long long lda, const void* W, long long ldw, int M, int N, int K,
+                     Epi ep) {
   CUtensorMap ta, tb;
-  int rc = make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
+  int rc = make_tmap_op(&ta, A, K, M, lda, BM, I8);
   if (rc) return rc;
-  rc = make_tmap_bf16(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BK, BN);
+  rc = make_tmap_op(&tb, W, K, N, ldw, BN, I8);
   if (rc) return rc;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Cfg<BN>::SMEM_BYTES);
     attr_done[dev] = true;
   }
   const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K) : 1;  // <= kMaxSplit
+  ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K, I8 ? 2 * BK : BK) : 1;  // <= kMaxSplit
   const long long units = ntiles * ep.ksplit;
   if (units > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  launch_k(gemm_bf16_tc_kernel<BN>, grid, THREADS, Cfg<BN>::SMEM_BYTES, st, ta, tb, M, N, K, ep);
+  launch_k(gemm_bf16_tc_kernel<BN, I8>, grid, THREADS, Cfg<BN>::SMEM_BYTES, st, ta, tb, M, N, K, ep);
   return check_launch("vt_gemm");
 }
 
-static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M, int N,
-                  int K, Epi ep) {
+// i8: A and W are int8 (pitches in bytes, multiples of 16) and ep carries the int8 scales.
+static int launch(cudaStream_t st, const void* A, long long lda, const void* W, long long ldw, int M, int N, int K,
+                  Epi ep, bool i8 = false) {
   if (M < 0 || N < 0 || K < 0) return set_error(E_SHAPE, "vt_gemm: negative shape M=%d N=%d K=%d", M, N, K);
   if (M == 0 || N == 0) return OK;
   if (K == 0) return set_error(E_SHAPE, "vt_gemm: K must be >= 1");
   if (!A || !W || !ep.out) return set_error(E_SHAPE, "vt_gemm: null operand");
-  if (lda < K || ldw < K || lda % 8 || ldw % 8 || !aligned16(A) || !aligned16(W))
+  const int pal = i8 ? 16 : 8;  // pitch alignment in elements: 16 bytes
+  if (lda < K || ldw < K || lda % pal || ldw % pal || !aligned16(A) || !aligned16(W))
     return set_error(E_SHAPE, "vt_gemm: A/W need 16-byte aligned bases and row pitches (lda=%lld ldw=%lld K=%d)", lda,
                      ldw, K);
   if (ep.pk_T <= 0 && (ep.ldo < N || ep.ldo % 8 || !aligned16(ep.out)))
@@ -1108,7 +1209,7 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
     const char* e = getenv("VT_GEMM_BN");
     return e ? atoi(e) : 0;
   }();
-  if (forced == 192) return launch_bn<192>(st, A, lda, W, ldw, M, N, K, ep);
+  if (forced == 192 && !i8) return launch_bn<192, false>(st, A, lda, W, ldw, M, N, K, ep);
   // CTA-pair 256 x 256 tiles unless VT_GEMM_2SM=0 (A/B switch) or the problem is a single small tile row
   static const int pair = [] {
     const char* e = getenv("VT_GEMM_2SM");
@@ -1122,11 +1223,34 @@ static int launch(cudaStream_t st, const uint16_t* A, long long lda, const uint1
   const int sms = sm_count();
   const long long tiles_pair = (long long)((M + 255) / 256) * ((N + 255) / 256);
   const long long tiles_256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
-  if (pair && M > 128 && tiles_pair >= sms / 8) return launch_pair(st, A, lda, W, ldw, M, N, K, ep);
-  if (forced == 256 || tiles_256 >= sms / 2) return launch_bn<256>(st, A, lda, W, ldw, M, N, K, ep);
-  return launch_bn<64>(st, A, lda, W, ldw, M, N, K, ep);
+  if (pair && M > 128 && tiles_pair >= sms / 8) return launch_pair(st, A, lda, W, ldw, M, N, K, ep, i8);
+  if (forced == 256 || tiles_256 >= sms / 2)
+    return i8 ? launch_bn<256, true>(st, A, lda, W, ldw, M, N, K, ep)
+              : launch_bn<256, false>(st, A, lda, W, ldw, M, N, K, ep);
+  return i8 ? launch_bn<64, true>(st, A, lda, W, ldw, M, N, K, ep)
+            : launch_bn<64, false>(st, A, lda, W, ldw, M, N, K, ep);
 }
 
+}  // namespace gemm
+}  // namespace vt
+
+extern "C" long long vt_gemm_ws_bytes(int M, int N);
+
+namespace vt {
+namespace gemm {
+// Points ep's split-K state into the caller's workspace (null: no split-K).
+static int set_workspace(Epi& ep, void* ws, long long ws_bytes, int M, int N) {
+  if (!ws || M <= 0 || N <= 0) return OK;
+  if (!aligned16(ws) || ws_bytes < vt_gemm_ws_bytes(M, N))
+    return set_error(E_SHAPE, "vt_gemm: workspace of %lld bytes (needs %lld, 16-byte aligned)", ws_bytes,
+                     vt_gemm_ws_bytes(M, N));
+  const int p = (N + 31) / 32 * 32;
+  const size_t planes = (size_t)kMaxSplit * M * p * 4;
+  ep.sk_cnt = static_cast<int*>(ws);
+  ep.sk_ws = reinterpret_cast<float*>(static_cast<char*>(ws) + ((size_t)ws_bytes / 16 * 16 - planes));
+  ep.sk_pitch = p;
+  return OK;
+}
 }  // namespace gemm
 }  // namespace vt
 
@@ -1195,17 +1319,27 @@ int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const ui
                    tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
                    reinterpret_cast<const float2*>(ln_moments), ln_c, 0};
-  if (ws && M > 0 && N > 0) {
-    if (!aligned16(ws) || ws_bytes < vt_gemm_ws_bytes(M, N))
-      return set_error(E_SHAPE, "vt_gemm_fused_ws: workspace of %lld bytes (needs %lld, 16-byte aligned)", ws_bytes,
-                       vt_gemm_ws_bytes(M, N));
-    const int p = (N + 31) / 32 * 32;
-    const size_t planes = (size_t)gemm::kMaxSplit * M * p * 4;
-    ep.sk_cnt = static_cast<int*>(ws);
-    ep.sk_ws = reinterpret_cast<float*>(static_cast<char*>(ws) + ((size_t)ws_bytes / 16 * 16 - planes));
-    ep.sk_pitch = p;
-  }
+  const int rc = vt::gemm::set_workspace(ep, ws, ws_bytes, M, N);
+  if (rc) return rc;
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+// W8A8 int8 GEMM: out[M,N] = epilogue(((float)(A[M,K] . W[N,K]^T) * sa[m]) * sw[n] + bias[n]), the int32
+// dot products exact, GELU-tanh on the fp32 value when gelu; A / W signed int8 with pitches in bytes
+// (multiples of 16).  Same output / residual / workspace rules as vt_gemm_fused_ws.
+int vt_gemm_i8(cudaStream_t st, const int8_t* A, long long lda, const int8_t* W, long long ldw, const float* sa,
+               const float* sw, int M, int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu,
+               const void* res, long long ldr, int res_bf16, void* ws, long long ws_bytes) {
+  using namespace vt;
+  if ((M > 0 && N > 0) && (!sa || !sw || !aligned16(sw)))
+    return set_error(E_SHAPE, "vt_gemm_i8: row scales sa and 16-byte aligned column scales sw are required");
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, 0, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 2 : 0, nullptr, 0,
+                   0, 0, 0, 0, 0, nullptr, nullptr, nullptr, 0};
+  ep.i8_sa = sa;
+  ep.i8_sw = sw;
+  const int rc = vt::gemm::set_workspace(ep, ws, ws_bytes, M, N);
+  if (rc) return rc;
+  return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep, true);
 }
 
 // Fused QKV projection for attention: A[M = crops*T, K] . W[3*H*D, K]^T + bias, written as bf16 straight

@@ -89,6 +89,28 @@ int make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t row
   return OK;
 }
 
+// The same over an int8 matrix [rows][ld] (K-contiguous), box_cols = 128 (one 128-byte swizzle row).
+int make_tmap_i8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems, uint32_t box_cols,
+                 uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(E_TMAP, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base) || ld_elems % 16 != 0 || box_cols != 128)
+    return set_error(E_SHAPE, "tensor map: int8 base %p / row pitch %llu not 16-byte aligned", base,
+                     (unsigned long long)ld_elems);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_elems};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(E_TMAP, "cuTensorMapEncodeTiled (int8) failed (%d): cols %llu rows %llu ld %llu box %ux%u",
+                     (int)r, (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)ld_elems,
+                     box_cols, box_rows);
+  return OK;
+}
+
 // 2-D tensor map over a row-major bf16 (elem_bytes 2) or fp32 (4) matrix [rows][ld], box = box_cols x
 // box_rows, with the given swizzle (for epilogue staging boxes: the box's row is 64 or 128 bytes).
 int make_tmap_epi(CUtensorMap* m, const void* base, int elem_bytes, uint64_t cols, uint64_t rows, uint64_t ld_elems,

@@ -2,6 +2,7 @@
 // (vt::g_status), so they are compiled together rather than linked with relocatable device code.
 #include "host_common.cu"
 #include "gemm_tc.cu"
+#include "quant.cu"
 #include "attn.cu"
 #include "attn_tc.cu"
 #include "attn_noalloc.cu"

@@ -98,6 +98,20 @@ __device__ __forceinline__ unsigned long long gelu_tanh2(unsigned long long x) {
   return f2_fma(h, f2_pack(tanh_approx(u0), tanh_approx(u1)), h);
 }
 
+// GELU-tanh as x * sigmoid(2u) = x / (1 + e^(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3): the function of
+// 0.5 x (1 + tanh u) (the int8 epilogue's GELU, i8gemm.hip:11, there with tanh u = 1 - 2 / (1 + e^(2u)))
+// without the cancellation of 1 + tanh u in the negative tail, so the relative error stays near 1e-6
+// everywhere (tanh.approx leaves an absolute error near 1e-3 there); two MUFU operations (ex2, rcp).
+// e^(-2u) = inf gives -0, e^(-2u) = 0 gives x.
+__device__ __forceinline__ float gelu_sigmoid(float x) {
+  constexpr float k = -2.0f * 1.4426950408889634f * 0.7978845608028654f;  // -2 log2(e) sqrt(2/pi)
+  const float z = k * x * fmaf(0.044715f, x * x, 1.0f);                     // -2u log2(e)
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(z));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
+}
+
 // Attention-tile layout: offset (bf16 elements) of row t, 8-element d chunk c of operand w (0 q, 1 k, 2 v)
 // within one (crop, operand, head) block of ceil(T/128) tiles of NC * 1024 elements.  A Q tile is
 // [c][128 rows][8]; a K or V tile is two 64-row halves [half][c][64 rows][8], so each 64-key tile the
@@ -232,6 +246,16 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The same for signed 8-bit operands (kind::i8, K = 32 per instruction, s32 accumulators in TMEM).
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // The mbarrier gets one arrive once every tcgen05 op this thread issued before has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -339,6 +363,15 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, u
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void umma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // One arrive on the mbarrier at shared::cluster address `bar_addr` (this or the peer CTA) once every
 // tcgen05 op this thread issued before has completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_addr) {
@@ -373,6 +406,10 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
 // Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// kind::i8: s32 accumulator (bits 4-5 = 2), signed 8-bit A and B (bits 7-9, 10-12 = 1), both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace vt

@@ -40,6 +40,9 @@ bool aligned16(const void* p);
 // 128-byte swizzle when box_cols * 2 == 128, zero fill out of bounds.  Returns E_TMAP on failure.
 int make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems,
                    uint32_t box_cols, uint32_t box_rows);
+// The same over an int8 matrix (pitch in bytes, a multiple of 16), box 128 x box_rows, 128-byte swizzle.
+int make_tmap_i8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld_elems, uint32_t box_cols,
+                 uint32_t box_rows);
 // The same for epilogue boxes: bf16 (elem_bytes 2) or fp32 (4), swizzle 0, 64 or 128 bytes.
 int make_tmap_epi(CUtensorMap* m, const void* base, int elem_bytes, uint64_t cols, uint64_t rows, uint64_t ld_elems,
                   uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);

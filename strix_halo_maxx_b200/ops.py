@@ -4,10 +4,15 @@
   VtLin(weight, bias, dtype) -> __call__(x, gelu=False, res=None), class flags fused_gelu / fused_res
   (hgemm.HLin, hgemm.py:139-178).
 * VtAttn -- hattn.Attn(H, T, D) -> __call__(q, k, v, out=None) -> (B, T, H*D) (hattn.py:17-37).
+* I8Lin  -- the `tlin_cls` of the reference's int8 text model, hgemm.HI8Lin (hgemm.py:95-137): W8A8 with
+  quant(x) -> (q, s) and __call__(x, gelu=False, res=None, pre=None); quant_rows / layer_norm_quant / gemm_i8
+  are its kernels.
 * layer_norm / im2col / crop_combine / rglru -- thin wrappers of the remaining kernels.
 
 Every call launches on torch's current stream and raises VtError on a non-zero return code.
 """
+import os
+
 import torch
 
 from ._lib import lib, check as _check
@@ -67,6 +72,87 @@ def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=No
                                 tT, tH, tD, _ptr(ws), 0 if ws is None else ws.numel() * ws.element_size())
     check(rc, "vt_gemm_fused_ws")
     return out
+
+
+def _pad16(n):
+    return (n + 15) // 16 * 16
+
+
+def quant_rows(x2, q=None, s=None):
+    """Per-token int8 quantisation (vt_quant_rows; the reference's quant_rows, moondream/gpu/hgemm.py:10-16):
+    x2 bf16 [M, K] -> (q int8 [M, K] with a 16-byte row pitch, s fp32 [M])."""
+    M, K = x2.shape
+    if q is None:
+        q = torch.empty(M, _pad16(K + I8_PAD), dtype=torch.int8, device=x2.device)[:, :K]
+    if s is None:
+        s = torch.empty(M, dtype=torch.float32, device=x2.device)
+    rc = lib().vt_quant_rows(_stream(), x2.data_ptr(), x2.stride(0), M, K, q.data_ptr(), q.stride(0), s.data_ptr())
+    check(rc, "vt_quant_rows")
+    return q, s
+
+
+def layer_norm_quant(x2, w, b, eps, q, s, out=None):
+    """LayerNorm of x2 [M, N] (fp32 or bf16) fused with the per-token int8 quantisation of its bf16 output
+    (vt_layernorm_quant): fills q int8 [M, N] and s fp32 [M] (and the bf16 output `out` when given)."""
+    M, N = x2.shape
+    rc = lib().vt_layernorm_quant(_stream(), x2.data_ptr(), x2.stride(0), int(x2.dtype == BF16), w.data_ptr(),
+                                  b.data_ptr(), M, N, float(eps), q.data_ptr(), q.stride(0), s.data_ptr(), _ptr(out),
+                                  0 if out is None else out.stride(0))
+    check(rc, "vt_layernorm_quant")
+    return q, s
+
+
+def gemm_i8(q, sx, wq, ldw, K, N, sw, bias=None, gelu=False, res=None, out=None, out_f32=False, ws=None):
+    """out[M, N] = ((float)(q . wq^T) * sx[m]) * sw[n] + bias (+ GELU-tanh on the fp32 value) (+ res), the W8A8
+    GEMM vt_gemm_i8 (the reference's i8gemm_launch, moondream/gpu/hip/i8gemm.hip:480-533)."""
+    M = q.shape[0]
+    if out is None:
+        out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=q.device)[:, :N]
+    rc = lib().vt_gemm_i8(_stream(), q.data_ptr(), q.stride(0), wq.data_ptr(), ldw, sx.data_ptr(), sw.data_ptr(),
+                          M, N, K, _ptr(bias), out.data_ptr(), out.stride(0), int(out.dtype == torch.float32),
+                          int(gelu), _ptr(res), 0 if res is None else res.stride(0),
+                          int(res is not None and res.dtype == BF16), _ptr(ws),
+                          0 if ws is None else ws.numel() * ws.element_size())
+    check(rc, "vt_gemm_i8")
+    return out
+
+
+# Bytes of padding per int8 weight / activation row, the reference's HGEMM_WPAD switch (moondream/gpu/hgemm.py:85,
+# 104-110, default 64 there against DRAM-channel aliasing of power-of-two rows).  Measured on B200 (text
+# decoder, graph replay): 64 bytes made the int8 prefill 3.60 -> 3.64-3.71 ms, so the default here is 0.
+I8_PAD = int(os.environ.get("VT_I8_WPAD", "0"))
+
+
+class I8Lin:
+    """W8A8 int8 linear layer, the mirror of the reference's HI8Lin (moondream/gpu/hgemm.py:95-137): weights
+    quantised once per output channel, s = max(max|w|, 1e-8) / 127 and wq = round-half-even(w / s) clamped to
+    +-127 (hgemm.py:100-103), kept [N, K] with a 16-byte row pitch; each call quantises its activation rows
+    (vt_quant_rows, or takes `pre` = (q, s) already quantised, as md2fast.py:174 shares the LN output's) and
+    runs vt_gemm_i8 (GELU-tanh on the fp32 value when gelu)."""
+    fused_gelu = True
+
+    def __init__(self, weight, bias, device):
+        w = torch.as_tensor(weight).to(device=device, dtype=torch.float32)
+        self.N, self.K = w.shape
+        # true division, as the reference's numpy statement of these numerics does (moondream/npu/p4/
+        # pack_i8.py:56-61): torch on CUDA would turn a division by a Python scalar into a multiplication
+        # by its rounded reciprocal, one ulp off for some channels
+        s = w.abs().amax(dim=1).clamp_min(1e-8)
+        s = s / torch.full_like(s, 127.0)
+        wq = (w / s[:, None]).round().clamp(-127, 127).to(torch.int8)
+        self.ldw = _pad16(self.K + I8_PAD)
+        self.wq = torch.zeros(self.N, self.ldw, dtype=torch.int8, device=device)
+        self.wq[:, :self.K] = wq
+        self.sw = s.contiguous()
+        self.b = None if bias is None else torch.as_tensor(bias).to(device=device, dtype=torch.float32).contiguous()
+
+    def quant(self, x2, q=None, s=None):
+        return quant_rows(x2, q, s)
+
+    def __call__(self, x2, gelu=False, res=None, pre=None, out=None, out_f32=False, ws=None):
+        q, sx = pre if pre is not None else quant_rows(x2)
+        return gemm_i8(q, sx, self.wq, self.ldw, self.K, self.N, self.sw, self.b, gelu=gelu, res=res, out=out,
+                       out_f32=out_f32, ws=ws)
 
 
 def gemm_workspace(M, N, device):

@@ -10,8 +10,12 @@ Per layer (md2fast.py:169-199, the parallel block):
                                                 md2fast.py:182-183); question: vt_attn_causal over the cache
     x += a Wproj^T + b                          vt_gemm, fp32 residual epilogue
     x += gelu_tanh(h W1^T + b1) W2^T + b2       vt_gemm (GELU epilogue), vt_gemm + residual
-The yes / no logits are LN(x[last]) Wyn^T + byn (md2fast.py:210-212).  The reference runs these GEMMs as int8
-W8A8 (hgemm.HI8Lin); here they are the bf16 tcgen05 GEMMs of the tower.  The KV caches ([layers][H][762][64]
+The yes / no logits are LN(x[last]) Wyn^T + byn (md2fast.py:210-212).  The four linears run either as the
+tower's bf16 tcgen05 GEMMs (int8=False, the reference's FastMD2 with tlin_cls=HLin) or as W8A8 int8 tcgen05
+GEMMs (int8=True, tlin_cls=HI8Lin, md2fast.py:88, 112-113): per layer the LN output is quantised once, in the
+LayerNorm kernel (vt_layernorm_quant), and shared by qkv and fc1 (md2fast.py:174); the attention output and the
+fc1 output (GELU fused into its epilogue) are quantised before proj and fc2 (vt_quant_rows + vt_gemm_i8,
+ops.I8Lin).  The KV caches ([layers][H][762][64]
 bf16) live on the device, owned by this object: encode() fills positions 0 .. 729, query() 730 .. 761.
 """
 import torch
@@ -32,9 +36,10 @@ def rope_tables(cfg: TextConfig, device):
 
 
 class TextDecoder:
-    def __init__(self, weights, cfg: TextConfig = TEXT, device="cuda", graphs=True):
+    def __init__(self, weights, cfg: TextConfig = TEXT, device="cuda", graphs=True, int8=False):
         self.cfg = cfg
         self.use_graphs = graphs
+        self.int8 = int8
         self._qgraph = self._egraph = None
         dev = self.dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -47,6 +52,9 @@ class TextDecoder:
             p = f"tblocks.{i}."
             b = {"ln_w": _dev_vec(W[p + "ln_w"], dev), "ln_b": _dev_vec(W[p + "ln_b"], dev)}
             for n in ("qkv", "proj", "fc1", "fc2"):
+                if int8:
+                    b[n] = ops.I8Lin(W[p + n + "_w"], W[p + n + "_b"], dev)
+                    continue
                 b[n + "_w"], b[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
                 b[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
             self.layers.append(b)
@@ -71,6 +79,12 @@ class TextDecoder:
         self._emb = torch.zeros(P - 1, D, dtype=F32, device=dev)
         self.logits = torch.empty(1, 8, dtype=F32, device=dev)
         self.attn = ops.VtAttn(H, P, hd, dev)
+        if int8:  # quantised activations (padded 16-byte row pitches) and their per-token scales
+            pad = lambda k: (k + ops.I8_PAD + 15) // 16 * 16
+            self.hq = torch.empty(P, pad(D), dtype=torch.int8, device=dev)[:, :D]
+            self.aq = torch.empty(P, pad(D), dtype=torch.int8, device=dev)[:, :D]
+            self.fq = torch.empty(P, pad(cfg.ff), dtype=torch.int8, device=dev)[:, :cfg.ff]
+            self.hs, self.as_, self.fs = (torch.empty(P, dtype=F32, device=dev) for _ in range(3))
         # split-K workspace of the question's GEMMs (32 rows; the widest output is fc1's)
         self.ws = ops.gemm_workspace(cfg.q_len, max(3 * D, cfg.ff), dev)
 
@@ -80,6 +94,8 @@ class TextDecoder:
         x, h, qkv, a, f = self.x[:n], self.h[:n], self.qkv[:n], self.a[:n], self.f[:n]
         q = self.qflat[:H * n * hd].view(H, n, hd)
         ws = None if full else self.ws  # the question's GEMMs are too small to fill the GPU: split K
+        if self.int8:
+            return self._layers_i8(n, pos0, full, q, ws)
         for i, b in enumerate(self.layers):
             ops.layer_norm(x, b["ln_w"], b["ln_b"], cfg.eps, out=h)
             ops.gemm(h, b["qkv_w"], b["qkv_ld"], D, 3 * D, b["qkv_b"], out=qkv, ws=ws)
@@ -91,6 +107,25 @@ class TextDecoder:
             ops.gemm(a, b["proj_w"], b["proj_ld"], D, D, b["proj_b"], res=x, out=x, ws=ws)
             ops.gemm(h, b["fc1_w"], b["fc1_ld"], D, Fh, b["fc1_b"], gelu=True, out=f, ws=ws)
             ops.gemm(f, b["fc2_w"], b["fc2_ld"], Fh, D, b["fc2_b"], res=x, out=x, ws=ws)
+
+    def _layers_i8(self, n, pos0, full, q, ws):
+        """The same layers with the W8A8 linears (HI8Lin, md2fast.py:169-199 with SHARE_QUANT)."""
+        cfg = self.cfg
+        x, h, qkv, a, f = self.x[:n], self.h[:n], self.qkv[:n], self.a[:n], self.f[:n]
+        hq, aq, fq = self.hq[:n], self.aq[:n], self.fq[:n]
+        hs, as_, fs = self.hs[:n], self.as_[:n], self.fs[:n]
+        for i, b in enumerate(self.layers):
+            # LN + per-token quantisation in one kernel; the int8 rows are shared by qkv and fc1 (md2fast.py:174)
+            pre = ops.layer_norm_quant(x, b["ln_w"], b["ln_b"], cfg.eps, hq, hs)
+            b["qkv"](h, pre=pre, out=qkv, ws=ws)
+            ops.rope_qkv(qkv, pos0, self.cos, self.sin, q, self.kc[i], self.vc[i])
+            if full:
+                self.attn(q[None], self.kc[i][None, :, pos0:pos0 + n], self.vc[i][None, :, pos0:pos0 + n], out=a[None])
+            else:
+                ops.attn_causal(q, self.kc[i], self.vc[i], pos0, a)
+            b["proj"](a, pre=b["proj"].quant(a, aq, as_), res=x, out=x, ws=ws)
+            b["fc1"](h, gelu=True, pre=pre, out=f, ws=ws)
+            b["fc2"](f, pre=b["fc2"].quant(f, fq, fs), res=x, out=x, ws=ws)
 
     def encode(self, emb, bos):
         """Image prefill (md2fast.py:201-206): emb [729, D] fp32 / bf16 on the device, bos id.  The image

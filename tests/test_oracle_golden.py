@@ -138,3 +138,43 @@ def test_resize_restatement_matches_pillow_bit_for_bit(h, w):
     img[..., 1] = ((np.sin(xx / 13.0) + np.cos(yy / 7.0)) * 60 + 128).astype(np.uint8)
     ref = np.asarray(Image.fromarray(img).resize((378, 378), Image.Resampling.LANCZOS))
     assert np.array_equal(resize_lanczos(img, 378, 378), ref)
+
+
+def _i8_golden():
+    return np.load(os.path.join(os.path.dirname(__file__), "golden", "i8_quant_gemm.npz"))
+
+
+def test_i8_restatement_matches_reference_numerics_bit_for_bit():
+    """oracle/i8_ref.py against the reference's own numpy HI8Lin numerics (tests/golden/make_golden_i8.py):
+    activation and weight quantisation, the exact int32 products and the fp32 epilogue, with and without GELU."""
+    from oracle import i8_ref
+    g = _i8_golden()
+    q, sx = i8_ref.quant_rows(g["x"])
+    wq, sw = i8_ref.quant_w(g["w"])
+    assert np.array_equal(q, g["q"]) and np.array_equal(sx, g["sx"])
+    assert np.array_equal(wq, g["wq"]) and np.array_equal(sw, g["sw"])
+    acc = i8_ref.i8_matmul(q, wq)
+    assert np.array_equal(acc, g["acc"])
+    assert np.array_equal(i8_ref.epilogue(acc, sx, sw, g["bias"], False), g["y0"])
+    assert np.allclose(i8_ref.epilogue(acc, sx, sw, g["bias"], True), g["y1"], rtol=1e-6, atol=1e-7)
+    # the edge rows: scale floors, half-way points rounded away from zero (activations) / to even (weights)
+    assert sx[0] == np.float32(1e-5) / np.float32(127) and not q[0].any()
+    assert sw[0] == np.float32(1e-8) / np.float32(127) and not wq[0].any()
+    assert sx[3] == 1.0 and sw[1] == 1.0
+    xh, wh = g["x"][3], g["w"][1]
+    half_x, half_w = (xh % 1) == 0.5, (wh % 1) == 0.5
+    assert half_x.sum() > 100 and half_w.sum() > 100
+    assert np.array_equal(q[3][half_x], (np.sign(xh) * np.ceil(np.abs(xh)))[half_x].astype(np.int8))
+    assert np.array_equal(wq[1][half_w], np.rint(wh)[half_w].astype(np.int8))
+    assert (np.abs(q[3][half_x]) % 2 == 1).any() and (np.abs(wq[1][half_w]) % 2 == 0).all()
+
+
+def test_i8_restatement_detects_a_planted_error():
+    """A quantiser that rounds half to even (instead of away from zero) is caught by the fixture."""
+    from oracle import i8_ref
+    g = _i8_golden()
+    x = g["x"].astype(np.float32)
+    s = (np.maximum(np.abs(x).max(axis=1), np.float32(1e-5)) / np.float32(127.0)).astype(np.float32)
+    wrong = np.clip(np.rint(x / s[:, None]), -127, 127).astype(np.int8)
+    assert not np.array_equal(wrong, g["q"])
+    assert np.array_equal(i8_ref.quant_rows(x)[0], g["q"])
