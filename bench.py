@@ -371,17 +371,10 @@ def text_ms(dev, reps=10):
     gamma 1, beta 0) directly on the device from a seeded generator instead of the host generator the parity
     tests use."""
     from strix_halo_maxx_b200.config import TEXT
-    from strix_halo_maxx_b200.weights import text_spec
+    from strix_halo_maxx_b200.weights import text_weights_device
     from strix_halo_maxx_b200.text import TextDecoder
-    g = torch.Generator(device=dev).manual_seed(0)
-    W = {}
-    for name, shape, kind in text_spec(TEXT):
-        if kind == "gamma":
-            W[name] = torch.ones(shape, device=dev)
-        elif kind in ("beta", "bias"):
-            W[name] = torch.zeros(shape, device=dev)
-        else:
-            W[name] = torch.randn(shape, device=dev, generator=g) * (1.0 if kind == "normal1" else 0.02)
+    W = text_weights_device(TEXT, dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(1)
     emb = torch.randn(TEXT.prefix - 1, TEXT.dim, device=dev, generator=g)
     ids = torch.randint(1, TEXT.vocab, (TEXT.q_len,), device=dev, generator=g)
 

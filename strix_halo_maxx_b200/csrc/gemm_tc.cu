@@ -714,7 +714,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
                              const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epi ep) {
-  static_assert(!(I8 && MODE == 2), "the staged fp32-residual epilogue has no int8 form");
   using C = PairCfg<MODE>;
   constexpr int P_STAGES = C::STAGES, P_STAGE_BYTES = C::STAGE_BYTES;
   constexpr int BN = 256;
@@ -924,20 +923,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             uint8_t* fr = stg + b * 4096 + lane * 128;
             uint8_t* br = stg + 8192 + b * 2048 + lane * 64;
             unsigned long long v[16];
+            if constexpr (I8) {  // ((acc * sa) * sw + bias) + res, the int8 epilogue's order
+              i8_row_scale(r, sa);
+              const float4* s4 = reinterpret_cast<const float4*>(ep.i8_sw + n0);
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-              const float4 x = *reinterpret_cast<const float4*>(fr + ((c ^ (lane & 7)) << 4));
-              v[2 * c] = f2_add(f2_pack(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1])), f2_pack(x.x, x.y));
-              v[2 * c + 1] =
-                  f2_add(f2_pack(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), f2_pack(x.z, x.w));
-            }
-            if (ep.bias) {
-              const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+              for (int c = 0; c < 8; c++) {
+                const float4 sw = __ldg(s4 + c);
+                const float4 bb = ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias + n0) + c)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 x = *reinterpret_cast<const float4*>(fr + ((c ^ (lane & 7)) << 4));
+                unsigned long long a0 = f2_mul(f2_pack(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1])),
+                                               f2_pack(sw.x, sw.y));
+                unsigned long long a1 = f2_mul(f2_pack(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])),
+                                               f2_pack(sw.z, sw.w));
+                if (ep.bias) {
+                  a0 = f2_add(a0, f2_pack(bb.x, bb.y));
+                  a1 = f2_add(a1, f2_pack(bb.z, bb.w));
+                }
+                v[2 * c] = f2_add(a0, f2_pack(x.x, x.y));
+                v[2 * c + 1] = f2_add(a1, f2_pack(x.z, x.w));
+              }
+            } else {
 #pragma unroll
-              for (int j = 0; j < 8; j++) {
-                const float4 bb = __ldg(b4 + j);
-                v[2 * j] = f2_add(v[2 * j], f2_pack(bb.x, bb.y));
-                v[2 * j + 1] = f2_add(v[2 * j + 1], f2_pack(bb.z, bb.w));
+              for (int c = 0; c < 8; c++) {
+                const float4 x = *reinterpret_cast<const float4*>(fr + ((c ^ (lane & 7)) << 4));
+                v[2 * c] =
+                    f2_add(f2_pack(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1])), f2_pack(x.x, x.y));
+                v[2 * c + 1] =
+                    f2_add(f2_pack(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), f2_pack(x.z, x.w));
+              }
+              if (ep.bias) {
+                const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                  const float4 bb = __ldg(b4 + j);
+                  v[2 * j] = f2_add(v[2 * j], f2_pack(bb.x, bb.y));
+                  v[2 * j + 1] = f2_add(v[2 * j + 1], f2_pack(bb.z, bb.w));
+                }
               }
             }
             if (ep.stats_out && m < M) {  // four independent fp32x2 partial sums per pass
@@ -1093,7 +1115,7 @@ static int launch_pair(cudaStream_t st, const void* A, long long lda, const void
   if (rc) return rc;
   rc = make_tmap_op(&tb, W, K, N, ldw, 128, i8);
   if (rc) return rc;
-  const int mode = !ep.res ? 0 : (!i8 && pair_mode2_ok(ep, N, K)) ? 2 : 1;
+  const int mode = !ep.res ? 0 : pair_mode2_ok(ep, N, K) ? 2 : 1;
   if (mode == 2) {
     rc = make_tmap_epi(&tr, ep.res, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldr, 32, 32, 128);
     if (!rc) rc = make_tmap_epi(&to, ep.out, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo, 32, 32, 128);
@@ -1105,7 +1127,8 @@ static int launch_pair(cudaStream_t st, const void* A, long long lda, const void
   const int max_clusters = sm_count() / 2;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
   if (i8) {
-    if (mode == 1) launch_pair_mode<1, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    if (mode == 2) launch_pair_mode<2, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    else if (mode == 1) launch_pair_mode<1, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
     else launch_pair_mode<0, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   } else if (mode == 2) {
     launch_pair_mode<2, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);

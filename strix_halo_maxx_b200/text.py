@@ -175,3 +175,49 @@ class TextDecoder:
         torch.index_select(self.x, 0, self._last, out=self.xl)
         ops.layer_norm(self.xl, self.post_w, self.post_b, cfg.eps, out=self.hl)
         ops.gemm(self.hl, self.yn_w, self.yn_ld, cfg.dim, cfg.n_yn, self.yn_b, out=self.logits[:, :cfg.n_yn], ws=self.ws)
+
+
+def main(argv=None):
+    """python -m strix_halo_maxx_b200.text [--int8] [--bf16] [--reps N] [--eager]: the 24-layer decoder on
+    device-random weights (weights.text_weights_device); prints the mean prefill / question ms of each
+    selected variant (both by default).  With --reps 0 it runs one eager prefill and one question per variant
+    and prints nothing else: the command to put under a profiler's launch list."""
+    import argparse
+    from .weights import text_weights_device
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--int8", action="store_true")
+    ap.add_argument("--bf16", action="store_true")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--eager", action="store_true", help="no CUDA-graph replay")
+    a = ap.parse_args(argv)
+    variants = [v for v, on in (("bf16", a.bf16), ("int8", a.int8)) if on] or ["bf16", "int8"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W = text_weights_device(TEXT, dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    emb = torch.randn(TEXT.prefix - 1, TEXT.dim, device=dev, generator=g)
+    ids = torch.randint(1, TEXT.vocab, (TEXT.q_len,), device=dev, generator=g)
+    for v in variants:
+        dec = TextDecoder(W, TEXT, device=dev, graphs=not a.eager and a.reps > 0, int8=(v == "int8"))
+        res = {}
+        for name, fn in (("prefill_ms", lambda: dec.encode(emb, 0)), ("question_ms", lambda: dec.query(ids, TEXT.q_len - 1))):
+            if a.reps <= 0:
+                fn()
+                continue
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = round(e0.elapsed_time(e1) / a.reps, 4)
+        torch.cuda.synchronize()
+        if res:
+            print(v, res, flush=True)
+        del dec
+
+
+if __name__ == "__main__":
+    main()
