@@ -28,6 +28,21 @@ __device__ __forceinline__ void store4(void* base, long long idx, float4 v, int 
   }
 }
 
+// The per-float4 terms of the LayerNorm sums and the affine step, written with explicit roundings so the
+// warp-per-row and CTA-per-row kernels below produce the same bits for a row (no compiler-chosen FMA
+// contraction differs between them).
+__device__ __forceinline__ float sum4(float4 v) { return __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)); }
+__device__ __forceinline__ float sq4(float4 v, float mean) {
+  const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean), c = __fsub_rn(v.z, mean), d = __fsub_rn(v.w, mean);
+  return __fadd_rn(__fmaf_rn(a, a, __fmul_rn(b, b)), __fmaf_rn(c, c, __fmul_rn(d, d)));
+}
+__device__ __forceinline__ float4 norm4(float4 v, float mean, float rstd, float4 g, float4 b) {
+  return make_float4(__fmaf_rn(__fmul_rn(__fsub_rn(v.x, mean), rstd), g.x, b.x),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.y, mean), rstd), g.y, b.y),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.z, mean), rstd), g.z, b.z),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.w, mean), rstd), g.w, b.w));
+}
+
 // LayerNorm over rows of N (N % 4 == 0, N <= 4096): one warp per row, the row held in registers
 // (two-pass mean / variance in fp32), y = (x - mean) * rsqrt(var + eps) * gamma + beta.
 // Follows F.layer_norm as md2fast.py:43-44 calls it.
@@ -61,16 +76,13 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXV; i++)
-    if (i * 32 + lane < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    if (i * 32 + lane < nv) s = __fadd_rn(s, sum4(v[i]));
   const float mean = RMS ? 0.f : warp_sum(s) / (float)N;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXV; i++) {
     const int c = (i * 32 + lane);
-    if (c < nv) {
-      const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
-      q += (a * a + b * b) + (cc * cc + d * d);
-    }
+    if (c < nv) q = __fadd_rn(q, sq4(v[i], mean));
   }
   const float rstd = rsqrtf(warp_sum(q) / (float)N + eps);
   // all gamma / beta loads before the first store (the compiler may not move a load past a store to y)
@@ -80,10 +92,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
     if (c < nv) {
       const float4 gg = *reinterpret_cast<const float4*>(g + 4 * c);
       const float4 bb = bta ? *reinterpret_cast<const float4*>(bta + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[i].x = (v[i].x - mean) * rstd * gg.x + bb.x;
-      v[i].y = (v[i].y - mean) * rstd * gg.y + bb.y;
-      v[i].z = (v[i].z - mean) * rstd * gg.z + bb.z;
-      v[i].w = (v[i].w - mean) * rstd * gg.w + bb.w;
+      v[i] = norm4(v[i], mean, rstd, gg, bb);
     }
   }
   if constexpr (QUANT) {
@@ -296,6 +305,120 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
   }
 }
 
+// Max over the 256 threads of a CTA; every thread gets the result.  buf: 8 floats of shared memory used by
+// this reduction only.
+__device__ __forceinline__ float cta_max(float v, float* buf) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = buf[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) t = fmaxf(t, buf[w]);
+  return t;
+}
+
+// Sum of the per-float4 terms part[0 .. nv) in the warp-per-row kernel's order: "lane" l adds the terms
+// l, l + 32, l + 64, ... one after another, then the 32 lane sums meet in warp_sum's butterfly.  Warp 0 does
+// it; the result (divided by N) is broadcast through *out.
+__device__ __forceinline__ float lane_order_mean(const float* part, int nv, int N, float* out) {
+  __syncthreads();  // every term is in part[]
+  if (threadIdx.x < 32) {
+    float a = 0.f;
+    for (int c = threadIdx.x; c < nv; c += 32) a = __fadd_rn(a, part[c]);
+    a = warp_sum(a) / (float)N;
+    if (threadIdx.x == 0) *out = a;
+  }
+  __syncthreads();
+  return *out;
+}
+
+// The same LayerNorm / RMSNorm (and LayerNorm + quantisation) for few rows: one CTA of 256 threads per row,
+// G float4 per thread (N <= 1024 G).  The warp-per-row kernel puts 8 rows in a CTA, so a few hundred rows
+// (the text decoder's 730 / 32, TAPNext's 1280) occupy a fraction of the SMs and each row waits out its
+// serial load -> reduce -> gamma / beta -> store chain on one warp.  The sums are formed in that kernel's
+// order (lane_order_mean), so both kernels give the same bits for a row: results do not depend on how many
+// rows a call has.
+template <int G, bool RMS, bool QUANT>
+__global__ void __launch_bounds__(256) norm_row_kernel(const void* x, long long ldx, int in_bf16, const float* g,
+                                                       const float* bta, void* y, long long ldy, int out_f32, int N,
+                                                       float eps, int8_t* qout, long long ldq, float* qs) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
+  __shared__ float part[1024];
+  __shared__ float stat[2];
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  const int nv = N / 4;
+  float4 v[G];
+#pragma unroll
+  for (int i = 0; i < G; i++) {
+    const int c = i * 256 + threadIdx.x;
+    v[i] = c < nv ? load4(x, row * ldx + 4LL * c, in_bf16) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean = 0.f;
+  if constexpr (!RMS) {
+#pragma unroll
+    for (int i = 0; i < G; i++) {
+      const int c = i * 256 + threadIdx.x;
+      if (c < nv) part[c] = sum4(v[i]);
+    }
+    mean = lane_order_mean(part, nv, N, &stat[0]);
+  }
+#pragma unroll
+  for (int i = 0; i < G; i++) {
+    const int c = i * 256 + threadIdx.x;
+    if (c < nv) part[c] = sq4(v[i], mean);
+  }
+  const float rstd = rsqrtf(lane_order_mean(part, nv, N, &stat[1]) + eps);
+#pragma unroll
+  for (int i = 0; i < G; i++) {
+    const int c = i * 256 + threadIdx.x;
+    if (c < nv) {
+      const float4 gg = *reinterpret_cast<const float4*>(g + 4 * c);
+      const float4 bb = bta ? *reinterpret_cast<const float4*>(bta + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[i] = norm4(v[i], mean, rstd, gg, bb);
+    }
+  }
+  if constexpr (QUANT) {  // the rules of layernorm_kernel<.., QUANT = true>
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < G; i++) {
+      if (i * 256 + threadIdx.x < nv) {
+        v[i] = make_float4(bfround(v[i].x), bfround(v[i].y), bfround(v[i].z), bfround(v[i].w));
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+      }
+    }
+    amax = cta_max(amax, red);
+    const float sc = __fdiv_rn(fmaxf(amax, 1e-5f), 127.f);
+    auto q8 = [sc](float xv) -> uint32_t {
+      const float t = __fdiv_rn(xv, sc);
+      int qi = __float2int_rz(__fadd_rn(t, t >= 0.f ? 0.5f : -0.5f));
+      qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+      return (uint32_t)qi & 0xffu;
+    };
+#pragma unroll
+    for (int i = 0; i < G; i++) {
+      const int c = i * 256 + threadIdx.x;
+      if (c < nv) {
+        *reinterpret_cast<uint32_t*>(qout + row * ldq + 4LL * c) =
+            q8(v[i].x) | (q8(v[i].y) << 8) | (q8(v[i].z) << 16) | (q8(v[i].w) << 24);
+        if (y) store4(y, row * ldy + 4LL * c, v[i], 0);
+      }
+    }
+    if (threadIdx.x == 0) qs[row] = sc;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < G; i++) {
+    const int c = i * 256 + threadIdx.x;
+    if (c < nv) store4(y, row * ldy + 4LL * c, v[i], out_f32);
+  }
+}
+
+// Rows below which the CTA-per-row kernel runs (the warp-per-row kernel fills 148 SMs x 2 CTAs x 8 rows).
+constexpr int kRowKernelMaxM = 2368;
+
 static int grid_for(long long work, int threads) {
   long long g = (work + threads - 1) / threads;
   const long long cap = (long long)sm_count() * 16;
@@ -315,6 +438,17 @@ static int norm_launch(const char* what, cudaStream_t st, const void* x, long lo
     return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
+  if (M < kRowKernelMaxM) {
+    const int g = (N / 4 + 255) / 256;
+#define VT_LNR(G)                                                                                                  \
+  launch_k(norm_row_kernel<G, RMS, false>, (unsigned)M, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, N, \
+           eps, (int8_t*)nullptr, 0LL, (float*)nullptr)
+    if (g <= 1) VT_LNR(1);
+    else if (g <= 2) VT_LNR(2);
+    else VT_LNR(4);
+#undef VT_LNR
+    return check_launch(what);
+  }
   const int per_lane = (N / 4 + 31) / 32;
 #define VT_LN(V)                                                                                                  \
   launch_k(layernorm_kernel<V, RMS>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, M, N, \
@@ -341,6 +475,17 @@ static int ln_quant_launch(cudaStream_t st, const void* x, long long ldx, int in
     return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
+  if (M < kRowKernelMaxM) {
+    const int g = (N / 4 + 255) / 256;
+#define VT_LNQR(G)                                                                                                  \
+  launch_k(norm_row_kernel<G, false, true>, (unsigned)M, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, 0, N, eps, \
+           q, ldq, s)
+    if (g <= 1) VT_LNQR(1);
+    else if (g <= 2) VT_LNQR(2);
+    else VT_LNQR(4);
+#undef VT_LNQR
+    return check_launch(what);
+  }
   const int per_lane = (N / 4 + 31) / 32;
 #define VT_LNQ(V)                                                                                                \
   launch_k(layernorm_kernel<V, false, true>, (unsigned)blocks, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, 0, \

@@ -178,7 +178,7 @@ class TextDecoder:
 
 
 def main(argv=None):
-    """python -m strix_halo_maxx_b200.text [--int8] [--bf16] [--reps N] [--eager]: the 24-layer decoder on
+    """python -m strix_halo_maxx_b200.text [--int8] [--bf16] [--reps N] [--eager] [--layers L]: the decoder on
     device-random weights (weights.text_weights_device); prints the mean prefill / question ms of each
     selected variant (both by default).  With --reps 0 it runs one eager prefill and one question per variant
     and prints nothing else: the command to put under a profiler's launch list."""
@@ -189,10 +189,11 @@ def main(argv=None):
     ap.add_argument("--bf16", action="store_true")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--eager", action="store_true", help="no CUDA-graph replay")
+    ap.add_argument("--layers", type=int, default=None, help="fewer layers than the model's 24 (small profiles)")
     a = ap.parse_args(argv)
     variants = [v for v, on in (("bf16", a.bf16), ("int8", a.int8)) if on] or ["bf16", "int8"]
     dev = torch.device("cuda", torch.cuda.current_device())
-    W = text_weights_device(TEXT, dev, seed=0)
+    W = text_weights_device(TEXT, dev, seed=0, n_layers=a.layers)
     g = torch.Generator(device=dev).manual_seed(1)
     emb = torch.randn(TEXT.prefix - 1, TEXT.dim, device=dev, generator=g)
     ids = torch.randint(1, TEXT.vocab, (TEXT.q_len,), device=dev, generator=g)

@@ -148,14 +148,14 @@ def text_weights(cfg, seed=0, n_layers=None, affine="zero"):
     return _generate(text_spec(cfg, n_layers), seed, affine)
 
 
-def text_weights_device(cfg, device, seed=0):
+def text_weights_device(cfg, device, seed=0, n_layers=None):
     """Timing weights for the text decoder drawn directly on the device from a seeded torch generator:
     N(0, 0.02) matrices (N(0, 1) embeddings), LayerNorm gamma 1 and beta / bias 0 (the parity tests use the
     host generator of text_weights instead)."""
     import torch
     g = torch.Generator(device=device).manual_seed(seed)
     W = {}
-    for name, shape, kind in text_spec(cfg):
+    for name, shape, kind in text_spec(cfg, n_layers):
         if kind == "gamma":
             W[name] = torch.ones(shape, device=device)
         elif kind in ("beta", "bias"):

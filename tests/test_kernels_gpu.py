@@ -335,6 +335,26 @@ def test_layernorm(M, N, in_bf16, out_f32):
     assert rel(out, ref) < (1e-5 if out_f32 else 4e-3)
 
 
+@pytest.mark.parametrize("N,in_bf16", [(1152, False), (2048, True), (768, False), (4096, False)])
+def test_layernorm_rows_do_not_depend_on_the_row_count(N, in_bf16):
+    """Few rows run one CTA per row, many rows one warp per row: the same row gives the same bits either way
+    (LayerNorm, RMSNorm and the fused int8 quantisation)."""
+    gen = torch.Generator().manual_seed(N)
+    big = (torch.randn(3000, N, generator=gen) * 2 + 0.3).to(DEV)
+    if in_bf16:
+        big = big.to(BF)
+    w = (torch.randn(N, generator=gen) + 1).to(DEV)
+    b = torch.randn(N, generator=gen).to(DEV)
+    few = big[:17].clone()
+    assert torch.equal(ops.layer_norm(few, w, b, 1e-5), ops.layer_norm(big, w, b, 1e-5)[:17])
+    assert torch.equal(ops.rms_norm(few, w, 1e-6, out_f32=True), ops.rms_norm(big, w, 1e-6, out_f32=True)[:17])
+    qf, sf = torch.empty(17, N, dtype=torch.int8, device=DEV), torch.empty(17, device=DEV)
+    qb, sb = torch.empty(3000, N, dtype=torch.int8, device=DEV), torch.empty(3000, device=DEV)
+    ops.layer_norm_quant(few, w, b, 1e-5, qf, sf)
+    ops.layer_norm_quant(big, w, b, 1e-5, qb, sb)
+    assert torch.equal(qf, qb[:17]) and torch.equal(sf, sb[:17])
+
+
 @pytest.mark.parametrize("kind", [torch.float32, BF, torch.uint8])
 def test_im2col(kind):
     from oracle.tower_ref import im2col, normalize_u8
