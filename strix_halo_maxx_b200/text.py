@@ -177,8 +177,65 @@ class TextDecoder:
         ops.gemm(self.hl, self.yn_w, self.yn_ld, cfg.dim, cfg.n_yn, self.yn_b, out=self.logits[:, :cfg.n_yn], ws=self.ws)
 
 
+def op_times(dev, n=20, reps=5):
+    """Warm time (us) of each kernel of a decoder layer at the prefill (730) and question (32) row counts:
+    every op captured n times in one CUDA graph, replayed `reps` times; inputs L2-resident."""
+    F32_ = torch.float32
+
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(n):
+                    fn()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return round(e0.elapsed_time(e1) / (n * reps) * 1000, 2)
+
+    D, Fh = TEXT.dim, TEXT.ff
+    out = {}
+    for M in (TEXT.prefix, TEXT.q_len):
+        ws = ops.gemm_workspace(M, Fh, dev) if M == TEXT.q_len else None
+        x = torch.randn(M, D, device=dev)
+        w_ln, b_ln = torch.ones(D, device=dev), torch.zeros(D, device=dev)
+        h = torch.empty(M, D, device=dev, dtype=BF16)
+        hq, hs = torch.empty(M, D, device=dev, dtype=torch.int8), torch.empty(M, device=dev)
+        f = torch.randn(M, Fh, device=dev).to(BF16)
+        fq, fs = torch.empty(M, Fh, device=dev, dtype=torch.int8), torch.empty(M, device=dev)
+        r = {"ln": graph_us(lambda: ops.layer_norm(x, w_ln, b_ln, 1e-5, out=h)),
+             "ln_quant": graph_us(lambda: ops.layer_norm_quant(x, w_ln, b_ln, 1e-5, hq, hs)),
+             "quant_2048": graph_us(lambda: ops.quant_rows(h, hq, hs)),
+             "quant_8192": graph_us(lambda: ops.quant_rows(f, fq, fs))}
+        for name, N, K, res, gelu in (("qkv", 3 * D, D, False, False), ("proj", D, D, True, False),
+                                      ("fc1", Fh, D, False, True), ("fc2", D, Fh, True, False)):
+            a = torch.randn(M, K, device=dev).to(BF16)
+            wt = torch.randn(N, K, device=dev) * 0.02
+            bias = torch.zeros(N, device=dev)
+            lin, wb = ops.I8Lin(wt, bias, dev), wt.to(BF16)
+            aq, asc = ops.quant_rows(a)
+            o = torch.zeros(M, N, device=dev, dtype=F32_ if res else BF16)
+            rr = o if res else None
+            r[name + "_bf16"] = graph_us(lambda: ops.gemm(a, wb, K, K, N, bias, gelu=gelu, res=rr, out=o, ws=ws))
+            r[name + "_i8"] = graph_us(lambda: ops.gemm_i8(aq, asc, lin.wq, lin.ldw, K, N, lin.sw, bias, gelu=gelu,
+                                                           res=rr, out=o, ws=ws))
+        out[M] = r
+    return out
+
+
 def main(argv=None):
-    """python -m strix_halo_maxx_b200.text [--int8] [--bf16] [--reps N] [--eager] [--layers L]: the decoder on
+    """python -m strix_halo_maxx_b200.text [--int8] [--bf16] [--reps N] [--eager] [--layers L] [--ops]: the decoder on
     device-random weights (weights.text_weights_device); prints the mean prefill / question ms of each
     selected variant (both by default).  With --reps 0 it runs one eager prefill and one question per variant
     and prints nothing else: the command to put under a profiler's launch list."""
@@ -190,7 +247,12 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--eager", action="store_true", help="no CUDA-graph replay")
     ap.add_argument("--layers", type=int, default=None, help="fewer layers than the model's 24 (small profiles)")
+    ap.add_argument("--ops", action="store_true", help="warm per-kernel times of one layer (op_times) instead")
     a = ap.parse_args(argv)
+    if a.ops:
+        for M, r in op_times(torch.device("cuda", torch.cuda.current_device())).items():
+            print(M, r, flush=True)
+        return
     variants = [v for v, on in (("bf16", a.bf16), ("int8", a.int8)) if on] or ["bf16", "int8"]
     dev = torch.device("cuda", torch.cuda.current_device())
     W = text_weights_device(TEXT, dev, seed=0, n_layers=a.layers)
