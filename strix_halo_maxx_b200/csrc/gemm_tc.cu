@@ -698,10 +698,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 //      memory one chunk ahead, adds in place and TMA-stores the fp32 box (and a bf16 box), so every
 //      global access is a whole-line bulk copy instead of one 32-byte sector in each of 32 rows.  It
 //      trades two of the six mainloop stages for the 96 KB of staging buffers.
-template <int MODE>
+// PBN: the pair tile's width, 256 (each CTA stages 128 rows of B) or 128 (64 rows; for GEMMs whose 256-wide
+// tiles would leave most SM pairs idle, e.g. the text prefill's 730 x 2048 proj / fc2 with 24 tiles).
+template <int MODE, int PBN = 256>
 struct PairCfg {
-  static constexpr int STAGES = MODE == 2 ? 4 : 6;
-  static constexpr int STAGE_BYTES = 2 * 128 * BK * 2;  // this CTA's 128 rows of A and of B
+  static constexpr int B_ROWS = PBN / 2;
+  static constexpr int STAGES = PBN == 256 ? (MODE == 2 ? 4 : 6) : (MODE == 2 ? 5 : 8);
+  static constexpr int STAGE_BYTES = (128 + B_ROWS) * BK * 2;  // this CTA's 128 rows of A and B_ROWS of B
   static constexpr int EPI_WARP_BYTES = MODE == 2 ? 2 * 4096 + 2 * 2048 : 0;  // 2 fp32 + 2 bf16 32x32 boxes
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * EPI_WARP_BYTES;
@@ -709,14 +712,14 @@ struct PairCfg {
 };
 constexpr int P_A_BYTES = 128 * BK * 2;
 
-template <int MODE, bool I8>
+template <int MODE, bool I8, int PBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
                              const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epi ep) {
-  using C = PairCfg<MODE>;
+  using C = PairCfg<MODE, PBN>;
   constexpr int P_STAGES = C::STAGES, P_STAGE_BYTES = C::STAGE_BYTES;
-  constexpr int BN = 256;
+  constexpr int BN = PBN;
   constexpr uint32_t TMEM_COLS = 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -777,8 +780,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int t = cluster; t < ntiles && ok; t += nclusters) {
         const int mt = t / nN, nt = t % nN;
-        // a column tile with at most 128 valid columns runs as N = 128: each CTA then holds 64 B rows
-        const int bhalf = (N - nt * BN <= 128) ? 64 : 128;
+        // (256-wide tiles) a column tile with at most 128 valid columns runs as N = 128: each CTA then holds
+        // 64 B rows; 128-wide tiles always hold 64
+        const int bhalf = (PBN == 128 || N - nt * BN <= 128) ? 64 : 128;
         for (int kb = 0; kb < nk; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, ST_GEMM_PRODUCER)) {
             ok = false;
@@ -822,7 +826,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        const uint32_t idesc = (N - (t % nN) * BN <= 128) ? IDESC_HALF : IDESC;  // see the producer
+        const uint32_t idesc = (PBN == 256 && N - (t % nN) * BN <= 128) ? IDESC_HALF : IDESC;  // see the producer
         for (int kb = 0; kb < nk; kb++) {
           if (!mbar_wait(&full[stage], phase, abort_flag, ST_GEMM_MMA)) {
             ok = false;
@@ -1078,12 +1082,12 @@ static bool pair_mode2_ok(const Epi& ep, int N, int K) {
          (!ep.out2 || ep.ldo2 % 8 == 0);
 }
 
-template <int MODE, bool I8>
+template <int MODE, bool I8, int PBN>
 static void pair_attr(int dev) {
   static bool done[64] = {false};
   if (dev >= 0 && dev < 64 && !done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         PairCfg<MODE>::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE, I8, PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PairCfg<MODE, PBN>::SMEM_BYTES);
     done[dev] = true;
   }
 }
@@ -1094,26 +1098,35 @@ static int make_tmap_op(CUtensorMap* m, const void* p, int K, int rows, long lon
             : make_tmap_bf16(m, p, (uint64_t)K, (uint64_t)rows, (uint64_t)ld, BK, box_rows);
 }
 
-template <int MODE, bool I8>
+template <int MODE, bool I8, int PBN>
 static void launch_pair_mode(cudaStream_t st, int clusters, const CUtensorMap& ta, const CUtensorMap& tb,
                              const CUtensorMap& tr, const CUtensorMap& to, const CUtensorMap& to2, int M, int N, int K,
                              const Epi& ep) {
   int dev = 0;
   cudaGetDevice(&dev);
-  pair_attr<MODE, I8>(dev);
-  launch_k(gemm_bf16_tc_pair_kernel<MODE, I8>, 2 * clusters, THREADS, PairCfg<MODE>::SMEM_BYTES, st, ta, tb, tr, to, to2,
-           M, N, K, ep);
+  pair_attr<MODE, I8, PBN>(dev);
+  launch_k(gemm_bf16_tc_pair_kernel<MODE, I8, PBN>, 2 * clusters, THREADS, PairCfg<MODE, PBN>::SMEM_BYTES, st, ta, tb,
+           tr, to, to2, M, N, K, ep);
+}
+
+template <bool I8, int PBN>
+static void launch_pair_width(cudaStream_t st, int mode, int clusters, const CUtensorMap& ta, const CUtensorMap& tb,
+                              const CUtensorMap& tr, const CUtensorMap& to, const CUtensorMap& to2, int M, int N, int K,
+                              const Epi& ep) {
+  if (mode == 2) launch_pair_mode<2, I8, PBN>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+  else if (mode == 1) launch_pair_mode<1, I8, PBN>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+  else launch_pair_mode<0, I8, PBN>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
 }
 
 static int launch_pair(cudaStream_t st, const void* A, long long lda, const void* W, long long ldw, int M, int N,
-                       int K, const Epi& ep, bool i8) {
+                       int K, const Epi& ep, bool i8, int pbn) {
   CUtensorMap ta, tb, tr, to, to2;
   memset(&tr, 0, sizeof(tr));
   memset(&to, 0, sizeof(to));
   memset(&to2, 0, sizeof(to2));
   int rc = make_tmap_op(&ta, A, K, M, lda, 128, i8);
   if (rc) return rc;
-  rc = make_tmap_op(&tb, W, K, N, ldw, 128, i8);
+  rc = make_tmap_op(&tb, W, K, N, ldw, pbn / 2, i8);
   if (rc) return rc;
   const int mode = !ep.res ? 0 : pair_mode2_ok(ep, N, K) ? 2 : 1;
   if (mode == 2) {
@@ -1122,20 +1135,16 @@ static int launch_pair(cudaStream_t st, const void* A, long long lda, const void
     if (!rc && ep.out2) rc = make_tmap_epi(&to2, ep.out2, 2, (uint64_t)N, (uint64_t)M, (uint64_t)ep.ldo2, 32, 32, 64);
     if (rc) return rc;
   }
-  const long long ntiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  const long long ntiles = (long long)((M + 255) / 256) * ((N + pbn - 1) / pbn);
   if (ntiles > 0x7fffffffLL) return set_error(E_SHAPE, "vt_gemm: too many tiles");
   const int max_clusters = sm_count() / 2;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
   if (i8) {
-    if (mode == 2) launch_pair_mode<2, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
-    else if (mode == 1) launch_pair_mode<1, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
-    else launch_pair_mode<0, true>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
-  } else if (mode == 2) {
-    launch_pair_mode<2, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
-  } else if (mode == 1) {
-    launch_pair_mode<1, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    if (pbn == 128) launch_pair_width<true, 128>(st, mode, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    else launch_pair_width<true, 256>(st, mode, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   } else {
-    launch_pair_mode<0, false>(st, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    if (pbn == 128) launch_pair_width<false, 128>(st, mode, clusters, ta, tb, tr, to, to2, M, N, K, ep);
+    else launch_pair_width<false, 256>(st, mode, clusters, ta, tb, tr, to, to2, M, N, K, ep);
   }
   return check_launch("vt_gemm (CTA pair)");
 }
@@ -1246,7 +1255,16 @@ static int launch(cudaStream_t st, const void* A, long long lda, const void* W, 
   const int sms = sm_count();
   const long long tiles_pair = (long long)((M + 255) / 256) * ((N + 255) / 256);
   const long long tiles_256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
-  if (pair && M > 128 && tiles_pair >= sms / 8) return launch_pair(st, A, lda, W, ldw, M, N, K, ep, i8);
+  // 256 x 128 pair tiles where 256-wide ones would occupy fewer than half of the SM pairs (the text prefill's
+  // 730 x 2048 proj / fc2: 24 -> 48 tiles); VT_GEMM_PAIR_BN=256 / 128 forces one width (A/B switch)
+  static const int pair_bn = [] {
+    const char* e = getenv("VT_GEMM_PAIR_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (pair && M > 128 && tiles_pair >= sms / 8) {
+    const int pbn = pair_bn == 256 ? 256 : (pair_bn == 128 || tiles_pair * 4 < sms) ? 128 : 256;
+    return launch_pair(st, A, lda, W, ldw, M, N, K, ep, i8, pbn);
+  }
   if (forced == 256 || tiles_256 >= sms / 2)
     return i8 ? launch_bn<256, true>(st, A, lda, W, ldw, M, N, K, ep)
               : launch_bn<256, false>(st, A, lda, W, ldw, M, N, K, ep);

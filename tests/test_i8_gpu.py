@@ -116,9 +116,11 @@ def _dev_i8(t):
     return buf[:, :K]
 
 
-# (M, N, K, ws): the CTA-pair kernel (full and half-width last column tile, N and K tails), the 128 x 256
+# (M, N, K, ws): the CTA-pair kernel (full and half-width last column tile, N and K tails; 256 x 128 tiles for
+# the 24-tile 730 x 2048 shapes, with the staged and the register residual epilogue), the 128 x 256
 # tile (M <= 128, many columns), the 128 x 64 tile with and without split-K (the text question's shapes)
-SHAPES = [(730, 6144, 2048, False), (730, 5960, 2048, False), (730, 2048, 8192, False), (100, 19000, 200, False),
+SHAPES = [(730, 6144, 2048, False), (730, 5960, 2048, False), (730, 2048, 8192, False), (730, 2048, 2048, False),
+          (730, 2040, 1024, False), (100, 19000, 200, False),
           (32, 2048, 8192, True), (32, 6144, 2048, True), (32, 2048, 2048, False), (7, 40, 72, True)]
 
 

@@ -55,7 +55,8 @@ def test_gemm_bf16(M, K, N, gelu):
     assert rel(out, ref) < 5e-3
 
 
-@pytest.mark.parametrize("M,K,N", [(729, 1152, 1152), (1458, 4304, 1152), (77, 200, 96)])
+@pytest.mark.parametrize("M,K,N", [(729, 1152, 1152), (1458, 4304, 1152), (77, 200, 96), (730, 2048, 2048),
+                                   (730, 1024, 2040)])
 @pytest.mark.parametrize("res_dtype", [torch.float32, BF])
 def test_gemm_residual(M, K, N, res_dtype):
     x, w, b = _operands(M, K, N, 1)
