@@ -44,7 +44,9 @@ def inputs():
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: python " + os.path.basename(__file__) + " /path/to/reference")
+    ref = sys.argv[1]
     sys.path.insert(0, os.path.join(ref, "moondream", "npu", "p4"))
     import pack_i8  # noqa: E402  (numpy only)
     x, w, bias = inputs()

@@ -33,7 +33,9 @@ def bfv(a):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: python " + os.path.basename(__file__) + " /path/to/reference")
+    ref_root = sys.argv[1]
     ssm_ref = load_ssm_ref(ref_root)
     rng = np.random.Generator(np.random.PCG64(20261202))
     R, C = 96, 64

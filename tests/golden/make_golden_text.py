@@ -33,7 +33,9 @@ def probe(dim):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: python " + os.path.basename(__file__) + " /path/to/reference")
+    ref = sys.argv[1]
     sys.path.insert(0, os.path.join(ref, "moondream", "gpu"))
     import md2fast  # noqa: E402
     cfg, f32 = TEXT, torch.float32
