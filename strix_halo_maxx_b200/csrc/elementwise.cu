@@ -107,8 +107,9 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* x, long long
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float sc = __fdiv_rn(fmaxf(amax, 1e-5f), 127.f);
-    auto q8 = [sc](float xv) -> uint32_t {
-      const float t = __fdiv_rn(xv, sc);
+    const float rsc = __frcp_rn(sc);
+    auto q8 = [sc, rsc](float xv) -> uint32_t {
+      const float t = div_rn_by(xv, sc, rsc);  // == xv / sc (IEEE)
       int qi = __float2int_rz(__fadd_rn(t, t >= 0.f ? 0.5f : -0.5f));
       qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
       return (uint32_t)qi & 0xffu;
@@ -391,8 +392,9 @@ __global__ void __launch_bounds__(256) norm_row_kernel(const void* x, long long 
     }
     amax = cta_max(amax, red);
     const float sc = __fdiv_rn(fmaxf(amax, 1e-5f), 127.f);
-    auto q8 = [sc](float xv) -> uint32_t {
-      const float t = __fdiv_rn(xv, sc);
+    const float rsc = __frcp_rn(sc);
+    auto q8 = [sc, rsc](float xv) -> uint32_t {
+      const float t = div_rn_by(xv, sc, rsc);  // == xv / sc (IEEE)
       int qi = __float2int_rz(__fadd_rn(t, t >= 0.f ? 0.5f : -0.5f));
       qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
       return (uint32_t)qi & 0xffu;

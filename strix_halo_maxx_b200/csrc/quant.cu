@@ -3,7 +3,8 @@
 // HI8Lin.quant, hgemm.py:116-117).  Row m of x (bf16) becomes
 //     s[m] = max(max_k |x[m,k]|, 1e-5) / 127
 //     q[m,k] = trunc(x[m,k] / s[m] + (x / s >= 0 ? 0.5 : -0.5))      (round half away from zero)
-// with IEEE fp32 division and addition, clamped to [-127, 127] (a no-op: |x / s| <= 127 within rounding).
+// with IEEE fp32 division (div_rn_by: the correctly rounded quotient from one reciprocal per row) and
+// addition, clamped to [-127, 127] (a no-op: |x / s| <= 127 within rounding).
 // One CTA of 256 threads per row; the row stays in registers between the max and the quantisation pass
 // (16-byte loads of 8 bf16 values, G of them per thread, K <= 2048 * G).
 #include "vt_common.cuh"
@@ -44,6 +45,7 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const uint16_t* __restri
 #pragma unroll
   for (int i = 1; i < QT / 32; i++) amax = fmaxf(amax, red[i]);
   const float sc = __fdiv_rn(fmaxf(amax, 1e-5f), 127.f);
+  const float rsc = __frcp_rn(sc);
   int8_t* qr = q + row * ldq;
 #pragma unroll
   for (int g = 0; g < G; g++) {
@@ -54,7 +56,7 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const uint16_t* __restri
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         const float xv = (e & 1) ? __uint_as_float(w[e >> 1] & 0xffff0000u) : __uint_as_float(w[e >> 1] << 16);
-        const float v = __fdiv_rn(xv, sc);
+        const float v = div_rn_by(xv, sc, rsc);  // == xv / sc (IEEE)
         int qi = __float2int_rz(__fadd_rn(v, v >= 0.f ? 0.5f : -0.5f));
         qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
         packed[e >> 2] |= ((uint32_t)qi & 0xffu) << (8 * (e & 3));

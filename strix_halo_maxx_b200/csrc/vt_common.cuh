@@ -98,6 +98,20 @@ __device__ __forceinline__ unsigned long long gelu_tanh2(unsigned long long x) {
   return f2_fma(h, f2_pack(tanh_approx(u0), tanh_approx(u1)), h);
 }
 
+// x / d rounded to nearest even, for many x and one d > 0 (normal) whose correctly rounded reciprocal
+// rd = __frcp_rn(d) the caller computed once.  q = x * rd is within 1.5 ulp of x / d; a first correction
+// q + (x - q d) rd (the residual formed in one FMA) brings it within one ulp, and by Markstein's theorem
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990: with rd within half an ulp of 1/d and q within one ulp of
+// x / d, the FMA residual is exact and q + r rd rounds to the correctly rounded quotient) the second
+// correction returns exactly the IEEE quotient.  Five FP operations instead of a full division; valid
+// while the residual does not underflow (|x| above ~1e-30 here, far below any quotient whose rounding
+// matters to the int8 result).
+__device__ __forceinline__ float div_rn_by(float x, float d, float rd) {
+  float q = __fmul_rn(x, rd);
+  q = __fmaf_rn(__fmaf_rn(-q, d, x), rd, q);
+  return __fmaf_rn(__fmaf_rn(-q, d, x), rd, q);
+}
+
 // GELU-tanh as x * sigmoid(2u) = x / (1 + e^(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3): the function of
 // 0.5 x (1 + tanh u) (the int8 epilogue's GELU, i8gemm.hip:11, there with tanh u = 1 - 2 / (1 + e^(2u)))
 // without the cancellation of 1 + tanh u in the negative tail, so the relative error stays near 1e-6
