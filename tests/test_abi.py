@@ -52,3 +52,19 @@ def test_errors_are_reported_without_a_gpu():
     assert rc == -2 and b"16-byte" in L.vt_last_error_string()
     rc = L.vt_attn_fwd(None, 16, 16, 16, 16, 1, 10, 2, 72 + 4, *([8] * 12), 1.0)
     assert rc == -1
+
+
+def test_int8_entry_points_validate_on_the_host():
+    """The W8A8 entry points reject bad shapes / scales before any CUDA call."""
+    L = _lib.lib()
+    # K not a multiple of 8
+    assert L.vt_quant_rows(None, 16, 16, 4, 12, 16, 16, 16) == -2
+    assert b"multiple of 8" in L.vt_last_error_string()
+    # missing scales
+    assert L.vt_gemm_i8(None, 16, 64, 16, 64, None, None, 4, 8, 64, None, 16, 8, 0, 0, None, 0, 0, None, 0) == -2
+    assert b"scales" in L.vt_last_error_string()
+    # LayerNorm width not a multiple of 4
+    assert L.vt_layernorm_quant(None, 16, 16, 0, 16, 16, 4, 6, 1e-5, 16, 16, 16, None, 0) == -2
+    # empty problems are no-ops
+    assert L.vt_quant_rows(None, 16, 16, 0, 16, 16, 16, 16) == 0
+    assert L.vt_gemm_i8(None, 16, 64, 16, 64, None, None, 0, 8, 64, None, 16, 8, 0, 0, None, 0, 0, None, 0) == 0
