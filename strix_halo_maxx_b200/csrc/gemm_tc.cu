@@ -1,7 +1,9 @@
-// bf16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM, operands staged by TMA):
+// bf16 and W8A8 int8 GEMMs on the 5th-generation tensor cores (tcgen05 / TMEM, operands staged by TMA):
 //     C[M, N] = epilogue( A[M, K] . W[N, K]^T )
 // the replacement of the reference's bf16gemm_kernel / bf16gemm_launch
-// (moondream/gpu/hip/i8gemm.hip:286-385, 534-552) that HLin calls (moondream/gpu/hgemm.py:139-178).
+// (moondream/gpu/hip/i8gemm.hip:286-385, 534-552) that HLin calls (moondream/gpu/hgemm.py:139-178), and, with
+// I8 = true (signed int8 operands, kind::i8, s32 accumulators scaled in the epilogue), of the int8 kernels
+// i8gemm_launch / i8gemm_small_launch (i8gemm.hip:91-204, 480-593) that HI8Lin calls (hgemm.py:95-137).
 //
 // Design (one CTA per SM, persistent over output tiles):
 //   * tile 128 x 256 x 64, 4-stage shared-memory ring (48 KB per stage), 128-byte swizzle;
@@ -14,6 +16,8 @@
 //   * epilogue: + bias, then either bf16 output (optionally GELU-tanh applied after rounding to bf16,
 //     as i8gemm.hip:378 does) or fp32 output with a residual / periodic addend (fp32 or bf16) and an
 //     optional bf16 copy.  M, N and K tails are handled by TMA zero fill and masked stores.
+// The CTA-pair kernel below (256 x 256 or 256 x 128 tiles, cta_group::2) runs every GEMM with enough rows
+// to give the SM pairs work; the single-CTA kernel takes the rest (128 x 256, or 128 x 64 with split K).
 #include <cstdlib>
 
 #include "vt_common.cuh"
