@@ -149,10 +149,16 @@ class I8Lin:
     def quant(self, x2, q=None, s=None):
         return quant_rows(x2, q, s)
 
-    def __call__(self, x2, gelu=False, res=None, pre=None, out=None, out_f32=False, ws=None):
-        q, sx = pre if pre is not None else quant_rows(x2)
-        return gemm_i8(q, sx, self.wq, self.ldw, self.K, self.N, self.sw, self.b, gelu=gelu, res=res, out=out,
-                       out_f32=out_f32, ws=ws)
+    def __call__(self, x, gelu=False, res=None, pre=None, out=None, out_f32=False, ws=None):
+        """x [..., K] (any leading shape, as hgemm.py:127 reshapes it) -> [..., N]; `out` (2-D) is filled and
+        returned as given."""
+        shp = x.shape
+        assert shp[-1] == self.K, (shp, self.K)
+        q, sx = pre if pre is not None else quant_rows(as_gemm_operand(x.reshape(-1, self.K)))
+        r2 = None if res is None else res.reshape(-1, self.N)
+        y = gemm_i8(q, sx, self.wq, self.ldw, self.K, self.N, self.sw, self.b, gelu=gelu, res=r2, out=out,
+                    out_f32=out_f32, ws=ws)
+        return y if out is not None else y.reshape(*shp[:-1], self.N)
 
 
 def gemm_workspace(M, N, device):
