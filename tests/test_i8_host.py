@@ -47,3 +47,46 @@ def test_oracle_int8_text_layer_tracks_fp32():
     x8, _ = R.encode(emb, bos, W, TEXT, n_layers=1, i8=i8)
     x32, _ = R.encode(emb, bos, W, TEXT, n_layers=1)
     assert rel(x8, x32) < 3e-2
+
+
+def _rn32(v):
+    """Exact rational v -> nearest float32 (ties to even)."""
+    from fractions import Fraction
+    c = np.float32(float(v))
+    best = None
+    for k in (c, np.nextafter(c, np.float32(np.inf)), np.nextafter(c, np.float32(-np.inf))):
+        if not np.isfinite(k):
+            continue
+        dist = abs(Fraction(float(k)) - v)
+        even = (int(np.array(k, np.float32).view(np.uint32)) & 1) == 0
+        if best is None or dist < best[0] or (dist == best[0] and even):
+            best = (dist, k)
+    return best[1]
+
+
+def test_reciprocal_division_equals_ieee_division():
+    """The quantisation kernels form x / s as q = x * RN(1/s) followed by two FMA corrections q + (x - q s) RN(1/s)
+    (div_rn_by in csrc/vt_common.cuh, Markstein's theorem).  Emulated here in exact arithmetic (each FMA and
+    product rounded once) it equals the IEEE quotient on random activations and on the half-way points of the
+    int8 grid, for scales over 24 binades."""
+    from fractions import Fraction as Fr
+    f32 = np.float32
+
+    def fma(a, b, c):
+        return _rn32(Fr(float(a)) * Fr(float(b)) + Fr(float(c)))
+
+    rng = np.random.default_rng(3)
+    n = 0
+    for _ in range(60):
+        amax = f32(np.exp(rng.uniform(-12, 12)))
+        s = f32(max(amax, f32(1e-5)) / f32(127))
+        rs = _rn32(1 / Fr(float(s)))
+        xs = i8_ref.bf16_round(np.concatenate([rng.uniform(-1, 1, 40).astype(f32) * amax,
+                                                ((rng.integers(-127, 127, 10) + 0.5) * s).astype(f32), [amax, -amax]]))
+        for x in xs:
+            q = _rn32(Fr(float(x)) * Fr(float(rs)))
+            q = fma(fma(-q, s, x), rs, q)
+            q = fma(fma(-q, s, x), rs, q)
+            assert q == f32(x) / s, (x, s)
+            n += 1
+    assert n == 60 * 52
