@@ -22,6 +22,27 @@ from .tower import _dev_mat, _dev_vec
 F32 = torch.float32
 
 
+class RgLruGate:
+    """The RG-LRU temporal update of one block (tapnext/npu/r9/cpuemu.py:33-47) on the device:
+    G = t . [Wx; Wa]^T + [bx; ba] (one GEMM, fp32 out), then vt_rglru: gates, recurrence, state and x += h.
+    gx_w / ga_w are [768 out, 768 in] (dense; the reference's block-diagonal gates are the special case that
+    tests/golden/rglru_ref_cases.npz pins), a_param [768]; G an fp32 [rows >= M, 2 * 768] buffer."""
+
+    def __init__(self, gx_w, gx_b, ga_w, ga_b, a_param, c, dev, G):
+        g = torch.cat([torch.as_tensor(gx_w), torch.as_tensor(ga_w)], 0)
+        self.W = g.shape[1]
+        self.w, self.ld = _dev_mat(g, dev)
+        self.b = _dev_vec(torch.cat([torch.as_tensor(gx_b), torch.as_tensor(ga_b)]), dev)
+        self.a_param = _dev_vec(a_param, dev)
+        self.c = c
+        self.G = G  # fp32 [rows, 2 W] scratch for the gate pre-activations, shareable between blocks
+
+    def __call__(self, t, state, x, first):
+        """t [M, W] bf16 (the normed input), state [M, W] fp32 and x [M, W] fp32 updated in place."""
+        ops.gemm(t, self.w, self.ld, self.W, 2 * self.W, self.b, out=self.G[:t.shape[0]])
+        ops.rglru(self.G[:t.shape[0]], self.a_param, t, state, x, self.c, first)
+
+
 class TapNextStep:
     def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True):
         self.cfg = cfg
@@ -37,16 +58,16 @@ class TapNextStep:
         self.pe_b = _dev_vec(W["patch_b"], dev)
         self.pos = _dev_vec(W["pos_emb"], dev).reshape(cfg.n_img_tok, cfg.width)
         self.blocks = []
+        self.G = torch.empty(cfg.ntok, 2 * cfg.width, dtype=F32, device=dev)
         for i in range(self.n_blocks):
             p = f"blocks.{i}."
             blk = {}
             for n in ("qkv", "proj", "fc1", "fc2"):
                 blk[n + "_w"], blk[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
                 blk[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
-            g = torch.cat([torch.as_tensor(W[p + "gx_w"]), torch.as_tensor(W[p + "ga_w"])], 0)
-            blk["gate_w"], blk["gate_ld"] = _dev_mat(g, dev)
-            blk["gate_b"] = _dev_vec(torch.cat([torch.as_tensor(W[p + "gx_b"]), torch.as_tensor(W[p + "ga_b"])]), dev)
-            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "rms_w", "a_param"):
+            blk["lru"] = RgLruGate(W[p + "gx_w"], W[p + "gx_b"], W[p + "ga_w"], W[p + "ga_b"], W[p + "a_param"],
+                                   cfg.lru_c, dev, self.G)
+            for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "rms_w"):
                 blk[n] = _dev_vec(W[p + n], dev)
             self.blocks.append(blk)
         self.fin_w = _dev_vec(W["final_ln_w"], dev)
@@ -59,7 +80,6 @@ class TapNextStep:
         self.tiles = ops.attn_tiles(1, T, cfg.heads, cfg.head_dim, dev)
         self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.f = torch.empty(T, _pad8(cfg.ff), dtype=BF16, device=dev)
-        self.G = torch.empty(T, 2 * Wd, dtype=F32, device=dev)
         self.state = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
         self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.first = True
@@ -104,6 +124,5 @@ class TapNextStep:
             ops.gemm(self.h, blk["fc1_w"], blk["fc1_ld"], Wd, cfg.ff, blk["fc1_b"], gelu=True, out=self.f[:, :cfg.ff])
             ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x)
             ops.rms_norm(self.x, blk["rms_w"], cfg.eps, out=self.t)
-            ops.gemm(self.t, blk["gate_w"], blk["gate_ld"], Wd, 2 * Wd, blk["gate_b"], out=self.G)
-            ops.rglru(self.G, blk["a_param"], self.t, self.state[i], self.x, cfg.lru_c, first)
+            blk["lru"](self.t, self.state[i], self.x, first)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)

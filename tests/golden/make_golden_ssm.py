@@ -9,6 +9,13 @@ their code is used by ssm_ref.  Run once where the reference is available:
 
 Inputs are seeded (numpy PCG64): bf16-valued activations, conv taps, gate weights and biases of the
 reference's shapes for one head (64 channels), 96 rows, for a first frame (no state) and a later frame.
+
+A second file, rglru_ref_cases.npz, pins the dense-gate RG-LRU restatement of the TAPNext-style step
+(oracle/tapnext_ref.py rglru): ssm_ref is run for all 12 heads (48 rows, distinct seeded weights per head)
+with the conv taps set to the identity (w = [0, 0, 0, 1], bias 0, so the conv output is x itself).  Then
+ssm_ref's h is exactly the RG-LRU of x with a 768 x 768 gate matrix that is block-diagonal in 12 blocks
+of 64 x 64 (the reference's gate structure, pack8.py:124-129), for a first frame and the next one (whose
+state is the first frame's h).
 """
 import os
 import sys
@@ -56,6 +63,36 @@ def main():
                          wx=wx, bx=bx, wa=wa, ba=ba, z=np.asarray(z, np.float32), h=np.asarray(h, np.float32)).items():
             out[f"{case}.{k}"] = v
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "ssm_ref_cases.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, sum(v.nbytes for v in out.values()), "bytes")
+
+    # 12 heads, identity conv: ssm_ref's h = RG-LRU(x) with block-diagonal gates; one block's weights, two
+    # frames of a stream (the second frame's state is the first frame's h)
+    rng = np.random.Generator(np.random.PCG64(20261203))
+    R, H = 48, 12
+    ident_w = np.zeros((4, C), np.float32)
+    ident_w[3] = 1.0
+    zero_b = np.zeros(C, np.float32)
+    zeros = np.zeros((R, C), np.float32)
+    wx = bfv(rng.standard_normal((H, C, C)) * 0.15)
+    wa = bfv(rng.standard_normal((H, C, C)) * 0.15)
+    bx = bfv(rng.standard_normal((H, C)) * 0.1)
+    ba = bfv(rng.standard_normal((H, C)) * 0.1)
+    a_param = bfv(rng.standard_normal((H, C)))
+    out = dict(wx=wx, bx=bx, wa=wa, ba=ba, a_param=a_param)
+    h_prev = np.zeros((R, H * C), np.float32)
+    for case, first in (("first", True), ("next", False)):
+        x = bfv(rng.standard_normal((R, H * C)))
+        h = np.zeros((R, H * C), np.float32)
+        for q in range(H):
+            cs = slice(q * C, (q + 1) * C)
+            _, hq = ssm_ref(zeros, x[:, cs], zeros, zeros, zeros, h_prev[:, cs], ident_w, zero_b, a_param[q],
+                            wx[q], bx[q], wa[q], ba[q], first)
+            h[:, cs] = np.asarray(hq, np.float32)
+        out[f"{case}.x"] = x
+        out[f"{case}.h"] = h
+        h_prev = h
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "rglru_ref_cases.npz")
     np.savez_compressed(path, **out)
     print("wrote", path, sum(v.nbytes for v in out.values()), "bytes")
 

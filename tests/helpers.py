@@ -56,3 +56,24 @@ def golden_rel(out, g):
     pr = np.linalg.norm(proj - g["tok_proj"], axis=-1) / (np.sqrt(8.0) * g["tok_norm"])
     sr = np.abs(out.sum(-1) - g["tok_sum"]) / g["tok_norm"]
     return float(rr.max()), float(pr.max()), float(sr.max())
+
+
+def rglru_case():
+    """The 12-head RG-LRU fixture (tests/golden/make_golden_ssm.py): the reference's ssm_ref with identity conv
+    taps, i.e. the RG-LRU of x with block-diagonal gates.  Returns (W, frames) with W in oracle.tapnext_ref's
+    dense-gate convention ([out, in] matrices, 768 x 768, block-diagonal) and frames = [(x, h), ...] in order."""
+    g = np.load(os.path.join(GOLDEN, "rglru_ref_cases.npz"))
+
+    def dense(w):  # [heads, 64 in, 64 out] (BlockDiagonalLinear) -> [768 out, 768 in]
+        H, C, _ = w.shape
+        d = np.zeros((H * C, H * C), np.float32)
+        for q in range(H):
+            d[q * C:(q + 1) * C, q * C:(q + 1) * C] = w[q].T
+        return d
+
+    W = {"gx_w": dense(g["wx"]), "gx_b": g["bx"].reshape(-1), "ga_w": dense(g["wa"]), "ga_b": g["ba"].reshape(-1),
+         "a_param": g["a_param"].reshape(-1)}
+    return W, [(g["first.x"], g["first.h"]), (g["next.x"], g["next.h"])]
+
+
+RGLRU_TOL = 1e-2  # per row; ssm_ref rounds every intermediate to bf16, the restatement computes in fp32

@@ -10,7 +10,7 @@ import torch
 from strix_halo_maxx_b200.config import TowerConfig
 from strix_halo_maxx_b200 import weights as wg
 from oracle import tower_ref
-from helpers import load_golden, golden_rel
+from helpers import load_golden, golden_rel, rglru_case, RGLRU_TOL
 
 CFG = TowerConfig()
 TOL = 2e-4   # fp32 vs fp32 (same algorithm, possibly different summation order)
@@ -21,7 +21,7 @@ def _weights(meta):
     return W
 
 
-@pytest.mark.parametrize("name", ["vision_u8_27_zero", "vision_u8_2_random"])
+@pytest.mark.parametrize("name", ["vision_u8_27_zero", "vision_u8_2_random", "vision_u8_2_random_foldproj"])
 def test_vision_u8(name):
     g = load_golden(name)
     m = g["meta"]
@@ -29,7 +29,7 @@ def test_vision_u8(name):
     assert np.allclose(g["wsum"], [np.abs(W["patch_w"]).sum(), np.abs(W["blocks.0.qkv_w"]).sum(),
                                    np.abs(W["pos_emb"]).sum()], rtol=1e-6), "weight generator drifted"
     img = wg.crop_u8(1, CFG, seed=m["img_seed"])[0]
-    out = tower_ref.vision_u8(img, W, CFG, eps=m["eps"], n_blocks=m["n_blocks"])
+    out = tower_ref.vision_u8(img, W, CFG, eps=m["eps"], n_blocks=m["n_blocks"], fold_proj=m.get("fold_proj", False))
     assert max(golden_rel(out, g)) < TOL
 
 
@@ -95,6 +95,40 @@ def test_ssm_restatement_detects_a_planted_error():
     z, _ = ssm_bf16(a["y"], a["x"], a["xm1"], a["xm2"], a["xm3"], a["h0"], a["conv_w"][::-1].copy(), a["conv_b"],
                     a["a_param"], a["wx"], a["bx"], a["wa"], a["ba"], False)
     assert not np.array_equal(z.numpy(), a["z"])
+
+
+def _rglru_stream(W, frames, c=8.0):
+    from oracle import tapnext_ref
+    h, errs = None, []
+    for x, ref in frames:
+        h = tapnext_ref.rglru(torch.from_numpy(x), W, "", h, c)
+        r = torch.from_numpy(ref)
+        errs.append(float(((h - r).norm(dim=-1) / r.norm(dim=-1)).max()))
+    return errs
+
+
+def test_rglru_restatement_matches_reference_ssm_ref():
+    """oracle.tapnext_ref.rglru (the RG-LRU of the TAPNext-style step, dense 768 x 768 gates) against the reference's
+    own ssm_ref (tapnext/npu/pack8.py:252-279) run with 12 heads of block-diagonal gates and identity conv taps:
+    a first frame and the next one, state carried, every row within 1e-2 (ssm_ref's bf16 rounding points)."""
+    W, frames = rglru_case()
+    errs = _rglru_stream(W, frames)
+    assert max(errs) < RGLRU_TOL, errs
+
+
+@pytest.mark.parametrize("plant", ["transposed_gates", "swapped_gates", "coefficient_4"])
+def test_rglru_restatement_detects_a_planted_error(plant):
+    """The same fixture rejects gate matrices used transposed, the input and recurrence gates swapped, and the
+    wrong recurrence coefficient (c = 4 instead of 8, which only the second frame sees)."""
+    W, frames = rglru_case()
+    c = 8.0
+    if plant == "transposed_gates":
+        W = {**W, "gx_w": W["gx_w"].T.copy(), "ga_w": W["ga_w"].T.copy()}
+    elif plant == "swapped_gates":
+        W = {**W, "gx_w": W["ga_w"], "ga_w": W["gx_w"], "gx_b": W["ga_b"], "ga_b": W["gx_b"]}
+    else:
+        c = 4.0
+    assert max(_rglru_stream(W, frames, c)) > 10 * RGLRU_TOL
 
 
 def _text_case():
