@@ -72,10 +72,19 @@ def projection(feats, W):
         return linear(gelu(linear(feats, W["proj_fc1_w"], W["proj_fc1_b"])), W["proj_fc2_w"], W["proj_fc2_b"])
 
 
-def vision_u8(img_u8, W, cfg, eps=1e-5, n_blocks=None):
-    """The whole of FastMD2._vision for one uint8 crop -> [729, proj_out] (md2fast.py:147-160)."""
+def vision_u8(img_u8, W, cfg, eps=1e-5, n_blocks=None, fold_proj=False):
+    """The whole of FastMD2._vision for one uint8 crop -> [729, proj_out] (md2fast.py:147-160).  fold_proj:
+    proj_fc1's two K-halves summed in fp32 (md2fast.py:97-101) and applied to x instead of cat([x, x])."""
     x = tower(normalize_u8(img_u8), W, cfg, eps, n_blocks)[0]
+    if fold_proj:
+        return projection(x, fold_projection(W, cfg))
     return projection(torch.cat([x, x], dim=-1), W)
+
+
+def fold_projection(W, cfg):
+    """W with proj_fc1_w [hidden, 2 width] replaced by the sum of its K-halves [hidden, width] (md2fast.py:99)."""
+    w1 = _t(W["proj_fc1_w"]).float()
+    return dict(W, proj_fc1_w=w1[:, :cfg.width] + w1[:, cfg.width:])
 
 
 def combine_crops(feats):

@@ -99,6 +99,10 @@ class VisionTower:
         self.post_b = _dev_vec(W["post_ln_b"], dev)
         self.has_projection = projection and "proj_fc1_w" in W
         if self.has_projection:
+            # fc1 over cat([x, x]) ([proj_hidden, 2 width]), or with its two K-halves already summed
+            # ([proj_hidden, width]) as FastMD2(fold_proj=True) builds it (md2fast.py:97-101)
+            self.p1_k = int(W["proj_fc1_w"].shape[1])
+            assert self.p1_k in (cfg.width, 2 * cfg.width), "proj_fc1 must take width or 2 * width inputs"
             self.p1_w, self.p1_ld = _dev_mat(W["proj_fc1_w"], dev)
             self.p1_b = _dev_vec(W["proj_fc1_b"], dev)
             self.p2_w, self.p2_ld = _dev_mat(W["proj_fc2_w"], dev)
@@ -184,8 +188,9 @@ class VisionTower:
                        out=bf.x)
 
     def project(self, feats2):
-        """Projection MLP (md2fast.py:159-160): [T, 2*width] bf16 -> [T, proj_out] bf16."""
-        assert self.has_projection
+        """Projection MLP (md2fast.py:159-160): [T, 2*width] bf16 ([T, width] for a folded fc1) ->
+        [T, proj_out] bf16."""
+        assert self.has_projection and feats2.shape[-1] == self.p1_k
         cfg = self.cfg
         T = feats2.shape[0]
         if T not in self._proj_bufs:
@@ -193,13 +198,16 @@ class VisionTower:
                                   torch.empty(T, cfg.proj_out, dtype=BF16, device=self.dev))
         hid, out = self._proj_bufs[T]
         x2 = ops.as_gemm_operand(feats2)
-        self._gemm("proj_fc1", x2, self.p1_w, self.p1_ld, 2 * cfg.width, cfg.proj_hidden, self.p1_b, gelu=True, out=hid)
+        self._gemm("proj_fc1", x2, self.p1_w, self.p1_ld, self.p1_k, cfg.proj_hidden, self.p1_b, gelu=True, out=hid)
         self._gemm("proj_fc2", hid, self.p2_w, self.p2_ld, cfg.proj_hidden, cfg.proj_out, self.p2_b, out=out)
         return out
 
     def vision_u8(self, img_u8):
-        """The whole of FastMD2._vision: uint8 [378, 378, 3] -> [729, proj_out] bf16 (one crop: cat([x, x]))."""
+        """The whole of FastMD2._vision: uint8 [378, 378, 3] -> [729, proj_out] bf16 (one crop: cat([x, x]),
+        or x itself when fc1 is folded, md2fast.py:159)."""
         f = self.forward(img_u8.reshape(1, *img_u8.shape[-3:]))
+        if self.p1_k == self.cfg.width:
+            return self.project(f[0])
         cat = torch.empty(self.cfg.ntok, 2 * self.cfg.width, dtype=BF16, device=self.dev)
         cat[:, :self.cfg.width] = f[0]
         cat[:, self.cfg.width:] = f[0]
@@ -207,6 +215,7 @@ class VisionTower:
 
     def frame(self, crops):
         """Config 2: 1 global + n local crops [1+n, 3, 378, 378] -> projected frame features [729, proj_out]."""
+        assert self.p1_k == 2 * self.cfg.width, "the multi-crop frame needs the unfolded [hidden, 2 width] fc1"
         f = self.forward(crops)
         comb = torch.empty(self.cfg.ntok, 2 * self.cfg.width, dtype=BF16, device=self.dev)
         ops.crop_combine(f, comb)
@@ -239,8 +248,7 @@ def weights_from_fastmd2(m):
         W[p + "ln1_w"], W[p + "ln1_b"] = (t.float().cpu() for t in b["ln1"])
         W[p + "ln2_w"], W[p + "ln2_b"] = (t.float().cpu() for t in b["ln2"])
     W["post_ln_w"], W["post_ln_b"] = (t.float().cpu() for t in m.post_ln)
-    if getattr(m, "fold_proj", False):
-        raise NotImplementedError("vt_vision: fold_proj=True is not supported (use the stock two-half projection)")
+    # with fold_proj=True proj_fc1 holds the summed K-halves [hidden, width]; VisionTower takes either shape
     put("proj_fc1", m.proj_fc1)
     put("proj_fc2", m.proj_fc2)
     return W

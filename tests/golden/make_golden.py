@@ -131,6 +131,20 @@ def main():
         m._vision(torch.zeros(cfg.img, cfg.img, 3, dtype=torch.uint8))
     save("block_1_random", dict(case="block", n_blocks=1, affine="random", wseed=6, x_seed=4, eps=1e-5), rec.ln_in[0], W)
 
+    # (4) _vision with fold_proj=True: proj_fc1's two K-halves summed into one [8192, 1152] weight, applied to x
+    #     instead of cat([x, x]) -- built the way FastMD2.__init__ folds it (md2fast.py:97-101)
+    W = wg.tower_weights(cfg, seed=5, n_blocks=2, affine="random")
+    img = wg.crop_u8(1, cfg, seed=3)[0]
+    m = shell(md2fast, W, cfg, 2)
+    w1 = torch.from_numpy(W["proj_fc1_w"]).float()
+    w1 = (w1[:, :cfg.width] + w1[:, cfg.width:]).to(torch.float32)
+    m.fold_proj = True
+    m.proj_fc1 = md2fast.Lin(w1, torch.from_numpy(W["proj_fc1_b"]), torch.float32)
+    with torch.no_grad():
+        out = m._vision(torch.from_numpy(img))
+    save("vision_u8_2_random_foldproj", dict(case="vision_u8", n_blocks=2, affine="random", wseed=5, img_seed=3, eps=1e-5,
+                                             fold_proj=True), out, W)
+
 
 if __name__ == "__main__":
     main()
