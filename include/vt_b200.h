@@ -45,16 +45,6 @@ int vt_gemm_ex(cudaStream_t stream, const uint16_t* A, long long lda, const uint
                int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
                long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2);
 
-/* Non-causal, mask-free attention O = softmax(Q K^T * scale) V for B crops x H heads of T tokens,
- * head_dim D (multiple of 8, <= 80; zero-padded to 64 / 80 on chip).  Element (b,t,h,d) of X is at
- * X + b*sx_b + t*sx_t + h*sx_h + d; Q/K/V read in place (no transposed V copy).
- * Replaces: attn_fwd2, moondream/gpu/hip/attn.hip:442 (plus vtranspose, attn.hip:284), called from
- * hattn.Attn.__call__ (moondream/gpu/hattn.py:26-37). */
-int vt_attn_fwd(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int B,
-                int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b, long long sk_t,
-                long long sk_h, long long sv_b, long long sv_t, long long sv_h, long long so_b, long long so_t,
-                long long so_h, float scale);
-
 /* Superset of vt_gemm_ex with the tower's LayerNorm fusions (NULL / 0 disables each):
  *   stats_out (fp32 output, N % 32 == 0): stats_out[m][j] = (mean, sum of squared deviations) of output row
  *     m over columns 32j..32j+31, float pairs [M][N/32] -- the row statistics of the new residual stream;
@@ -157,14 +147,15 @@ int vt_attn_pack(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, cons
 int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
                       long long so_b, long long so_t, long long so_h, float scale);
 
-/* Attention without any device allocation, for callers that cannot allocate device memory where they
- * need attention: code running during CUDA-graph stream capture (cudaMalloc is not allowed there), hosts
- * with a device-memory budget fixed at start-up, and plain C / FFI callers with no device allocator.
+/* Attention without any device allocation, for callers that cannot allocate device memory where they need
+ * attention: hosts that fix their device-memory budget at start-up and allow no allocation while serving,
+ * and plain C / FFI callers with no device allocator of their own.
  * Same result as vt_attn_pack + vt_attn_tiles_fwd (same strides and scale); the attention tiles live in a
  * fixed 16 MiB array inside the library (held by every GPU that loads it until exit), so problems needing
- * more than 16 MiB of tiles (vt_attn_tiles_bytes) return -2.  Each call zeroes the part it uses; calls that
- * overlap on the GPU race on the shared array.  The first call on a device looks up the array's address
- * with that device current: make it before any stream capture.
+ * more than 16 MiB of tiles (vt_attn_tiles_bytes) return -2.  Every call shares the array, which keeps the
+ * last call's contents; each call writes the zeros its pad rows and lanes need, and calls that overlap on
+ * the GPU race on the array.  The first call on a device does the set-up (the array's device address and
+ * the attention kernels' attributes) with that device current: make it before any stream capture.
  * No counterpart in the reference (its attention always takes a caller-allocated V^T buffer). */
 int vt_attn_fwd_noalloc(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
                         int B, int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b,

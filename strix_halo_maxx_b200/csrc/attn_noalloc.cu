@@ -4,12 +4,11 @@
 // attention tiles those two kernels pass between them live in a fixed array compiled into this library
 // instead of a buffer the caller allocates.  Some callers have no way to allocate device memory at the
 // point where they need attention:
-//   * code that runs while a stream is being captured into a CUDA graph (cudaMalloc is not allowed
-//     during capture, and a caching allocator may have to call it);
 //   * hosts that plan their whole device-memory budget at start-up and forbid allocation afterwards,
-//     such as inference servers with a fixed memory budget per model;
+//     such as inference servers that give each model a fixed share of the GPU's memory and must not
+//     grow past it while serving;
 //   * plain C or FFI callers (a ctypes / cgo / JNI binding without torch) that have no device
-//     allocator of their own.
+//     allocator of their own to hand out a scratch buffer.
 // They pass only Q, K, V and O, all of which they own.
 //
 // Limits and rules:
@@ -18,11 +17,14 @@
 //     larger problems are rejected with E_SHAPE (use vt_attn_pack + vt_attn_tiles_fwd with a buffer of
 //     vt_attn_tiles_bytes(...) bytes instead);
 //   * every GPU that loads this library holds the 16 MiB until the process exits;
-//   * every call shares the one array.  A call first zeroes the part it uses (pad rows and lanes must be
-//     zero), so what an earlier call left there does not matter, but calls that overlap on the GPU --
-//     on streams without ordering between them, or from several host threads -- race on the array;
-//   * the first call on a device looks up the array's device address with that device current
-//     (cudaGetSymbolAddress); make that first call before any stream capture.
+//   * every call shares the one array, which keeps what the last call wrote.  A call first writes zeros
+//     into the pad rows and lanes of the part it uses (the attention kernel reads them and they must be
+//     zero; vt_attn_pack then writes every other element), so what an earlier call left there does not
+//     matter.  Calls that overlap on the GPU -- on streams without ordering between them, or from several
+//     host threads -- race on the array;
+//   * the first call on a device does its set-up with that device current: it looks up the array's
+//     device address (cudaGetSymbolAddress) and sets the attention kernels' shared-memory attributes.
+//     Make that first call before any stream capture.
 #include <mutex>
 
 #include "vt_common.cuh"
@@ -34,6 +36,11 @@ extern "C" int vt_attn_pack(cudaStream_t st, const uint16_t* Q, const uint16_t* 
                             long long sk_t, long long sk_h, long long sv_b, long long sv_t, long long sv_h);
 extern "C" int vt_attn_tiles_fwd(cudaStream_t st, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
                                  long long so_b, long long so_t, long long so_h, float scale);
+namespace vt {
+namespace attn_tc {
+int prepare_device();
+}
+}  // namespace vt
 
 namespace vt {
 namespace noalloc {
@@ -42,7 +49,9 @@ constexpr long long kScratchBytes = 16LL << 20;
 static __device__ __align__(256) uint16_t g_attn_scratch[kScratchBytes / 2];
 
 // Device address of g_attn_scratch on the current device.  In host code the name g_attn_scratch is only
-// a host-side stand-in, never a device address, so the address is looked up once per device.
+// a host-side stand-in, never a device address, so the address is looked up once per device; the same
+// one-time block sets the attention kernels' attributes (attn_tc::prepare_device), so that every set-up
+// step of this entry point happens on its first call per device, whatever the head_dim of later calls.
 static int scratch_address(uint16_t** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};
@@ -57,10 +66,33 @@ static int scratch_address(uint16_t** out) {
     if (e != cudaSuccess || !p)
       return set_error(E_LAUNCH, "vt_attn_fwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
                        cudaGetErrorString(e));
+    const int rc = attn_tc::prepare_device();
+    if (rc) return rc;
     addr[dev] = p;
   }
   *out = static_cast<uint16_t*>(addr[dev]);
   return OK;
+}
+
+// Zeros into the pad slots of the attention tiles of B crops: every 16-byte (8-element) chunk of a row
+// t >= T or of a d chunk c >= D/8, for rows t < Tt*128 and chunks c < NC of every (crop, operand, head).
+// vt_attn_pack writes all the other chunks, so the two kernels together define the whole buffer.
+__global__ void __launch_bounds__(256) zero_pads_kernel(uint16_t* __restrict__ tiles, int B, int T, int H, int D,
+                                                        int NC, int Tt) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
+  const int dch = D / 8, rows = Tt * 128;
+  const long long per_op = (long long)rows * NC;
+  const long long total = (long long)B * 3 * H * per_op;
+  const size_t op_elems = (size_t)Tt * NC * 1024;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long op = i / per_op;  // (crop * 3 + operand) * H + head
+    const int r = (int)(i % per_op);
+    const int t = r / NC, c = r % NC;
+    if (t < T && c < dch) continue;
+    const int w = (int)((op / H) % 3);
+    *reinterpret_cast<uint4*>(tiles + (size_t)op * op_elems + attn_tile_off(w, t, c, NC)) = make_uint4(0, 0, 0, 0);
+  }
 }
 
 }  // namespace noalloc
@@ -87,8 +119,12 @@ int vt_attn_fwd_noalloc(cudaStream_t st, const uint16_t* Q, const uint16_t* K, c
   uint16_t* tiles = nullptr;
   int rc = noalloc::scratch_address(&tiles);
   if (rc) return rc;
-  cudaError_t e = cudaMemsetAsync(tiles, 0, (size_t)need, st);
-  if (e != cudaSuccess) return set_error(E_LAUNCH, "vt_attn_fwd_noalloc: clearing the scratch: %s", cudaGetErrorString(e));
+  const int NC = D <= 64 ? 8 : 10, Tt = (T + 127) / 128;
+  const long long slots = (long long)B * 3 * H * Tt * 128 * NC;
+  const long long g = (slots + 255) / 256, cap = (long long)sm_count() * 16;
+  launch_k(noalloc::zero_pads_kernel, (int)(g < cap ? g : cap), 256, 0, st, tiles, B, T, H, D, NC, Tt);
+  rc = check_launch("vt_attn_fwd_noalloc (pad zeros)");
+  if (rc) return rc;
   rc = vt_attn_pack(st, Q, K, V, tiles, B, T, H, D, sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, sv_b, sv_t, sv_h);
   if (rc) return rc;
   return vt_attn_tiles_fwd(st, tiles, O, B, T, H, D, so_b, so_t, so_h, scale);

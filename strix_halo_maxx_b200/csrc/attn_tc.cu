@@ -20,6 +20,8 @@
 //              bf16 pairs written back over S, row sums in fp32.
 // O is rescaled only when a row max grows by more than 2^8 (P <= 256 otherwise, exact in fp32
 // accumulation), so TMEM round trips of O are rare.  tcgen05 ops of one thread complete in issue order.
+#include <mutex>
+
 #include "vt_common.cuh"
 #include "vt_host.h"
 
@@ -342,22 +344,38 @@ __global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ 
   }
 }
 
+// Once per device, with that device current: the dynamic shared-memory size and carveout of both
+// instantiations (head_dim <= 64 and <= 80).  std::call_once keeps first calls from several host threads safe.
+int prepare_device() {
+  static std::once_flag once[64];
+  static cudaError_t status[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(E_LAUNCH, "attention: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(E_LAUNCH, "attention: device %d out of range", dev);
+  std::call_once(once[dev], [dev] {
+    // two CTAs per SM need (almost) the whole 228 KB as shared memory
+    cudaError_t r = cudaFuncSetAttribute(attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = cudaFuncSetAttribute(attn_tc_kernel<8>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(attn_tc_kernel<10>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<10>::BYTES);
+    if (r == cudaSuccess) r = cudaFuncSetAttribute(attn_tc_kernel<10>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    status[dev] = r;
+  });
+  if (status[dev] != cudaSuccess)
+    return set_error(E_LAUNCH, "attention: setting the kernel attributes: %s", cudaGetErrorString(status[dev]));
+  return OK;
+}
+
 template <int NC>
 static int launch_nc(cudaStream_t st, Args a, int B) {
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(attn_tc_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<NC>::BYTES);
-    // two CTAs per SM need (almost) the whole 228 KB as shared memory
-    cudaFuncSetAttribute(attn_tc_kernel<NC>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr_done[dev] = true;
-  }
+  int rc = prepare_device();
+  if (rc) return rc;
   for (int b0 = 0; b0 < B; b0 += 65535) {
     a.b0 = b0;
     const int nb = (B - b0) < 65535 ? (B - b0) : 65535;
     launch_k(attn_tc_kernel<NC>, dim3(a.Tt, a.H, nb), THREADS, Smem<NC>::BYTES, st, a);
-    int rc = check_launch("vt_attn_tiles_fwd");
+    rc = check_launch("vt_attn_tiles_fwd");
     if (rc) return rc;
   }
   return OK;
