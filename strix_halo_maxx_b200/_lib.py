@@ -18,7 +18,6 @@ SIGNATURES = {
     "vt_device_status": (I, [I, ctypes.POINTER(U)]),
     "vt_gemm_bf16": (I, [P, P, LL, P, LL, P, P, LL, I, I, I, I]),
     "vt_gemm_ex": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL]),
-    "vt_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, F]),
     "vt_gemm_qkv_tiles": (I, [P, P, LL, P, LL, P, P, I, I, I, I, I]),
     "vt_gemm_fused": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, P, I, I, I]),
     "vt_gemm_ws_bytes": (LL, [I, I]),

@@ -3,7 +3,6 @@
 #include "host_common.cu"
 #include "gemm_tc.cu"
 #include "quant.cu"
-#include "attn.cu"
 #include "attn_tc.cu"
 #include "attn_noalloc.cu"
 #include "elementwise.cu"

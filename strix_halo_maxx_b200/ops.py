@@ -281,19 +281,6 @@ class VtAttn:
         return out
 
 
-def attention_mma_sync(q, k, v, out=None):
-    """The first-generation mma.sync attention kernel (vt_attn_fwd), kept as an independent GPU cross-check
-    of the tcgen05 kernel in the tests; no product path calls it."""
-    B, H, T, D = q.shape
-    if out is None:
-        out = torch.empty(B, T, H * D, dtype=BF16, device=q.device)
-    rc = lib().vt_attn_fwd(_stream(), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, T, H, D,
-                           q.stride(0), q.stride(2), q.stride(1), k.stride(0), k.stride(2), k.stride(1),
-                           v.stride(0), v.stride(2), v.stride(1), out.stride(0), out.stride(1), D, D ** -0.5)
-    check(rc, "vt_attn_fwd")
-    return out
-
-
 def layer_norm(x2, w, b, eps, out=None, out_f32=False):
     M, N = x2.shape
     if out is None:

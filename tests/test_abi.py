@@ -50,8 +50,10 @@ def test_errors_are_reported_without_a_gpu():
     L = _lib.lib()
     rc = L.vt_gemm_bf16(None, 16, 588, 16, 588, None, 16, 8, 4, 8, 588, 0)
     assert rc == -2 and b"16-byte" in L.vt_last_error_string()
-    rc = L.vt_attn_fwd(None, 16, 16, 16, 16, 1, 10, 2, 72 + 4, *([8] * 12), 1.0)
-    assert rc == -1
+    rc = L.vt_attn_tiles_fwd(None, 16, 16, 1, 10, 2, 72 + 4, 8, 8, 8, 1.0)
+    assert rc == -1 and b"head_dim" in L.vt_last_error_string()
+    rc = L.vt_attn_pack(None, 16, 16, 16, 16, 1, 10, 2, 72, *([4] * 9))
+    assert rc == -2 and b"multiples of 8" in L.vt_last_error_string()
 
 
 def test_int8_entry_points_validate_on_the_host():
