@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="vt", choices=["vt", "reference"])
     ap.add_argument("--crops", type=int, default=1040)
-    ap.add_argument("--mb", type=int, default=130, help="crops per chunk and rank")
+    ap.add_argument("--mb", type=int, default=130,
+                    help="crops per chunk and rank (at most; with N > 1 capped so every rank has >= 2 chunks)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-frame", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
@@ -224,7 +225,9 @@ def run_vt(a):
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
                                 device_id=dev)
     cfg = TOWER
-    mb = min(a.mb, a.crops // world)
+    # every rank gets at least two chunks when N > 1, so the all-gather of a chunk overlaps the next one's
+    # compute (130 crops per chunk up to N = 4, 65 at N = 8)
+    mb = min(a.mb, a.crops // world if world == 1 else max(1, a.crops // (2 * world)))
     ids = local_crop_ids(a.crops, world, rank, mb)
     n_local = len(ids)
 
@@ -240,8 +243,10 @@ def run_vt(a):
     local_out = torch.empty(n_local, cfg.ntok, cfg.width, dtype=torch.bfloat16, device=dev) if world > 1 else None
     fwd = lambda p, out: tower.forward(p, out=out)   # noqa: E731
 
+    exposed = []
+
     def step():
-        encode_sharded(fwd, pix_dev, feats_all, local_out, mb)
+        encode_sharded(fwd, pix_dev, feats_all, local_out, mb, exposed=exposed)
 
     def barrier():
         if world > 1:
@@ -258,6 +263,7 @@ def run_vt(a):
         step()
     torch.cuda.synchronize()
     device_status(clear=True)
+    exposed.clear()
 
     # ---------------- timed: device-resident inputs
     timer = OpTimer()
@@ -277,6 +283,7 @@ def run_vt(a):
     barrier()
     launches = ops.LAUNCHES - l0
     ms = max_over_ranks(e0.elapsed_time(e1))
+    ag_exposed = max_over_ranks(sum(s.elapsed_time(e) for s, e in exposed) / a.steps) if world > 1 else 0.0
     tower.op_timer = None
     ops_summary = timer.summary()
     clocks = clk.summary()
@@ -326,9 +333,9 @@ def run_vt(a):
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        v, cores = cpu_oracle_rate(W, cfg, 1, 2)
+        v, cores = cpu_oracle_rate(W, cfg, 4, 5)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": "1 crop (27 blocks + post-LN, fp32 torch CPU oracle = port of md2fast.FastMD2._vision), median of 2 after 1 warm-up"}
+               "sample": "4 crops per run (27 blocks + post-LN, fp32 torch CPU oracle = port of md2fast.FastMD2._vision), median of 5 runs after 1 warm-up"}
 
     if rank == 0:
         fl = cfg.flops_per_crop()
@@ -338,8 +345,10 @@ def run_vt(a):
             "dtype": "bf16", "data": "synthetic (seeded U[-1,1] pixels, N(0,0.02) weights; no checkpoints offline)",
             "config": {"workload": f"config 4: {a.crops} crops (80 frames x 13) through the 27-block tower of config 1, "
                                    f"all-gathered [{a.crops},729,1152] bf16", "crops_per_step": a.crops,
-                       "chunk_crops_per_rank": mb, "parallelism": f"dp{world} (crop sharding) + NCCL all-gather",
+                       "chunk_crops_per_rank": mb, "chunks_per_rank": n_local // mb,
+                       "parallelism": f"dp{world} (crop sharding) + NCCL all-gather",
                        "l2": "inputs larger than L2 (pixels %.0f MB per step, activations GBs)" % (a.crops * 3 * 378 * 378 * 2 / 1e6)},
+            "allgather_exposed_ms_per_step": ag_exposed,
             "ms_per_frame_13crop_throughput": 13 * 1000.0 / value,
             "ms_per_frame_13crop_latency": frame_ms,
             "tapnext_ms_per_frame": tap,
@@ -350,6 +359,9 @@ def run_vt(a):
             "roofline": {"kernel": "gemm_bf16_tc_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
                          "bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
                          "frac": achieved / sustained, "traffic": traffic,
+                         "traffic_source": "profiles/gemm_traffic.json: dram__bytes_read.sum + dram__bytes_write.sum per "
+                                           "GEMM launch from an ncu capture of a 26-crop chunk, scaled to the bench's "
+                                           "chunk by its rows (not measured in this run)",
                          "peak_source": f"{src} bf16_tflops_sustained" + (" of measured" if src == "measured" else " of fallback"),
                          "launches": gemm_n, "avg_launch_ms": gemm_ms / max(gemm_n, 1)},
             "kernels": breakdown,

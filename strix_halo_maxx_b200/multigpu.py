@@ -22,10 +22,12 @@ def local_crop_ids(n_total, world, rank, mb):
     return ids
 
 
-def encode_sharded(forward, pix_local, feats_all, local_out, mb, group=None):
+def encode_sharded(forward, pix_local, feats_all, local_out, mb, group=None, exposed=None):
     """forward(pix_chunk, out=chunk_out) computes one chunk; pix_local [n_local, ...] holds this rank's
     crops in local_crop_ids order; local_out [n_local, T, W] receives this rank's features and
-    feats_all [n_total, T, W] the gathered features of every rank.  Returns feats_all."""
+    feats_all [n_total, T, W] the gathered features of every rank.  Returns feats_all.
+    exposed: optional list; with more than one rank it gets a pair of CUDA events recorded on the current
+    stream around the final waits for the collectives, i.e. the all-gather time not hidden behind compute."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     n_local = pix_local.shape[0]
     if n_local % mb:
@@ -39,8 +41,14 @@ def encode_sharded(forward, pix_local, feats_all, local_out, mb, group=None):
         forward(pix_local[sl], out=local_out[sl])
         dst = feats_all[j * world * mb:(j + 1) * world * mb]
         works.append(dist.all_gather_into_tensor(dst, local_out[sl], group=group, async_op=True))
+    if exposed is not None and works:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
     for w in works:
         w.wait()
+    if exposed is not None and works:
+        e1.record()
+        exposed.append((e0, e1))
     return feats_all
 
 
