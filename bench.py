@@ -444,27 +444,33 @@ def frame_input_ms(dev, reps=20):
 
 
 def tapnext_frame_ms(dev, n_frames=16):
-    """Config 3 (the BASELINE simplification) and the full TAPNext++ block: 12 blocks, 1280 tokens, the
+    """Config 3 (the BASELINE simplification) and the full TAPNext++ step (blocks + tracking heads): 12 blocks,
+    1280 tokens, the
     state carried over n_frames frames of one video; mean ms per frame (CUDA events, 4 warm-up frames, so
     that every CUDA graph the engines replay -- one per history-ring position -- is captured before the
     timed frames; a video's first frame always runs eagerly)."""
     from strix_halo_maxx_b200.config import TAPNEXT
-    from strix_halo_maxx_b200.weights import tapnext_weights, tapnextpp_weights, tapnext_inputs
+    from strix_halo_maxx_b200.weights import tapnext_weights, tapnextpp_weights, tapnext_inputs, heads_weights
     from strix_halo_maxx_b200.tapnext import TapNextStep
     from strix_halo_maxx_b200.tapnextpp import TapNextPPStep
     frames, queries = tapnext_inputs(TAPNEXT, n_frames, seed=2)
     fr, qs = torch.from_numpy(frames).to(dev), torch.from_numpy(queries).to(dev)
     out = {}
     for name, cls, wfn in (("config3", TapNextStep, tapnext_weights), ("tapnextpp", TapNextPPStep, tapnextpp_weights)):
-        eng = cls(wfn(TAPNEXT, seed=9), TAPNEXT, device=dev)
+        if cls is TapNextPPStep:  # the reference's whole per-frame step: blocks + tracking heads (step8.py:316-325)
+            eng = cls(wfn(TAPNEXT, seed=9), TAPNEXT, device=dev, heads=heads_weights(TAPNEXT, seed=21))
+            run = eng.track
+        else:
+            eng = cls(wfn(TAPNEXT, seed=9), TAPNEXT, device=dev)
+            run = eng.step
         for f in range(4):
-            eng.step(fr[f], qs[f])
+            run(fr[f], qs[f])
         eng.reset()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for f in range(n_frames):
-            eng.step(fr[f], qs[f])
+            run(fr[f], qs[f])
         e1.record()
         torch.cuda.synchronize()
         out[name] = e0.elapsed_time(e1) / n_frames

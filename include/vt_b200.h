@@ -244,6 +244,26 @@ int vt_resize_pass_u8(cudaStream_t stream, const uint8_t* in, long long sa, long
                       long long oa, long long ob, long long oc, int n_out, int n_other, const int* bounds,
                       const int* weights, int ksize);
 
+/* TAPNext++ tracking heads (fp32 on the CUDA cores), the host heads of the reference: Step8.heads_np,
+ * tapnext/npu/step8.py:327-362 (numpy fp32; the torch form Step8.heads, step8.py:364-372).
+ * vt_head_linear: Y[M, N] fp32 = X[M, K] . Wt + bias, X bf16 (x_bf16) or fp32 with row pitch ldx, Wt fp32
+ *   [K][ldw] (the transposed nn.Linear weight, as heads_np's lin() stores it, step8.py:332-333), each output
+ *   summed over k in order.  Replaces the `x @ w + b` of heads_np's mlp (step8.py:341-342, 348). */
+int vt_head_linear(cudaStream_t stream, const void* X, long long ldx, int x_bf16, const float* Wt, long long ldw,
+                   const float* bias, float* Y, long long ldy, int M, int N, int K);
+
+/* In place per row of N (256 or 512) fp32 values: LayerNorm with gamma / beta group row % groups (two-pass
+ * statistics), then the exact GELU 0.5 y (1 + erf(y / sqrt 2)).  Replaces heads_np's LayerNorm + erf GELU,
+ * tapnext/npu/step8.py:343-347. */
+int vt_head_ln_gelu(cudaStream_t stream, float* Y, long long ldy, int rows, int N, const float* gamma,
+                    const float* beta, int groups, float eps);
+
+/* Soft-argmax tracks: per query q and axis a (bins 256 or 512 logits at logits[q][a * bins]), the softmax of
+ * logits * temperature restricted to +-window bins around the first maximum, renormalised; tracks[q][a] =
+ * its expectation over the bin indices + 0.5.  Replaces tapnext/npu/step8.py:352-361. */
+int vt_soft_argmax(cudaStream_t stream, const float* logits, long long ldl, int Q, int bins, int window,
+                   float temperature, float* tracks, long long ldt);
+
 #ifdef __cplusplus
 }
 #endif

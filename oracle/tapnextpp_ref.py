@@ -22,7 +22,9 @@ Two arithmetic levels:
     (tests/golden/make_golden_ssm.py).
 
 The vendored TAPNext model (model.py) is not in the repository, so the block as a whole is parity
-unpinned: only its recurrent element-wise part is pinned, by ssm_ref.
+unpinned: only its recurrent element-wise part is pinned, by ssm_ref.  heads() restates the host tracking
+heads (step8.py:327-362, heads_np) and is pinned to fixtures heads_np itself produced
+(tests/golden/make_golden_heads.py).
 """
 import math
 
@@ -136,3 +138,38 @@ def ssm_bf16(y, x, xm1, xm2, xm3, h0, conv_w, conv_b, a_param, wx, bx, wa, ba, f
         hb = f(h)
     z = f(hb * F32(y))
     return z, h
+
+
+def head_mlp(x, HW, name, eps):
+    """One tracking head (step8.py:341-348): (Linear, LayerNorm, erf GELU) twice, then the output Linear; fp32."""
+    for i, j in ((0, 1), (3, 4)):
+        h = linear(x, HW[f"{name}.{i}_w"], HW[f"{name}.{i}_b"])
+        mu = h.mean(-1, keepdim=True)
+        var = ((h - mu) ** 2).mean(-1, keepdim=True)
+        h = (h - mu) / torch.sqrt(var + eps) * _t(HW[f"{name}.{j}_w"]) + _t(HW[f"{name}.{j}_b"])
+        x = 0.5 * h * (1.0 + torch.erf(h * 0.7071067811865476))
+    return linear(x, HW[f"{name}.6_w"], HW[f"{name}.6_b"])
+
+
+def heads(x, HW, cfg):
+    """The TAPNext++ tracking heads on the query tokens x [Q, width] (step8.py:327-362): coordinate logits
+    [Q, 2 * bins] (y bins | x bins); per axis the softmax of logits * temperature, restricted to a window of
+    +-track_window bins around the argmax (the first maximum), renormalised, and its expectation over the bin
+    indices + 0.5 -> tracks [Q, 2] (y, x); the visibility logit [Q].  fp32 throughout."""
+    with torch.no_grad():
+        x = _t(x).float()
+        logits = head_mlp(x, HW, "coord", cfg.head_eps)
+        n = logits.shape[-1] // 2
+        idx = torch.arange(n, dtype=torch.float32)
+        out = []
+        for h in (logits[:, :n], logits[:, n:]):
+            am = h.argmax(-1, keepdim=True).float()
+            mask = (am - idx).abs() <= cfg.track_window
+            z = h * cfg.track_temperature
+            e = torch.exp(z - z.max(-1, keepdim=True).values)
+            pr = e / e.sum(-1, keepdim=True) * mask
+            pr = pr / pr.sum(-1, keepdim=True)
+            out.append((pr * idx).sum(-1))
+        tracks = torch.stack(out, -1) + 0.5
+        vis = head_mlp(x, HW, "vis", cfg.head_eps)[:, 0]
+        return tracks, logits, vis

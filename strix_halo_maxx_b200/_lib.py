@@ -30,6 +30,9 @@ SIGNATURES = {
     "vt_attn_tiles_bytes": (LL, [I, I, I, I]),
     "vt_attn_pack": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL]),
     "vt_attn_tiles_fwd": (I, [P, P, P, I, I, I, I, LL, LL, LL, F]),
+    "vt_head_linear": (I, [P, P, LL, I, P, LL, P, P, LL, I, I, I]),
+    "vt_head_ln_gelu": (I, [P, P, LL, I, I, P, P, I, F]),
+    "vt_soft_argmax": (I, [P, P, LL, I, I, I, F, P, LL]),
     "vt_attn_fwd_noalloc": (I, [P, P, P, P, P, I, I, I, I, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, LL, F]),
     "vt_layernorm": (I, [P, P, LL, I, P, P, P, LL, I, I, I, F]),
     "vt_rmsnorm": (I, [P, P, LL, I, P, P, LL, I, I, I, F]),

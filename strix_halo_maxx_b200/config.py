@@ -62,6 +62,14 @@ class TapNextConfig:
     n_queries: int = 256
     eps: float = 1e-6
     lru_c: float = 8.0          # a = sigmoid(-a_param) ** (c * r_t)
+    # tracking heads on the query tokens (the reference's model.coordinate_head / visible_head, run on the
+    # host by tapnext/npu/step8.py:327-362): Linear width -> head_hidden, LN, GELU, Linear, LN, GELU, Linear
+    # -> 2 x track_bins coordinate logits (y bins | x bins) or 1 visibility logit; soft-argmax window +-20
+    head_hidden: int = 256
+    track_bins: int = 256
+    track_window: int = 20
+    track_temperature: float = 0.5
+    head_eps: float = 1e-6
 
     @property
     def grid(self) -> int:

@@ -9,3 +9,4 @@
 #include "ssm.cu"
 #include "text.cu"
 #include "resize.cu"
+#include "heads.cu"

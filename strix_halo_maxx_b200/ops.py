@@ -383,3 +383,31 @@ def attn_causal(q, kc, vc, pos0, out, scale=None):
                               out.data_ptr(), out.stride(0))
     check(rc, "vt_attn_causal")
     return out
+
+
+def head_linear(x2, wt, bias, out):
+    """out [M, N] fp32 = x2 [M, K] (bf16 or fp32, unit column stride) . wt [K, N] fp32 + bias (vt_head_linear)."""
+    M, K = x2.shape
+    N = out.shape[1]
+    rc = lib().vt_head_linear(_stream(), x2.data_ptr(), x2.stride(0), int(x2.dtype == BF16), wt.data_ptr(), wt.stride(0),
+                              _ptr(bias), out.data_ptr(), out.stride(0), M, N, K)
+    check(rc, "vt_head_linear")
+    return out
+
+
+def head_ln_gelu(y2, gamma, beta, eps):
+    """In place on y2 [rows, N] fp32: LayerNorm (gamma / beta [groups, N], row r uses group r % groups) then the
+    exact GELU (vt_head_ln_gelu)."""
+    rows, N = y2.shape
+    rc = lib().vt_head_ln_gelu(_stream(), y2.data_ptr(), y2.stride(0), rows, N, gamma.data_ptr(), beta.data_ptr(),
+                               gamma.shape[0], float(eps))
+    check(rc, "vt_head_ln_gelu")
+    return y2
+
+
+def soft_argmax(logits, bins, window, temperature, tracks):
+    """tracks [Q, 2] = windowed soft-argmax of logits [Q, 2 * bins] per axis (vt_soft_argmax)."""
+    rc = lib().vt_soft_argmax(_stream(), logits.data_ptr(), logits.stride(0), logits.shape[0], int(bins), int(window),
+                              float(temperature), tracks.data_ptr(), tracks.stride(0))
+    check(rc, "vt_soft_argmax")
+    return tracks

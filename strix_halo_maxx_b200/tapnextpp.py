@@ -11,7 +11,8 @@ Per block, in the reference's order:
     x  += (gelu_tanh(gate) * up) Wdown^T + bdown       vt_gated_gelu_mul, vt_gemm + residual
     x  += MHA(LN_1(x))                                 the tower's qkv-tile GEMM + tcgen05 attention (d 64)
     x  += gelu_erf(LN_2(x) W0^T + b0) W3^T + b3        vt_gemm, vt_gelu_erf, vt_gemm + residual
-and the encoder LayerNorm after the last block.  The recurrent state (h fp32 and the last three xx of every
+and the encoder LayerNorm after the last block, then (with heads=) the tracking heads on the query tokens
+(TrackHeads; the reference's host heads, step8.py:327-362).  The recurrent state (h fp32 and the last three xx of every
 block) lives on the device, owned by this object; reset() starts a new video.
 
 A frame is ~200 kernel launches, more host time than the B200 needs to run them, so with graphs=True
@@ -31,8 +32,57 @@ from .tower import _dev_mat, _dev_vec
 F32 = torch.float32
 
 
+class TrackHeads:
+    """The tracking heads on the query tokens, on the device in fp32 (the reference runs them on the host after
+    every frame: Step8.heads_np, tapnext/npu/step8.py:327-362).  Per head: Linear width -> hidden, LayerNorm,
+    erf GELU, Linear hidden -> hidden, LayerNorm, erf GELU, Linear -> 2 x bins coordinate logits (y | x) or one
+    visibility logit; then per axis the soft-argmax over +-window bins of the first maximum at the temperature,
+    + 0.5.  The two heads' first Linear run as one [width, 2 hidden] product and their LayerNorms as one pass.
+    HW: weights as strix_halo_maxx_b200.weights.heads_weights names them ([out, in], torch's layout).
+    __call__(x [Q, width] bf16) -> (tracks [Q, 2], logits [Q, 2 bins], vis [Q]) fp32 views of buffers this
+    object owns (valid until the next call)."""
+
+    def __init__(self, HW, cfg: TapNextConfig = TAPNEXT, device="cuda", n_queries=None):
+        self.cfg = cfg
+        dev = torch.device(device)
+        Q = cfg.n_queries if n_queries is None else n_queries
+        Hh, nb = cfg.head_hidden, cfg.track_bins
+        t = lambda name: torch.as_tensor(HW[name]).float()                          # noqa: E731
+        wt = lambda name: t(name).t().contiguous().to(dev)                         # noqa: E731 [in, out]
+        self.w0 = torch.cat([t("coord.0_w").t(), t("vis.0_w").t()], 1).contiguous().to(dev)   # [width, 2 Hh]
+        self.b0 = torch.cat([t("coord.0_b"), t("vis.0_b")]).to(dev)
+        self.g1 = torch.stack([t("coord.1_w"), t("vis.1_w")]).to(dev)
+        self.be1 = torch.stack([t("coord.1_b"), t("vis.1_b")]).to(dev)
+        self.w3c, self.w3v = wt("coord.3_w"), wt("vis.3_w")
+        self.b3c, self.b3v = t("coord.3_b").to(dev), t("vis.3_b").to(dev)
+        self.g4 = torch.stack([t("coord.4_w"), t("vis.4_w")]).to(dev)
+        self.be4 = torch.stack([t("coord.4_b"), t("vis.4_b")]).to(dev)
+        self.w6c, self.w6v = wt("coord.6_w"), wt("vis.6_w")                        # [Hh, 2 nb], [Hh, 1]
+        self.b6c, self.b6v = t("coord.6_b").to(dev), t("vis.6_b").to(dev)
+        self.y1 = torch.empty(Q, 2 * Hh, dtype=F32, device=dev)                    # [coord | vis] per query
+        self.y2 = torch.empty(Q, 2 * Hh, dtype=F32, device=dev)
+        self.logits = torch.empty(Q, 2 * nb, dtype=F32, device=dev)
+        self.vis = torch.empty(Q, 1, dtype=F32, device=dev)
+        self.tracks = torch.empty(Q, 2, dtype=F32, device=dev)
+
+    def __call__(self, x):
+        cfg = self.cfg
+        Q, Hh = x.shape[0], cfg.head_hidden
+        assert Q <= self.y1.shape[0]
+        y1, y2, lg, vis, tr = self.y1[:Q], self.y2[:Q], self.logits[:Q], self.vis[:Q], self.tracks[:Q]
+        ops.head_linear(x, self.w0, self.b0, y1)
+        ops.head_ln_gelu(y1.view(2 * Q, Hh), self.g1, self.be1, cfg.head_eps)
+        ops.head_linear(y1[:, :Hh], self.w3c, self.b3c, y2[:, :Hh])
+        ops.head_linear(y1[:, Hh:], self.w3v, self.b3v, y2[:, Hh:])
+        ops.head_ln_gelu(y2.view(2 * Q, Hh), self.g4, self.be4, cfg.head_eps)
+        ops.head_linear(y2[:, :Hh], self.w6c, self.b6c, lg)
+        ops.head_linear(y2[:, Hh:], self.w6v, self.b6v, vis)
+        ops.soft_argmax(lg, cfg.track_bins, cfg.track_window, cfg.track_temperature, tr)
+        return tr, lg, vis[:, 0]
+
+
 class TapNextPPStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, heads=None):
         self.cfg = cfg
         self.use_graphs = graphs
         self._graphs = {}
@@ -79,6 +129,8 @@ class TapNextPPStep:
         self.h = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
         self.hist = torch.zeros(self.n_blocks, 3, T, Wd, dtype=BF16, device=dev)
         self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
+        # optional tracking heads (weights as weights.heads_weights): run on the query tokens inside the step
+        self.heads = TrackHeads(heads, cfg, dev) if heads is not None else None
         self.reset()
 
     def reset(self):
@@ -104,6 +156,16 @@ class TapNextPPStep:
             g.replay()
         self.frame += 1
         return self.out
+
+    def track(self, frame, queries):
+        """The reference's Step8.step (tapnext/npu/step8.py:316-325): one frame, then the heads on the query
+        tokens -> (tracks [Q, 2], logits [Q, 2 bins], visibility logits [Q], query tokens [Q, width] bf16).
+        Needs heads= at construction; the heads run inside the step (and its CUDA graph)."""
+        assert self.heads is not None, "TapNextPPStep(heads=...) is needed for tracks"
+        out = self.step(frame, queries)
+        h = self.heads
+        Q = self.cfg.n_queries
+        return h.tracks[:Q], h.logits[:Q], h.vis[:Q, 0], out[self.cfg.n_img_tok:]
 
     def _run(self, frame, queries, k, first):
         cfg = self.cfg
@@ -136,3 +198,5 @@ class TapNextPPStep:
             ops.gelu_erf(self.f)
             ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+        if self.heads is not None:
+            self.heads(self.out[NI:])

@@ -20,6 +20,8 @@ def _draw(seed, idx, shape, kind, affine):
         return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
     if kind == "normal1":
         return rng.standard_normal(shape, dtype=np.float32)
+    if kind == "wout":  # last layer of a tracking head: wider, so the soft-argmax sees peaked logits
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.25)
     if kind == "conv":  # temporal conv taps
         return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.5)
     if kind == "scale":  # RMSNorm scale of the (1 + scale) convention
@@ -124,6 +126,31 @@ def tapnextpp_spec(cfg: TapNextConfig, n_blocks=None):
 
 def tapnextpp_weights(cfg: TapNextConfig, seed=0, n_blocks=None, affine="zero"):
     return _generate(tapnextpp_spec(cfg, n_blocks), seed, affine)
+
+
+def heads_spec(cfg: TapNextConfig):
+    """The TAPNext++ tracking heads (model.coordinate_head / visible_head, indexed as step8.py:335 reads them:
+    [0] Linear, [1] LayerNorm, [3] Linear, [4] LayerNorm, [6] Linear): weights [out, in] as torch stores them."""
+    W, Hh, nb = cfg.width, cfg.head_hidden, cfg.track_bins
+    s = []
+    for name, n_out in (("coord", 2 * nb), ("vis", 1)):
+        s += [(f"{name}.0_w", (Hh, W), "w"), (f"{name}.0_b", (Hh,), "bias"),
+              (f"{name}.1_w", (Hh,), "gamma"), (f"{name}.1_b", (Hh,), "beta"),
+              (f"{name}.3_w", (Hh, Hh), "w"), (f"{name}.3_b", (Hh,), "bias"),
+              (f"{name}.4_w", (Hh,), "gamma"), (f"{name}.4_b", (Hh,), "beta"),
+              (f"{name}.6_w", (n_out, Hh), "wout"), (f"{name}.6_b", (n_out,), "bias")]
+    return s
+
+
+def heads_weights(cfg: TapNextConfig, seed=0, affine="random"):
+    return _generate(heads_spec(cfg), seed, affine)
+
+
+def heads_input(cfg: TapNextConfig, seed=11, n=None):
+    """Query tokens for the heads, N(0, 1) [n_queries, width] float32 (the GPU path feeds them as bf16; callers
+    that compare against it round them to bf16 first)."""
+    n = cfg.n_queries if n is None else n
+    return np.random.default_rng(np.random.SeedSequence([int(seed), 0])).standard_normal((n, cfg.width), dtype=np.float32)
 
 
 def text_spec(cfg, n_layers=None):

@@ -131,6 +131,36 @@ def test_rglru_restatement_detects_a_planted_error(plant):
     assert max(_rglru_stream(W, frames, c)) > 10 * RGLRU_TOL
 
 
+def _heads_case():
+    from strix_halo_maxx_b200.config import TAPNEXT
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "heads_ref_cases.npz"))
+    HW = wg.heads_weights(TAPNEXT, seed=int(g["wseed"]))
+    x = torch.from_numpy(wg.heads_input(TAPNEXT, seed=int(g["xseed"]))).to(torch.bfloat16).float()
+    return TAPNEXT, HW, x, g
+
+
+def test_heads_restatement_matches_reference_heads_np():
+    """oracle.tapnextpp_ref.heads against the reference's own Step8.heads_np (tapnext/npu/step8.py:327-362,
+    tests/golden/make_golden_heads.py): logits, tracks and visibility, fp32 against fp32."""
+    from oracle import tapnextpp_ref
+    cfg, HW, x, g = _heads_case()
+    tracks, logits, vis = tapnextpp_ref.heads(x, HW, cfg)
+    assert np.allclose(logits.numpy(), g["logits"], rtol=1e-4, atol=1e-4)
+    assert np.abs(tracks.numpy() - g["tracks"]).max() < 1e-3          # pixels
+    assert np.allclose(vis.numpy(), g["vis"], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("plant", ["window_10", "temperature_1"])
+def test_heads_restatement_detects_a_planted_error(plant):
+    """The fixture rejects a soft-argmax window of +-10 bins and a temperature of 1 (instead of +-20, 0.5)."""
+    import dataclasses
+    from oracle import tapnextpp_ref
+    cfg, HW, x, g = _heads_case()
+    bad = dataclasses.replace(cfg, track_window=10) if plant == "window_10" else dataclasses.replace(cfg, track_temperature=1.0)
+    tracks, _, _ = tapnextpp_ref.heads(x, HW, bad)
+    assert np.abs(tracks.numpy() - g["tracks"]).max() > 0.1
+
+
 def _text_case():
     from strix_halo_maxx_b200.config import TEXT
     from oracle import text_ref

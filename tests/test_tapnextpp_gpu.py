@@ -101,3 +101,49 @@ def test_tapnextpp_graph_replay_matches_eager():
         fr, q = torch.from_numpy(frames[f]).to(DEV), torch.from_numpy(queries[f]).to(DEV)
         assert torch.equal(eg.step(fr, q), ee.step(fr, q)), f"frame {f}"
     assert sorted(eg._graphs) == [0, 1, 2]
+
+
+def _heads_fixture():
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "heads_ref_cases.npz"))
+    HW = wg.heads_weights(CFG, seed=int(g["wseed"]))
+    x = torch.from_numpy(wg.heads_input(CFG, seed=int(g["xseed"]))).to(BF)
+    return HW, x, g
+
+
+def test_track_heads_against_reference_heads_np():
+    """TrackHeads (fp32 kernels) on the fixture's query tokens against the reference's own Step8.heads_np
+    outputs (tests/golden/heads_ref_cases.npz): tracks within 1e-3 px, logits and visibility within 1e-4."""
+    from strix_halo_maxx_b200.tapnextpp import TrackHeads
+    device_status(clear=True)
+    HW, x, g = _heads_fixture()
+    heads = TrackHeads(HW, CFG, DEV)
+    tracks, logits, vis = heads(x.to(DEV))
+    torch.cuda.synchronize()
+    assert np.abs(tracks.cpu().numpy() - g["tracks"]).max() < 1e-3
+    assert np.allclose(logits.cpu().numpy(), g["logits"], rtol=1e-4, atol=1e-4)
+    assert np.allclose(vis.cpu().numpy(), g["vis"], rtol=1e-4, atol=1e-4)
+    # a partial query block (37 rows) takes the same per-row path
+    t37, _, v37 = heads(x[:37].to(DEV))
+    assert np.abs(t37.cpu().numpy() - g["tracks"][:37]).max() < 1e-3
+    assert np.allclose(v37.cpu().numpy(), g["vis"][:37], rtol=1e-4, atol=1e-4)
+    assert device_status(clear=True) == 0
+
+
+def test_tapnextpp_track_runs_the_heads_inside_the_step():
+    """TapNextPPStep(heads=...).track: the tracks of frames replayed from the CUDA graph equal TrackHeads run on
+    the step's own query tokens, and the oracle heads of those tokens (CPU fp32) within 1e-3 px."""
+    from strix_halo_maxx_b200.tapnextpp import TrackHeads
+    W = wg.tapnextpp_weights(CFG, seed=8, n_blocks=2, affine="random")
+    HW = wg.heads_weights(CFG, seed=21)
+    frames, queries = wg.tapnext_inputs(CFG, 3, seed=4)
+    eng = TapNextPPStep(W, CFG, device=DEV, heads=HW)
+    ref_heads = TrackHeads(HW, CFG, DEV)
+    for f in range(3):
+        tracks, logits, vis, xq = eng.track(torch.from_numpy(frames[f]).cuda(), torch.from_numpy(queries[f]).cuda())
+        t2, l2, v2 = ref_heads(xq)
+        assert torch.equal(tracks, t2) and torch.equal(logits, l2) and torch.equal(vis, v2), f"frame {f}"
+        rt, rl, rv = R.heads(xq.float().cpu(), HW, CFG)
+        assert float((tracks.cpu() - rt).abs().max()) < 1e-3, f"frame {f}"
+        assert torch.allclose(vis.cpu(), rv, rtol=1e-4, atol=1e-4)
+    assert len(eng._graphs) == 2
