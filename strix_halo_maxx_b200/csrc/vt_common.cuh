@@ -21,6 +21,7 @@ enum : unsigned int {
   ST_ATTN_PRODUCER = 1u << 4,
   ST_ATTN_MMA = 1u << 5,
   ST_ATTN_SOFTMAX = 1u << 6,
+  ST_SSM_MMA = 1u << 7,
 };
 // A wait gives up after this many SM clock cycles (~2 s at 1.9 GHz); legitimate waits are microseconds.
 constexpr long long kSpinCycles = 4000000000LL;
@@ -316,6 +317,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 32 lanes x 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 
 // Non-tensor bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completion
 // counted on the mbarrier; it fills only the issuing CTA.
