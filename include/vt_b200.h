@@ -186,6 +186,22 @@ int vt_im2col(cudaStream_t stream, const void* pix, int kind, int B, int C, int 
 int vt_crop_combine(cudaStream_t stream, const uint16_t* f, long long crop_stride, long long ldf, int n_crops, int T,
                     int W, uint16_t* out, long long ldo);
 
+/* RMSNorm statistics for an RMSNorm folded into the GEMM after it: out[m] = (0, 1 / sqrt(mean over the row of
+ * x^2 + eps)) from the per-32-column chunk statistics (mean, M2) [M][nchunk] that vt_rowstats or a residual
+ * GEMM epilogue wrote; fp32.  The ln input of vt_gemm_fused then applies rstd * acc + bias (mean 0).
+ * Replaces: the statistics half of the temporal pre-norm (RMSNorm), tapnext/npu/step8.py:474. */
+int vt_row_rms(cudaStream_t stream, const float* stats, int M, int nchunk, float eps, float* out);
+
+/* vt_rglru with the temporal RMSNorm folded into the gate GEMM before it: G = [gx_pre | ga_pre] fp32 from a GEMM
+ * whose A was the bf16 copy of x and whose weights carry the RMSNorm gamma; the recurrence's input
+ * t = bf16(x * rstd * gamma) is formed here from the fp32 stream x and rms_moments [M][2] (vt_row_rms).
+ * Updates state and x (x += h) in place and writes the bf16 copy xb of the new x and its per-32-column chunk
+ * statistics stats [M][W/32][2] (mean, M2) for the next block's folded LayerNorm.  W % 32 == 0.
+ * Replaces: the RG-LRU step of tapnext/npu/r9/cpuemu.py:33-47 with its pre-norm (step8.py:474-479). */
+int vt_rglru_fold(cudaStream_t stream, const float* G, long long ldg, const float* a_param, const float* rms_moments,
+                  const float* rms_gamma, float* state, long long lds, float* x, long long ldx, uint16_t* xb,
+                  long long ldxb, float* stats, int M, int W, float c, int first);
+
 /* RG-LRU recurrence step over M tokens of width W on the bf16 input u (the normalised stream):
  * G = [gx_pre | ga_pre] fp32; state and the residual stream x fp32, updated in place (state <- h,
  * x <- x + h); first != 0 starts a sequence.

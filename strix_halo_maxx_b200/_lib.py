@@ -38,6 +38,8 @@ SIGNATURES = {
     "vt_rmsnorm": (I, [P, P, LL, I, P, P, LL, I, I, I, F]),
     "vt_im2col": (I, [P, P, I, I, I, I, I, P, LL]),
     "vt_crop_combine": (I, [P, P, LL, LL, I, I, I, P, LL]),
+    "vt_row_rms": (I, [P, P, I, I, F, P]),
+    "vt_rglru_fold": (I, [P, P, LL, P, P, P, P, LL, P, LL, P, LL, P, I, I, F, I]),
     "vt_rglru": (I, [P, P, LL, P, P, LL, P, LL, P, LL, I, I, F, I]),
     "vt_ssm_step": (I, [P, P, P, LL, P, P, P, LL, P, LL, P, P, P, P, P, P, P, P, LL, I, I, I]),
     "vt_gated_gelu_mul": (I, [P, P, LL, P, LL, I, I]),

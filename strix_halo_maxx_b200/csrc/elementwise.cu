@@ -176,24 +176,38 @@ __global__ void __launch_bounds__(256) rowstats_kernel(const float* __restrict__
 }
 
 // (mean, 1/sqrt(var + eps)) of every row from its nchunk per-32-column (mean, M2) pairs, merged with
-// Chan's parallel formula (equal chunk counts): one thread per row.
+// Chan's parallel formula (equal chunk counts).
+// RMS = true: (0, 1 / sqrt(mean(x^2) + eps)) instead, the sum of squares merged from the same chunk statistics
+// (sum over chunks of M2 + 32 mean^2) -- the RMSNorm of the TAPNext temporal block folded into its gate GEMM.
+// A warp per row: lane j reads chunks j and j + 32 (coalesced, nchunk <= 64) and the sums go through a fixed
+// shuffle tree, so a row's result does not depend on M or on the other rows.
+template <bool RMS>
 __global__ void __launch_bounds__(256) row_moments_kernel(const float2* __restrict__ stats, int nchunk, int M,
                                                           float eps, float2* __restrict__ out) {
   griddep_wait();  // programmatic dependent launch: the previous kernel has completed
   griddep_launch();
-  for (long long m = (long long)blockIdx.x * blockDim.x + threadIdx.x; m < M; m += (long long)gridDim.x * blockDim.x) {
-    const float2* st = stats + m * nchunk;
-    float s = 0.f;
-    for (int j = 0; j < nchunk; j++) s += st[j].x;
-    const float mu = s / (float)nchunk;
-    float m2 = 0.f;
-    for (int j = 0; j < nchunk; j++) {
-      const float2 v = st[j];
-      const float d = v.x - mu;
-      m2 += v.y + 32.f * d * d;
-    }
-    out[m] = make_float2(mu, rsqrtf(m2 / (32.f * (float)nchunk) + eps));
+  const int lane = threadIdx.x & 31;
+  const long long m = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const float2* st = stats + m * nchunk;
+  const float2 z = make_float2(0.f, 0.f);
+  const float2 v0 = lane < nchunk ? st[lane] : z, v1 = lane + 32 < nchunk ? st[lane + 32] : z;
+  if (RMS) {
+    float q = (v0.y + 32.f * v0.x * v0.x) + (v1.y + 32.f * v1.x * v1.x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) out[m] = make_float2(0.f, rsqrtf(q / (32.f * (float)nchunk) + eps));
+    return;
   }
+  float s = v0.x + v1.x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mu = s / (float)nchunk;
+  const float d0 = v0.x - mu, d1 = v1.x - mu;
+  float m2 = (lane < nchunk ? v0.y + 32.f * d0 * d0 : 0.f) + (lane + 32 < nchunk ? v1.y + 32.f * d1 * d1 : 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
+  if (lane == 0) out[m] = make_float2(mu, rsqrtf(m2 / (32.f * (float)nchunk) + eps));
 }
 
 // Patch im2col: pixels -> A[m, k] (bf16, pitch ldo) with m = crop*g*g + gy*g + gx and
@@ -303,6 +317,74 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
     }
     *reinterpret_cast<float4*>(state + m * lds + n) = make_float4(hv[0], hv[1], hv[2], hv[3]);
     *reinterpret_cast<float4*>(x + m * ldx + n) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+  }
+}
+
+// The RG-LRU step with the temporal RMSNorm folded into the gate GEMM (TAPNext-style step, fold_ln): G holds
+// rstd * (bf16(x) . (W gamma)^T) + b; the normed input the recurrence gates, t = bf16(x * rstd * gamma), is
+// formed here from the fp32 stream.  Besides state and x += h it writes the bf16 copy of the new x and its
+// per-32-column (mean, M2) statistics, the inputs of the next block's folded LayerNorm.  Thread = 4 columns;
+// the 8 threads of a 32-column chunk are consecutive lanes (W % 32 == 0), so a chunk's statistics are a
+// shuffle reduction over 8 lanes, and every lane of a warp runs the same number of iterations.
+__global__ void __launch_bounds__(256) rglru_fold_kernel(const float* G, long long ldg, const float* a_param,
+                                                         const float2* __restrict__ mom, const float* __restrict__ rms_g,
+                                                         float* state, long long lds, float* x, long long ldx,
+                                                         uint16_t* __restrict__ xb, long long ldxb,
+                                                         float2* __restrict__ stats, int M, int W, float c, int first) {
+  griddep_wait();  // programmatic dependent launch: the previous kernel has completed
+  griddep_launch();
+  const int nv = W / 4, nch = W / 32;
+  const long long total = (long long)M * nv;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i - (threadIdx.x & 31) < total; i += stride) {
+    const bool valid = i < total;  // whole 8-lane groups are valid or not (nv % 8 == 0)
+    float xv[4] = {0.f, 0.f, 0.f, 0.f};
+    long long m = 0;
+    int n = 0;
+    if (valid) {
+      m = i / nv;
+      n = (int)(i % nv) * 4;
+      const float4 gx4 = *reinterpret_cast<const float4*>(G + m * ldg + n);
+      const float4 ga4 = *reinterpret_cast<const float4*>(G + m * ldg + W + n);
+      const float4 ap4 = *reinterpret_cast<const float4*>(a_param + n);
+      const float4 rg4 = *reinterpret_cast<const float4*>(rms_g + n);
+      const float4 x4 = *reinterpret_cast<const float4*>(x + m * ldx + n);
+      const float4 h4 = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(state + m * lds + n);
+      const float rstd = mom[m].y;
+      const float gx[4] = {gx4.x, gx4.y, gx4.z, gx4.w}, ga[4] = {ga4.x, ga4.y, ga4.z, ga4.w};
+      const float ap[4] = {ap4.x, ap4.y, ap4.z, ap4.w}, rg[4] = {rg4.x, rg4.y, rg4.z, rg4.w};
+      const float hv0[4] = {h4.x, h4.y, h4.z, h4.w};
+      xv[0] = x4.x, xv[1] = x4.y, xv[2] = x4.z, xv[3] = x4.w;
+      float hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float u = bfround(xv[e] * rstd * rg[e]);  // the RMSNorm output, bf16 as the unfolded path stores it
+        const float gated = u * sigmoidf_(gx[e]);
+        float h;
+        if (first) {
+          h = gated;
+        } else {
+          const float log_a = -c * sigmoidf_(ga[e]) * softplusf_(ap[e]);
+          h = expf(log_a) * hv0[e] + gated * sqrtf(-expm1f(2.0f * log_a));
+        }
+        hv[e] = h;
+        xv[e] += h;
+      }
+      *reinterpret_cast<float4*>(state + m * lds + n) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<float4*>(x + m * ldx + n) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+      *reinterpret_cast<uint2*>(xb + m * ldxb + n) = make_uint2(pack_bf2(xv[0], xv[1]), pack_bf2(xv[2], xv[3]));
+    }
+    // chunk statistics of the new x: mean, then the sum of squared deviations, over the chunk's 8 lanes
+    float sm = (xv[0] + xv[1]) + (xv[2] + xv[3]);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    const float mean = sm * (1.f / 32.f);
+    float q = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; e++) q = fmaf(xv[e] - mean, xv[e] - mean, q);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (valid && (threadIdx.x & 7) == 0) stats[m * nch + n / 32] = make_float2(mean, q);
   }
 }
 
@@ -418,8 +500,16 @@ __global__ void __launch_bounds__(256) norm_row_kernel(const void* x, long long 
   }
 }
 
-// Rows below which the CTA-per-row kernel runs (the warp-per-row kernel fills 148 SMs x 2 CTAs x 8 rows).
-constexpr int kRowKernelMaxM = 2368;
+// Rows below which the CTA-per-row kernel runs (measured: 730 x 2048 rows 3.4 us against 6.4 us warp per row;
+// 1280 x 768 rows 3.7 us against 3.4 us);
+// VT_LN_ROW_MAX overrides it (tuning switch).
+static int row_kernel_max_m() {
+  static const int v = [] {
+    const char* e = getenv("VT_LN_ROW_MAX");
+    return e ? atoi(e) : 1024;
+  }();
+  return v;
+}
 
 static int grid_for(long long work, int threads) {
   long long g = (work + threads - 1) / threads;
@@ -440,7 +530,7 @@ static int norm_launch(const char* what, cudaStream_t st, const void* x, long lo
     return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
-  if (M < kRowKernelMaxM) {
+  if (M < row_kernel_max_m()) {
     const int g = (N / 4 + 255) / 256;
 #define VT_LNR(G)                                                                                                  \
   launch_k(norm_row_kernel<G, RMS, false>, (unsigned)M, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, out_f32, N, \
@@ -477,7 +567,7 @@ static int ln_quant_launch(cudaStream_t st, const void* x, long long ldx, int in
     return set_error(E_SHAPE, "%s: pitches / alignment invalid", what);
   const long long blocks = ((long long)M + 7) / 8;
   if (blocks > 0x7fffffffLL) return set_error(E_SHAPE, "%s: M too large", what);
-  if (M < kRowKernelMaxM) {
+  if (M < row_kernel_max_m()) {
     const int g = (N / 4 + 255) / 256;
 #define VT_LNQR(G)                                                                                                  \
   launch_k(norm_row_kernel<G, false, true>, (unsigned)M, 256, 0, st, x, ldx, in_bf16, gamma, beta, y, ldy, 0, N, eps, \
@@ -549,7 +639,8 @@ int vt_row_moments(cudaStream_t st, const float* stats, int M, int nchunk, float
   if (M == 0) return OK;
   if (!stats || !moments || (reinterpret_cast<uintptr_t>(stats) & 7) || (reinterpret_cast<uintptr_t>(moments) & 7))
     return set_error(E_SHAPE, "vt_row_moments: pointers must be 8-byte aligned");
-  launch_k(ew::row_moments_kernel, ew::grid_for(M, 256), 256, 0, st, reinterpret_cast<const float2*>(stats), nchunk, M, eps,
+  if (nchunk > 64) return set_error(E_SHAPE, "vt_row_moments: at most 64 chunks (2048 columns)");
+  launch_k(ew::row_moments_kernel<false>, (unsigned)((M + 7) / 8), 256, 0, st, reinterpret_cast<const float2*>(stats), nchunk, M, eps,
                                                                reinterpret_cast<float2*>(moments));
   return check_launch("vt_row_moments");
 }
@@ -582,6 +673,36 @@ int vt_crop_combine(cudaStream_t st, const uint16_t* f, long long crop_stride, l
 
 // RG-LRU step over M tokens of width W on the bf16 input u; G = [gx_pre | ga_pre] fp32 [M][ldg >= 2W];
 // state and x fp32, updated in place; first != 0 starts a new sequence (state ignored and overwritten).
+int vt_row_rms(cudaStream_t st, const float* stats, int M, int nchunk, float eps, float* out) {
+  using namespace vt;
+  if (M < 0 || nchunk <= 0) return set_error(E_SHAPE, "vt_row_rms: bad shape");
+  if (M == 0) return OK;
+  if (!stats || !out) return set_error(E_SHAPE, "vt_row_rms: null pointer");
+  if (nchunk > 64) return set_error(E_SHAPE, "vt_row_rms: at most 64 chunks (2048 columns)");
+  launch_k(ew::row_moments_kernel<true>, (unsigned)((M + 7) / 8), 256, 0, st, reinterpret_cast<const float2*>(stats), nchunk, M,
+           eps, reinterpret_cast<float2*>(out));
+  return check_launch("vt_row_rms");
+}
+
+int vt_rglru_fold(cudaStream_t st, const float* G, long long ldg, const float* a_param, const float* rms_moments,
+                  const float* rms_gamma, float* state, long long lds, float* x, long long ldx, uint16_t* xb,
+                  long long ldxb, float* stats, int M, int W, float c, int first) {
+  using namespace vt;
+  if (M < 0 || W <= 0 || W % 32) return set_error(E_SHAPE, "vt_rglru_fold: W must be a positive multiple of 32");
+  if (M == 0) return OK;
+  if (!G || !a_param || !rms_moments || !rms_gamma || !state || !x || !xb || !stats)
+    return set_error(E_SHAPE, "vt_rglru_fold: null pointer");
+  if (ldg < 2LL * W || lds < W || ldx < W || ldxb < W || ldg % 4 || lds % 4 || ldx % 4 || ldxb % 4 || !aligned16(G) ||
+      !aligned16(a_param) || !aligned16(rms_gamma) || !aligned16(state) || !aligned16(x) ||
+      (reinterpret_cast<uintptr_t>(xb) & 7) || (reinterpret_cast<uintptr_t>(rms_moments) & 7) ||
+      (reinterpret_cast<uintptr_t>(stats) & 7))
+    return set_error(E_SHAPE, "vt_rglru_fold: pitches / alignment invalid");
+  launch_k(ew::rglru_fold_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, a_param,
+           reinterpret_cast<const float2*>(rms_moments), rms_gamma, state, lds, x, ldx, xb, ldxb,
+           reinterpret_cast<float2*>(stats), M, W, c, first);
+  return check_launch("vt_rglru_fold");
+}
+
 int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_param, const uint16_t* u, long long ldu,
              float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first) {
   using namespace vt;

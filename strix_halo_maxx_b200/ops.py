@@ -183,6 +183,24 @@ def row_moments(stats, eps, out):
     return out
 
 
+def row_rms(stats, eps, out):
+    """(0, rstd) per row [M, 2] of an RMSNorm from chunk statistics [M, nchunk, 2] (vt_row_rms)."""
+    M, nchunk = stats.shape[0], stats.shape[1]
+    rc = lib().vt_row_rms(_stream(), stats.data_ptr(), M, nchunk, float(eps), out.data_ptr())
+    check(rc, "vt_row_rms")
+    return out
+
+
+def rglru_fold(G, a_param, rms_moments, rms_gamma, state, x, xb, stats, c, first):
+    """RG-LRU step with its RMSNorm folded into the gate GEMM (vt_rglru_fold): state, x updated in place; xb and
+    stats receive the bf16 copy and chunk statistics of the new x."""
+    M, W = x.shape
+    rc = lib().vt_rglru_fold(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), rms_moments.data_ptr(),
+                             rms_gamma.data_ptr(), state.data_ptr(), state.stride(0), x.data_ptr(), x.stride(0),
+                             xb.data_ptr(), xb.stride(0), stats.data_ptr(), M, W, float(c), int(bool(first)))
+    check(rc, "vt_rglru_fold")
+
+
 def fold_layernorm(w, b, gamma, beta):
     """Weights of a linear with the preceding LayerNorm's affine folded in: (bf16 W * diag(gamma),
     fp32 c = row sums of that bf16 matrix, fp32 b + W beta).  w [N, K], b [N], gamma / beta [K] (fp32)."""

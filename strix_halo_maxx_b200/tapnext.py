@@ -6,11 +6,18 @@ and the encoder LayerNorm.  The RG-LRU (tapnext/npu/r9/cpuemu.py:33-47) keeps on
 [1280, 768] per block, carried across frames in device memory owned by this object; reset() starts a
 new video.
 
-Per block the kernels are the tower's (vt_layernorm, vt_gemm_ex, vt_gemm_qkv_tiles + vt_attn_tiles_fwd
-with d = 64) plus:
-    t   = RMSNorm(x)                        vt_rmsnorm, bf16 out
-    G   = t . [Wx; Wa]^T + [bx; ba]         one vt_gemm_ex, N = 1536, fp32 out
-    vt_rglru(G, a_param, t, state_i, x)     gates, recurrence, state and residual update in one pass
+Per block the kernels are the tower's (vt_gemm_qkv_tiles + vt_attn_tiles_fwd with d = 64, vt_gemm_fused) plus
+the RG-LRU.  With fold_ln=True (default) every norm is folded into the GEMM after it, as in the tower:
+    mom = (mean, rstd) of x             vt_row_moments, from the chunk statistics the last writer of x left
+    qkv = LN1(x) . Wqkv^T + b           folded LN1 (A = bf16 copy of x, W * gamma1), tile scatter
+    x  += attn . Wo^T + b               residual epilogue + bf16 copy + chunk statistics
+    f   = gelu(LN2(x) . W1^T + b)       folded LN2
+    x  += f . W2^T + b                  residual epilogue + bf16 copy + chunk statistics
+    mom = (0, rstd) of x                vt_row_rms
+    G   = RMSNorm(x) . [Wx; Wa]^T + b   folded RMSNorm (W * gamma), N = 1536, fp32 out
+    vt_rglru_fold                       t = bf16(x rstd gamma), gates, recurrence, state, x += h, and the bf16 copy
+                                        and chunk statistics of the new x for the next block's LN1
+With fold_ln=False the norms run as vt_layernorm / vt_rmsnorm passes and the gate step as RgLruGate.
 """
 import torch
 
@@ -44,8 +51,9 @@ class RgLruGate:
 
 
 class TapNextStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, fold_ln=True):
         self.cfg = cfg
+        self.fold_ln = fold_ln
         self.use_graphs = graphs
         self._graph = None
         self._frame_in = self._q_in = None
@@ -69,6 +77,18 @@ class TapNextStep:
                                    cfg.lru_c, dev, self.G)
             for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "rms_w"):
                 blk[n] = _dev_vec(W[p + n], dev)
+            if fold_ln:   # LN1 into qkv, LN2 into fc1 (W * gamma, rowsum, b + W beta); RMSNorm gamma into the gates
+                for n, ln in (("qkv", "ln1"), ("fc1", "ln2")):
+                    wf, c, bf = ops.fold_layernorm(W[p + n + "_w"], W[p + n + "_b"], W[p + ln + "_w"], W[p + ln + "_b"])
+                    blk[n + "_wf"], blk[n + "_ldf"] = _dev_mat(wf, dev)
+                    blk[n + "_c"] = _dev_vec(c, dev)
+                    blk[n + "_bf"] = _dev_vec(bf, dev)
+                g = torch.cat([torch.as_tensor(W[p + "gx_w"]), torch.as_tensor(W[p + "ga_w"])], 0).float()
+                gb = torch.cat([torch.as_tensor(W[p + "gx_b"]), torch.as_tensor(W[p + "ga_b"])]).float()
+                wf, c, _ = ops.fold_layernorm(g, gb, W[p + "rms_w"], torch.zeros(g.shape[1]))
+                blk["gate_wf"], blk["gate_ldf"] = _dev_mat(wf, dev)
+                blk["gate_c"] = _dev_vec(c, dev)
+                blk["gate_b"] = _dev_vec(gb, dev)
             self.blocks.append(blk)
         self.fin_w = _dev_vec(W["final_ln_w"], dev)
         self.fin_b = _dev_vec(W["final_ln_b"], dev)
@@ -81,6 +101,10 @@ class TapNextStep:
         self.a = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.f = torch.empty(T, _pad8(cfg.ff), dtype=BF16, device=dev)
         self.state = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
+        if fold_ln:
+            self.xb = torch.empty(T, Wd, dtype=BF16, device=dev)                  # bf16 copy of x
+            self.stats = torch.empty(T, Wd // 32, 2, dtype=F32, device=dev)      # per-32-column (mean, M2) of x
+            self.mom = torch.empty(T, 2, dtype=F32, device=dev)                  # (mean | 0, rstd) per row
         self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
         self.first = True
 
@@ -114,6 +138,10 @@ class TapNextStep:
         ops.gemm(self.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
                  res=self.pos, res_period=NI, out=self.x[:NI])
         self.x[NI:].copy_(queries)
+        if self.fold_ln:
+            self._blocks_folded(first)
+            ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+            return
         for i, blk in enumerate(self.blocks):
             ops.layer_norm(self.x, blk["ln1_w"], blk["ln1_b"], cfg.eps, out=self.h)
             ops.gemm_qkv_tiles(self.h, blk["qkv_w"], blk["qkv_ld"], Wd, blk["qkv_b"], self.tiles, T, cfg.heads,
@@ -126,3 +154,25 @@ class TapNextStep:
             ops.rms_norm(self.x, blk["rms_w"], cfg.eps, out=self.t)
             blk["lru"](self.t, self.state[i], self.x, first)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+
+    def _blocks_folded(self, first):
+        cfg = self.cfg
+        T, Wd = cfg.ntok, cfg.width
+        fold = dict(out2=self.xb, stats_out=self.stats)
+        ops.row_stats(self.x, self.stats, self.xb)
+        for i, blk in enumerate(self.blocks):
+            ops.row_moments(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, blk["qkv_wf"], blk["qkv_ldf"], Wd, 3 * Wd, blk["qkv_bf"], out=self.tiles,
+                     ln=(self.mom, blk["qkv_c"]), tiles=(T, cfg.heads, cfg.head_dim))
+            ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
+            ops.gemm(self.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=self.x, out=self.x, **fold)
+            ops.row_moments(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, blk["fc1_wf"], blk["fc1_ldf"], Wd, cfg.ff, blk["fc1_bf"], gelu=True,
+                     out=self.f[:, :cfg.ff], ln=(self.mom, blk["fc1_c"]))
+            ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x,
+                     **fold)
+            ops.row_rms(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, blk["gate_wf"], blk["gate_ldf"], Wd, 2 * Wd, blk["gate_b"], out=self.G,
+                     ln=(self.mom, blk["gate_c"]))
+            ops.rglru_fold(self.G, blk["lru"].a_param, self.mom, blk["rms_w"], self.state[i], self.x, self.xb,
+                           self.stats, cfg.lru_c, first)
