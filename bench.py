@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-fold", action="store_true", help="LayerNorm as separate passes instead of folded into GEMMs")
     ap.add_argument("--no-tapnext", action="store_true",
                     help="skip the TAPNext per-frame step and text-decoder timings (N=1 only)")
+    ap.add_argument("--tapnext-only", action="store_true",
+                    help="profiling runs: only the config-3 and TAPNext++ per-frame steps, printed as one JSON line")
     return ap.parse_args()
 
 
@@ -360,8 +362,9 @@ def run_vt(a):
                          "bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
                          "frac": achieved / sustained, "traffic": traffic,
                          "traffic_source": "profiles/gemm_traffic.json: dram__bytes_read.sum + dram__bytes_write.sum per "
-                                           "GEMM launch from an ncu capture of a 26-crop chunk, scaled to the bench's "
-                                           "chunk by its rows (not measured in this run)",
+                                           "GEMM launch from an ncu capture of the 26-crop case, scaled to the bench's "
+                                           "chunk by its rows (not measured in this run; writes still in L2 when a "
+                                           "kernel ends are not counted)",
                          "peak_source": f"{src} bf16_tflops_sustained" + (" of measured" if src == "measured" else " of fallback"),
                          "launches": gemm_n, "avg_launch_ms": gemm_ms / max(gemm_n, 1)},
             "kernels": breakdown,
@@ -481,6 +484,11 @@ def tapnext_frame_ms(dev, n_frames=16):
 
 def main():
     a = parse()
+    if a.tapnext_only:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"tapnext_ms_per_frame": tapnext_frame_ms(dev)}), flush=True)
+        return
     if a.impl == "reference":
         run_reference(a)
     else:
