@@ -213,7 +213,9 @@ int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_
  * 64-channel heads): xc = conv_1d over the taps hist_old, hist_mid, hist_new (x_(t-3), x_(t-2), x_(t-1),
  * bf16) and xx (x_t, bf16), oldest first, + conv_b; the block-diagonal gates gx = sigmoid(xc_q wx[q] + bx),
  * ga = sigmoid(xc_q wa[q] + ba) per head q (wx / wa fp32 [W/64][64 in][64 out]); log_a = -8 ga softplus_a;
- * h = xc gx (first != 0) or a h + (xc gx) sqrt(1 - a^2) (fp32 state h, updated in place); z = bf16(h) yg.
+ * h = xc gx (first != 0) or a h + (xc gx) sqrt(1 - a^2) (fp32 state h, updated in place); z = bf16(h) yg,
+ * where yg is the bf16 input as given, or with gelu_y != 0 its GELU-tanh (the raw y half of linear_yx; the
+ * GELU rounds to bf16 as the GEMM epilogue's does).
  * Rounding follows the reference's bf16 restatement.  x_t is written over hist_old (the caller rotates
  * the three history roles); conv_w fp32 [4][W], conv_b / softplus_a / bx / ba fp32 [W].
  * Replaces: the recurrent block's conv_1d + rg_lru + (x * gelu(y)) of tapnext/npu/step8.py:477-480, whose
@@ -221,7 +223,7 @@ int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_
 int vt_ssm_step(cudaStream_t stream, const uint16_t* yg, const uint16_t* xx, long long ldi, uint16_t* hist_old,
                 const uint16_t* hist_mid, const uint16_t* hist_new, long long ldh, float* h, long long ldhs,
                 const float* conv_w, const float* conv_b, const float* softplus_a, const float* wx, const float* bx,
-                const float* wa, const float* ba, uint16_t* z, long long ldz, int R, int W, int first);
+                const float* wa, const float* ba, uint16_t* z, long long ldz, int R, int W, int first, int gelu_y);
 
 /* Gated MLP combine: out[r, j] = bf16(bf16(gelu_tanh(G[r, j])) * G[r, F + j]), j < F, for the bf16
  * ffw_up output G = [gate | up] [R][2F] (F % 8 == 0, 16-byte aligned rows).

@@ -41,7 +41,7 @@ SIGNATURES = {
     "vt_row_rms": (I, [P, P, I, I, F, P]),
     "vt_rglru_fold": (I, [P, P, LL, P, P, P, P, LL, P, LL, P, LL, P, I, I, F, I]),
     "vt_rglru": (I, [P, P, LL, P, P, LL, P, LL, P, LL, I, I, F, I]),
-    "vt_ssm_step": (I, [P, P, P, LL, P, P, P, LL, P, LL, P, P, P, P, P, P, P, P, LL, I, I, I]),
+    "vt_ssm_step": (I, [P, P, P, LL, P, P, P, LL, P, LL, P, P, P, P, P, P, P, P, LL, I, I, I, I]),
     "vt_gated_gelu_mul": (I, [P, P, LL, P, LL, I, I]),
     "vt_gelu_erf": (I, [P, P, LL, I, I]),
     "vt_rope_qkv": (I, [P, P, LL, I, I, I, P, P, P, P, P, I]),

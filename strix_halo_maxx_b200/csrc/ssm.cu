@@ -19,6 +19,15 @@ constexpr int RB = 32, HD = 64, THREADS = 256;
 
 __device__ __forceinline__ float bfr(float v) { return bfround(v); }
 
+// gelu_y: the y half of linear_yx arrives as the raw bf16 linear output and its GELU-tanh is taken here, with
+// the GEMM epilogue's arithmetic (gelu_tanh2 on the bf16 value, rounded to bf16), so z is the same as when the
+// GEMM applied the GELU.
+__device__ __forceinline__ uint32_t gelu_word(uint32_t w) {
+  float g0, g1;
+  f2_unpack(gelu_tanh2(f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u))), g0, g1);
+  return pack_bf2(g0, g1);
+}
+
 // One CTA: RB rows x one head (64 channels).  hist_old / hist_mid / hist_new hold x_(t-3) / x_(t-2) / x_(t-1)
 // (zeros before the first frames); x_t is written over hist_old, so the caller rotates the three roles.
 __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
@@ -26,7 +35,7 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
     const uint16_t* hist_mid, const uint16_t* hist_new, long long ldh, float* __restrict__ h, long long ldhs,
     const float* __restrict__ conv_w, const float* __restrict__ conv_b, const float* __restrict__ sp,
     const float* __restrict__ wx, const float* __restrict__ bx, const float* __restrict__ wa,
-    const float* __restrict__ ba, uint16_t* __restrict__ z, long long ldz, int R, int W, int first) {
+    const float* __restrict__ ba, uint16_t* __restrict__ z, long long ldz, int R, int W, int first, int gelu_y) {
   griddep_wait();  // programmatic dependent launch: the previous kernel has completed
   griddep_launch();
   __shared__ float xcs[RB][HD + 1];
@@ -90,7 +99,9 @@ __global__ void __launch_bounds__(THREADS) ssm_step_kernel(
       hb = bfr(hn);
     }
     h[is] = hn;
-    z[(size_t)row * ldz + col] = f2bf(__fmul_rn(hb, bf2f(yg[(size_t)row * ldi + col])));
+    uint32_t yb = yg[(size_t)row * ldi + col];
+    if (gelu_y) yb = gelu_word(yb) & 0xffffu;
+    z[(size_t)row * ldz + col] = f2bf(__fmul_rn(hb, bf2f((uint16_t)yb)));
   }
 }
 
@@ -140,7 +151,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) ssm_step_tc_kernel(
     const uint16_t* hist_mid, const uint16_t* hist_new, long long ldh, float* __restrict__ h, long long ldhs,
     const float* __restrict__ conv_w, const float* __restrict__ conv_b, const float* __restrict__ sp,
     const float* __restrict__ wx, const float* __restrict__ bx, const float* __restrict__ wa,
-    const float* __restrict__ ba, uint16_t* __restrict__ z, long long ldz, int R, int W, int first) {
+    const float* __restrict__ ba, uint16_t* __restrict__ z, long long ldz, int R, int W, int first, int gelu_y) {
   __shared__ __align__(1024) uint8_t a_tile[TC_ROWS * HD * 2];  // 16 KB: xc, bf16
   __shared__ __align__(1024) uint8_t b_tile[2][HD * HD * 2];    // 2 x 8 KB: Wx^T, Wa^T, bf16
   __shared__ __align__(8) uint64_t mma_done;
@@ -257,7 +268,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) ssm_step_tc_kernel(
         hv[0] = t0.x, hv[1] = t0.y, hv[2] = t0.z, hv[3] = t0.w, hv[4] = t1.x, hv[5] = t1.y, hv[6] = t1.z, hv[7] = t1.w;
       }
       const uint4 y0 = *reinterpret_cast<const uint4*>(yg + iy);
-      const uint32_t yw[4] = {y0.x, y0.y, y0.z, y0.w};
+      uint32_t yw[4] = {y0.x, y0.y, y0.z, y0.w};
+      if (gelu_y) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) yw[k] = gelu_word(yw[k]);
+      }
       const uint4 xa = *reinterpret_cast<const uint4*>(&a_tile[cc * 2048 + r * 16]);
       const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
       float hn[8], bxv[8], bav[8], spv[8];
@@ -397,7 +412,7 @@ extern "C" {
 int vt_ssm_step(cudaStream_t st, const uint16_t* yg, const uint16_t* xx, long long ldi, uint16_t* hist_old,
                 const uint16_t* hist_mid, const uint16_t* hist_new, long long ldh, float* h, long long ldhs,
                 const float* conv_w, const float* conv_b, const float* softplus_a, const float* wx, const float* bx,
-                const float* wa, const float* ba, uint16_t* z, long long ldz, int R, int W, int first) {
+                const float* wa, const float* ba, uint16_t* z, long long ldz, int R, int W, int first, int gelu_y) {
   using namespace vt;
   if (R < 0 || W <= 0 || W % ssm::HD) return set_error(E_SHAPE, "vt_ssm_step: W must be a positive multiple of 64");
   if (R == 0) return OK;
@@ -414,12 +429,12 @@ int vt_ssm_step(cudaStream_t st, const uint16_t* yg, const uint16_t* xx, long lo
     if (trc) return trc;
     const dim3 grid((R + ssm::TC_ROWS - 1) / ssm::TC_ROWS, W / ssm::HD);
     launch_k(ssm::ssm_step_tc_kernel, grid, ssm::TC_THREADS, 0, st, yg, xx, ldi, hist_old, hist_mid, hist_new, ldh, h, ldhs, conv_w,
-             conv_b, softplus_a, wx, bx, wa, ba, z, ldz, R, W, first);
+             conv_b, softplus_a, wx, bx, wa, ba, z, ldz, R, W, first, gelu_y);
     return check_launch("vt_ssm_step");
   }
   const dim3 grid((R + ssm::RB - 1) / ssm::RB, W / ssm::HD);
   launch_k(ssm::ssm_step_kernel, grid, ssm::THREADS, 0, st, yg, xx, ldi, hist_old, hist_mid, hist_new, ldh, h, ldhs, conv_w,
-                                                      conv_b, softplus_a, wx, bx, wa, ba, z, ldz, R, W, first);
+                                                      conv_b, softplus_a, wx, bx, wa, ba, z, ldz, R, W, first, gelu_y);
   return check_launch("vt_ssm_step");
 }
 

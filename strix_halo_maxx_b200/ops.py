@@ -352,16 +352,16 @@ def rglru(G, a_param, u, state, x, c, first):
     check(rc, "vt_rglru")
 
 
-def ssm_step(yg, xx, hist, h, conv_w, conv_b, softplus_a, wx, bx, wa, ba, z, first):
+def ssm_step(yg, xx, hist, h, conv_w, conv_b, softplus_a, wx, bx, wa, ba, z, first, gelu_y=False):
     """TAPNext++ recurrent step (vt_ssm_step): yg, xx [R, W] bf16 views; hist = (x_(t-3), x_(t-2), x_(t-1))
     bf16 [R, W] -- x_t is written over hist[0], so the caller rotates; h [R, W] fp32 state in place;
-    z [R, W] bf16 out."""
+    z [R, W] bf16 out.  gelu_y: yg is the raw y linear output and the kernel applies its GELU-tanh."""
     R, W = z.shape
     old, mid, new = hist
     rc = lib().vt_ssm_step(_stream(), yg.data_ptr(), xx.data_ptr(), yg.stride(0), old.data_ptr(), mid.data_ptr(),
                            new.data_ptr(), old.stride(0), h.data_ptr(), h.stride(0), conv_w.data_ptr(),
                            conv_b.data_ptr(), softplus_a.data_ptr(), wx.data_ptr(), bx.data_ptr(), wa.data_ptr(),
-                           ba.data_ptr(), z.data_ptr(), z.stride(0), R, W, int(bool(first)))
+                           ba.data_ptr(), z.data_ptr(), z.stride(0), R, W, int(bool(first)), int(bool(gelu_y)))
     check(rc, "vt_ssm_step")
     return z
 

@@ -4,8 +4,8 @@ of a 256x256 frame (1024 tokens) + position embedding, then the point-query toke
 
 Per block, in the reference's order:
     t   = RMSNorm(x) (1 + scale)                       vt_rmsnorm
-    yg  = gelu_tanh(t Wy^T + by), xx = t Wx^T + bx     two vt_gemm launches (linear_yx split), bf16
-    z   = RG-LRU(conv_1d(xx)) * yg                     vt_ssm_step (4-tap history ring, fp32 state)
+    y, xx = t Wyx^T + byx                              one vt_gemm (linear_yx, N = 1536), bf16
+    z   = RG-LRU(conv_1d(xx)) * gelu_tanh(y)           vt_ssm_step (4-tap history ring, fp32 state, GELU of y)
     x  += z Wout^T + bout                              vt_gemm, fp32 residual epilogue
     G   = RMSNorm(x) (1 + scale) Wup^T + bup           vt_rmsnorm, vt_gemm (N = 2 x 3072: [gate | up])
     x  += (gelu_tanh(gate) * up) Wdown^T + bdown       vt_gated_gelu_mul, vt_gemm + residual
@@ -82,8 +82,9 @@ class TrackHeads:
 
 
 class TapNextPPStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, heads=None):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, heads=None, fold_ln=True):
         self.cfg = cfg
+        self.fold_ln = fold_ln
         self.use_graphs = graphs
         self._graphs = {}
         self._frame_in = self._q_in = None
@@ -100,10 +101,10 @@ class TapNextPPStep:
         for i in range(self.n_blocks):
             p = f"blocks.{i}."
             b = {}
-            yx_w, yx_b = torch.as_tensor(W[p + "yx_w"]), torch.as_tensor(W[p + "yx_b"])
-            b["y_w"], b["y_ld"] = _dev_mat(yx_w[:Wd], dev)
-            b["x_w"], b["x_ld"] = _dev_mat(yx_w[Wd:], dev)
-            b["y_b"], b["x_b"] = _dev_vec(yx_b[:Wd], dev), _dev_vec(yx_b[Wd:], dev)
+            # linear_yx as one 768 -> 1536 GEMM ([y | x], the reference's layout); the GELU of y is taken in
+            # vt_ssm_step (gelu_y), which reads y from the same buffer
+            b["yx_w"], b["yx_ld"] = _dev_mat(W[p + "yx_w"], dev)
+            b["yx_b"] = _dev_vec(W[p + "yx_b"], dev)
             for n in ("out", "up", "down", "qkv", "proj", "fc1", "fc2"):
                 b[n + "_w"], b[n + "_ld"] = _dev_mat(W[p + n + "_w"], dev)
                 b[n + "_b"] = _dev_vec(W[p + n + "_b"], dev)
@@ -112,6 +113,17 @@ class TapNextPPStep:
             for n in ("conv_w", "conv_b", "gx_w", "gx_b", "ga_w", "ga_b", "ln1_w", "ln1_b", "ln2_w", "ln2_b"):
                 b[n] = _dev_vec(W[p + n], dev)
             b["softplus_a"] = _dev_vec(F.softplus(torch.as_tensor(W[p + "a_param"]).double()).float(), dev)
+            if fold_ln:
+                # each norm folded into the GEMM after it: W * gamma (bf16), c = rowsum, b + W beta; the RMSNorms'
+                # gamma is (1 + scale) and their GEMM epilogues use mean 0
+                zero = torch.zeros(Wd)
+                for n, g, be in (("yx", 1.0 + torch.as_tensor(W[p + "rms0_scale"]).float(), zero),
+                                 ("up", 1.0 + torch.as_tensor(W[p + "rms1_scale"]).float(), zero),
+                                 ("qkv", W[p + "ln1_w"], W[p + "ln1_b"]), ("fc1", W[p + "ln2_w"], W[p + "ln2_b"])):
+                    wf, c, bf = ops.fold_layernorm(W[p + n + "_w"], W[p + n + "_b"], g, be)
+                    b[n + "_wf"], b[n + "_ldf"] = _dev_mat(wf, dev)
+                    b[n + "_c"] = _dev_vec(c, dev)
+                    b[n + "_bf"] = _dev_vec(bf, dev)
             self.blocks.append(b)
         self.fin_w = _dev_vec(W["final_ln_w"], dev)
         self.fin_b = _dev_vec(W["final_ln_b"], dev)
@@ -129,6 +141,10 @@ class TapNextPPStep:
         self.h = torch.zeros(self.n_blocks, T, Wd, dtype=F32, device=dev)
         self.hist = torch.zeros(self.n_blocks, 3, T, Wd, dtype=BF16, device=dev)
         self.out = torch.empty(T, Wd, dtype=BF16, device=dev)
+        if fold_ln:
+            self.xb = torch.empty(T, Wd, dtype=BF16, device=dev)                  # bf16 copy of x
+            self.stats = torch.empty(T, Wd // 32, 2, dtype=F32, device=dev)      # per-32-column (mean, M2) of x
+            self.mom = torch.empty(T, 2, dtype=F32, device=dev)                  # (mean | 0, rstd) per row
         # optional tracking heads (weights as weights.heads_weights): run on the query tokens inside the step
         self.heads = TrackHeads(heads, cfg, dev) if heads is not None else None
         self.reset()
@@ -174,14 +190,24 @@ class TapNextPPStep:
         ops.gemm(self.a_pe[:, :cfg.patch_k], self.pe_w, self.pe_ld, cfg.patch_k, Wd, self.pe_b,
                  res=self.pos, res_period=NI, out=self.x[:NI])
         self.x[NI:].copy_(queries)
+        if self.fold_ln:
+            self._blocks_folded(k, first)
+        else:
+            self._blocks(k, first)
+        ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
+        if self.heads is not None:
+            self.heads(self.out[NI:])
+
+    def _blocks(self, k, first):
+        cfg = self.cfg
+        T, Wd, Fh = cfg.ntok, cfg.width, cfg.ff
         for i, b in enumerate(self.blocks):
             hist = (self.hist[i, k], self.hist[i, (k + 1) % 3], self.hist[i, (k + 2) % 3])
             # recurrent block (step8.py:474-481)
             ops.rms_norm(self.x, b["rms0"], cfg.eps, out=self.t)
-            ops.gemm(self.t, b["y_w"], b["y_ld"], Wd, Wd, b["y_b"], gelu=True, out=self.yx[:, :Wd])
-            ops.gemm(self.t, b["x_w"], b["x_ld"], Wd, Wd, b["x_b"], out=self.yx[:, Wd:])
+            ops.gemm(self.t, b["yx_w"], b["yx_ld"], Wd, 2 * Wd, b["yx_b"], out=self.yx)
             ops.ssm_step(self.yx[:, :Wd], self.yx[:, Wd:], hist, self.h[i], b["conv_w"], b["conv_b"],
-                         b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first)
+                         b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first, gelu_y=True)
             ops.gemm(self.z, b["out_w"], b["out_ld"], Wd, Wd, b["out_b"], res=self.x, out=self.x)
             # gated MLP (step8.py:482-483)
             ops.rms_norm(self.x, b["rms1"], cfg.eps, out=self.t)
@@ -197,6 +223,37 @@ class TapNextPPStep:
             ops.gemm(self.t, b["fc1_w"], b["fc1_ld"], Wd, Fh, b["fc1_b"], out=self.f)
             ops.gelu_erf(self.f)
             ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x)
-        ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
-        if self.heads is not None:
-            self.heads(self.out[NI:])
+
+    def _blocks_folded(self, k, first):
+        """The same blocks with every norm folded into the GEMM after it: the residual GEMMs (linear_out,
+        ffw_down, out_proj, mlp.3) also write the bf16 copy of x and its 32-column chunk statistics, from which
+        vt_row_rms / vt_row_moments give the next norm's row factors."""
+        cfg = self.cfg
+        T, Wd, Fh = cfg.ntok, cfg.width, cfg.ff
+        fold = dict(out2=self.xb, stats_out=self.stats)
+        ops.row_stats(self.x, self.stats, self.xb)
+        for i, b in enumerate(self.blocks):
+            hist = (self.hist[i, k], self.hist[i, (k + 1) % 3], self.hist[i, (k + 2) % 3])
+            # recurrent block (step8.py:474-481)
+            ops.row_rms(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, b["yx_wf"], b["yx_ldf"], Wd, 2 * Wd, b["yx_bf"], out=self.yx, ln=(self.mom, b["yx_c"]))
+            ops.ssm_step(self.yx[:, :Wd], self.yx[:, Wd:], hist, self.h[i], b["conv_w"], b["conv_b"],
+                         b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first, gelu_y=True)
+            ops.gemm(self.z, b["out_w"], b["out_ld"], Wd, Wd, b["out_b"], res=self.x, out=self.x, **fold)
+            # gated MLP (step8.py:482-483)
+            ops.row_rms(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, b["up_wf"], b["up_ldf"], Wd, 2 * Fh, b["up_bf"], out=self.G, ln=(self.mom, b["up_c"]))
+            ops.gated_gelu_mul(self.G, self.m)
+            ops.gemm(self.m, b["down_w"], b["down_ld"], Fh, Wd, b["down_b"], res=self.x, out=self.x, **fold)
+            # ViT block (step8.py:484-486)
+            ops.row_moments(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, b["qkv_wf"], b["qkv_ldf"], Wd, 3 * Wd, b["qkv_bf"], out=self.tiles,
+                     ln=(self.mom, b["qkv_c"]), tiles=(T, cfg.heads, cfg.head_dim))
+            ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
+            ops.gemm(self.a, b["proj_w"], b["proj_ld"], Wd, Wd, b["proj_b"], res=self.x, out=self.x, **fold)
+            ops.row_moments(self.stats, cfg.eps, self.mom)
+            ops.gemm(self.xb, b["fc1_wf"], b["fc1_ldf"], Wd, Fh, b["fc1_bf"], out=self.f, ln=(self.mom, b["fc1_c"]))
+            # the exact GELU as its own pass: in fc1's epilogue (one 256 x 256 tile per CTA pair at 1280 rows, so
+            # nothing hides it) it measured 20 us per frame slower
+            ops.gelu_erf(self.f)
+            ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x, **fold)

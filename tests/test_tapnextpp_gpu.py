@@ -73,12 +73,15 @@ def test_gated_gelu_mul_and_gelu_erf():
     assert torch.allclose(x.float(), ref2, rtol=1e-2, atol=1e-3)
 
 
-@pytest.mark.parametrize("n_blocks,n_frames,affine", [(12, 2, "zero"), (2, 6, "random")])
-def test_tapnextpp_stream(n_blocks, n_frames, affine):
+@pytest.mark.parametrize("n_blocks,n_frames,affine,fold_ln", [(12, 2, "zero", True), (2, 6, "random", True),
+                                                             (2, 6, "random", False)])
+def test_tapnextpp_stream(n_blocks, n_frames, affine, fold_ln):
+    """The full TAPNext++ step against the fp32 restatement, state and conv history carried, with the four norms
+    of a block folded into the GEMMs after them (default) and as separate passes."""
     device_status(clear=True)
     W = wg.tapnextpp_weights(CFG, seed=9, n_blocks=n_blocks, affine=affine)
     frames, queries = wg.tapnext_inputs(CFG, n_frames, seed=2)
-    eng = TapNextPPStep(W, CFG, device=DEV)
+    eng = TapNextPPStep(W, CFG, device=DEV, fold_ln=fold_ln)
     state = None
     for f in range(n_frames):
         ref, state = R.step(frames[f], queries[f], W, CFG, state, n_blocks)
@@ -147,3 +150,33 @@ def test_tapnextpp_track_runs_the_heads_inside_the_step():
         assert float((tracks.cpu() - rt).abs().max()) < 1e-3, f"frame {f}"
         assert torch.allclose(vis.cpu(), rv, rtol=1e-4, atol=1e-4)
     assert len(eng._graphs) == 2
+
+
+@pytest.mark.parametrize("first", [True, False])
+def test_ssm_step_gelu_y_equals_gelu_in_the_gemm(first):
+    """linear_yx as one GEMM with the GELU of y taken in vt_ssm_step (gelu_y) gives the same z, h and history
+    bit for bit as the GELU-tanh GEMM epilogue on the y half."""
+    g = torch.Generator(device=DEV).manual_seed(9)
+    Rn, W = 1280, 768
+    t = torch.randn(Rn, W, device=DEV, generator=g).to(BF)
+    wyx = (torch.randn(2 * W, W, device=DEV, generator=g) * 0.04).to(BF)
+    byx = torch.randn(2 * W, device=DEV, generator=g) * 0.1
+    H = W // 64
+    conv_w, conv_b = torch.randn(4, W, device=DEV, generator=g) * 0.5, torch.randn(W, device=DEV, generator=g) * 0.1
+    sp = torch.nn.functional.softplus(torch.randn(W, device=DEV, generator=g))
+    wx = (torch.randn(H, 64, 64, device=DEV, generator=g) * 0.15).to(BF).float()
+    wa = (torch.randn(H, 64, 64, device=DEV, generator=g) * 0.15).to(BF).float()
+    bx, ba = torch.randn(W, device=DEV, generator=g) * 0.1, torch.randn(W, device=DEV, generator=g) * 0.1
+    hist0 = [torch.randn(Rn, W, device=DEV, generator=g).to(BF) for _ in range(3)]
+    h0 = torch.randn(Rn, W, device=DEV, generator=g)
+    yx_raw = ops.gemm(t, wyx, W, W, 2 * W, byx)
+    yx_gelu = yx_raw.clone()       # y and x share one row pitch in vt_ssm_step: [gelu(y) | x]
+    yx_gelu[:, :W] = ops.gemm(t, wyx[:W], W, W, W, byx[:W], gelu=True)
+    outs = []
+    for gelu_y, yx in ((True, yx_raw), (False, yx_gelu)):
+        hist = [x.clone() for x in hist0]
+        h, z = h0.clone(), torch.empty(Rn, W, dtype=BF, device=DEV)
+        ops.ssm_step(yx[:, :W], yx[:, W:], hist, h, conv_w, conv_b, sp, wx, bx, wa, ba, z, first, gelu_y=gelu_y)
+        outs.append((z, h, hist[0]))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
