@@ -1,4 +1,5 @@
-"""CPU fp32 restatement of the TAPNext-style per-frame step -- TEST INFRASTRUCTURE, parity unpinned.
+"""CPU fp32 restatement of the TAPNext-style per-frame step -- TEST INFRASTRUCTURE; RG-LRU pinned, the
+composition unpinned.
 
 Token layout: 8x8 patch conv of a 256x256 frame (1024 tokens) + image position embedding, then the
 256 point-query tokens (tapnext/npu/step8.py:251-267).  Each of the 12 blocks is a pre-LN ViT block
@@ -10,9 +11,15 @@ transcendentals:
     h = t * gx                                  (first frame, h0 is None)
     h = a * h0 + (t * gx) * sqrt(1 - a^2)        (later frames)
     x <- x + h, state <- h (float32)
-then the encoder LayerNorm (step8.py:488).  The BASELINE config simplifies the reference block (no
-RMSNorm / conv1d / gated MLP, dense gates), and the vendored model is not in the repository, so
-nothing pins this restatement against the reference's outputs.
+then the encoder LayerNorm (step8.py:488).
+
+Pinning: rglru() is checked against the reference's own ssm_ref (tapnext/npu/pack8.py:252-279) run with
+12 heads of block-diagonal gates and identity conv taps, where ssm_ref's h is exactly this RG-LRU
+(tests/golden/make_golden_ssm.py -> rglru_ref_cases.npz, tests/test_oracle_golden.py, within 1e-2 per row:
+ssm_ref rounds its intermediates to bf16).  The ViT block is built from tower_ref's operations, which are
+pinned to FastMD2._vision.  The composition (a ViT block then the temporal block, dense gates, no conv1d /
+gated MLP) is the BASELINE config's simplification of the reference block; with the vendored model not in
+the repository, nothing pins the composed step against the reference's outputs.
 """
 import torch
 import torch.nn.functional as F
