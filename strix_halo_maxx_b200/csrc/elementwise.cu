@@ -278,8 +278,6 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* f, long lo
 //   h  = u * gx                                              (first frame)
 //   h  = exp(log_a) * h0 + (u * gx) * sqrt(-expm1(2 log_a))   (later frames)
 //   state <- h, x <- x + h     (u bf16; state and the residual stream x fp32, updated in place)
-__device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
-__device__ __forceinline__ float softplusf_(float z) { return z > 20.f ? z : log1pf(expf(z)); }
 
 __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param,
                                                     const uint16_t* u, long long ldu, float* state, long long lds,
@@ -304,14 +302,7 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
     float xv[4] = {x4.x, x4.y, x4.z, x4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
     for (int e = 0; e < 4; e++) {
-      const float gated = uv[e] * sigmoidf_(gx[e]);
-      float h;
-      if (first) {
-        h = gated;
-      } else {
-        const float log_a = -c * sigmoidf_(ga[e]) * softplusf_(ap[e]);
-        h = expf(log_a) * hv[e] + gated * sqrtf(-expm1f(2.0f * log_a));
-      }
+      const float h = rglru_elem(uv[e], gx[e], ga[e], ap[e], hv[e], c, first != 0);
       hv[e] = h;
       xv[e] += h;
     }
@@ -359,14 +350,7 @@ __global__ void __launch_bounds__(256) rglru_fold_kernel(const float* G, long lo
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         const float u = bfround(xv[e] * rstd * rg[e]);  // the RMSNorm output, bf16 as the unfolded path stores it
-        const float gated = u * sigmoidf_(gx[e]);
-        float h;
-        if (first) {
-          h = gated;
-        } else {
-          const float log_a = -c * sigmoidf_(ga[e]) * softplusf_(ap[e]);
-          h = expf(log_a) * hv0[e] + gated * sqrtf(-expm1f(2.0f * log_a));
-        }
+        const float h = rglru_elem(u, gx[e], ga[e], ap[e], hv0[e], c, first != 0);
         hv[e] = h;
         xv[e] += h;
       }
