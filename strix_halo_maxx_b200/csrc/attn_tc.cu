@@ -77,11 +77,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   uint64_t* v_full = bar + 1 + 2 * KVS;  // [KVS]
   uint64_t* v_empty = bar + 1 + 3 * KVS; // [KVS]
   uint64_t* s_full = bar + 1 + 4 * KVS;  // [2]
-  uint64_t* p_full = s_full + 2;         // [2], 128 arrivals
-  uint64_t* pv_done = s_full + 4;
-  uint64_t* o_full = s_full + 5;
-  uint64_t* drain = s_full + 6;
-  constexpr int NBAR = 1 + 4 * KVS + 7;
+  uint64_t* p_full = s_full + 2;         // [2], one arrival per softmax warp
+  uint64_t* o_full = s_full + 4;
+  uint64_t* drain = s_full + 5;
+  constexpr int NBAR = 1 + 4 * KVS + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -96,8 +95,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; i++) mbar_init(&bar[i], 1);
-    mbar_init(&p_full[0], 128);
-    mbar_init(&p_full[1], 128);
+    mbar_init(&p_full[0], 4);  // one arrival per softmax warp
+    mbar_init(&p_full[1], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -154,26 +153,35 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV);
       constexpr uint32_t IDESC_O = idesc_bf16(BQ, DP) | (1u << 16);  // B (= V) MN-major
       const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V);
-      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into S buffer j%2
+      // S_j = Q K_j^T into S buffer j%2; k_ready: K_j is known to have landed (checked off the S chain)
+      auto issue_s = [&](int j, bool k_ready) -> bool {
         const int s = j & 1;
         const int ks = j % KVS;
-        if (!mbar_wait(&k_full[ks], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) return false;
+        if (!k_ready && !mbar_wait(&k_full[ks], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) return false;
         tc_fence_after();
         const uint32_t kb = sk + ks * L::KT;
 #pragma unroll
         for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA: Q chunks 2k, 2k+1 (2048 B apart), K chunks (1024 B apart)
           umma_f16(tmem + s * BKV, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(kb + k * 2048, 1024, 128),
                    IDESC_S, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[s]);  // first: the softmax warps wait on this one
         umma_commit(&k_empty[ks]);
-        umma_commit(&s_full[s]);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, ST_ATTN_MMA) && issue_s(0);
+      // The chain that sets the tile rate runs P_j -> PV_j -> S_(j+2) (issued at the top of the next
+      // iteration) -> softmax of tile j+2, and one thread issues a tcgen05.mma every ~48 cycles and a commit
+      // every ~44 (measured): so the chain carries one commit per MMA group (O's rescale waits on v_empty, there
+      // is no separate PV barrier), and every wait that can be settled before P_j arrives is settled then (V_j,
+      // and a non-blocking look at K_(j+2), which usually has landed; its phase cannot alias: K_(j+2-KVS) was
+      // waited for and K_(j+2+KVS) needs S_(j+2)).
+      bool ok = mbar_wait(q_full, 0, abort_flag, ST_ATTN_MMA) && issue_s(0, false);
+      bool k_next = false;  // K_(j+1) seen landed during iteration j-1
       for (int j = 0; j < nkv && ok; j++) {
         const int s = j & 1;
-        if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait(&p_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        if (j + 1 < nkv && !issue_s(j + 1, k_next)) { ok = false; break; }
         if (!mbar_wait(&v_full[j % KVS], (j / KVS) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
+        k_next = j + 2 < nkv && mbar_try_wait(&k_full[(j + 2) % KVS], ((j + 2) / KVS) & 1);
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_MMA)) { ok = false; break; }
         tc_fence_after();
         const uint32_t vb = sv + (j % KVS) * L::KT;
 #pragma unroll
@@ -181,7 +189,6 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           umma_f16_ts(t_o, tmem + s * BKV + k * 8, sdesc_noswz(vb + k * 256, 128, 1024), IDESC_O,
                       (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&v_empty[j % KVS]);
-        umma_commit(pv_done);
       }
       if (ok) umma_commit(o_full);
       umma_commit(drain);
@@ -236,8 +243,9 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       } else {
         const bool need = mx > m_used + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {  // O round trip through registers (warp-collective), rare
-          // O must hold every P.V up to j-1: PV_(j-1) completes phase j-1 of pv_done
-          if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
+          // O must hold every P.V up to j-1: wait for PV_(j-1) on its V stage's barrier.  S_j is complete, so
+          // PV_(j-2) and everything before it are too, and PV_(j-1+KVS), the next arrival on that barrier, needs P_j
+          if (!mbar_wait(&v_empty[(j - 1) % KVS], ((j - 1) / KVS) & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
           tc_fence_after();
           const float m_new = need ? mx : m_used;
           const float alpha = exp2f(m_used - m_new);
@@ -281,7 +289,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[s]);
     }
     if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
       tc_fence_after();
