@@ -37,7 +37,9 @@ class TrackHeads:
     every frame: Step8.heads_np, tapnext/npu/step8.py:327-362).  Per head: Linear width -> hidden, LayerNorm,
     erf GELU, Linear hidden -> hidden, LayerNorm, erf GELU, Linear -> 2 x bins coordinate logits (y | x) or one
     visibility logit; then per axis the soft-argmax over +-window bins of the first maximum at the temperature,
-    + 0.5.  The two heads' first Linear run as one [width, 2 hidden] product and their LayerNorms as one pass.
+    + 0.5.  The two heads run side by side: their first Linear as one [width, 2 hidden] product, their second
+    and third as one product each with a block-diagonal weight (the other head's rows are zeros, so every output's
+    k-ordered fp32 sum is the head's own), and their LayerNorms as one pass.
     HW: weights as strix_halo_maxx_b200.weights.heads_weights names them ([out, in], torch's layout).
     __call__(x [Q, width] bf16) -> (tracks [Q, 2], logits [Q, 2 bins], vis [Q]) fp32 views of buffers this
     object owns (valid until the next call)."""
@@ -48,37 +50,43 @@ class TrackHeads:
         Q = cfg.n_queries if n_queries is None else n_queries
         Hh, nb = cfg.head_hidden, cfg.track_bins
         t = lambda name: torch.as_tensor(HW[name]).float()                          # noqa: E731
-        wt = lambda name: t(name).t().contiguous().to(dev)                         # noqa: E731 [in, out]
         self.w0 = torch.cat([t("coord.0_w").t(), t("vis.0_w").t()], 1).contiguous().to(dev)   # [width, 2 Hh]
         self.b0 = torch.cat([t("coord.0_b"), t("vis.0_b")]).to(dev)
         self.g1 = torch.stack([t("coord.1_w"), t("vis.1_w")]).to(dev)
         self.be1 = torch.stack([t("coord.1_b"), t("vis.1_b")]).to(dev)
-        self.w3c, self.w3v = wt("coord.3_w"), wt("vis.3_w")
-        self.b3c, self.b3v = t("coord.3_b").to(dev), t("vis.3_b").to(dev)
+        # second Linear: [2 Hh, 2 Hh] = diag(coord.3_w^T, vis.3_w^T)
+        self.w3 = torch.zeros(2 * Hh, 2 * Hh)
+        self.w3[:Hh, :Hh], self.w3[Hh:, Hh:] = t("coord.3_w").t(), t("vis.3_w").t()
+        self.w3 = self.w3.to(dev)
+        self.b3 = torch.cat([t("coord.3_b"), t("vis.3_b")]).to(dev)
         self.g4 = torch.stack([t("coord.4_w"), t("vis.4_w")]).to(dev)
         self.be4 = torch.stack([t("coord.4_b"), t("vis.4_b")]).to(dev)
-        self.w6c, self.w6v = wt("coord.6_w"), wt("vis.6_w")                        # [Hh, 2 nb], [Hh, 1]
-        self.b6c, self.b6v = t("coord.6_b").to(dev), t("vis.6_b").to(dev)
+        # third Linear: [2 Hh, 2 nb + 4]: coord.6_w^T in rows [0, Hh) x columns [0, 2 nb), vis.6_w^T in rows
+        # [Hh, 2 Hh) x column 2 nb; three zero columns keep the row pitch a multiple of 16 bytes
+        self.nout = 2 * nb + 4
+        self.w6 = torch.zeros(2 * Hh, self.nout)
+        self.w6[:Hh, :2 * nb], self.w6[Hh:, 2 * nb:2 * nb + 1] = t("coord.6_w").t(), t("vis.6_w").t()
+        self.w6 = self.w6.to(dev)
+        self.b6 = torch.cat([t("coord.6_b"), t("vis.6_b"), torch.zeros(3)]).to(dev)
         self.y1 = torch.empty(Q, 2 * Hh, dtype=F32, device=dev)                    # [coord | vis] per query
         self.y2 = torch.empty(Q, 2 * Hh, dtype=F32, device=dev)
-        self.logits = torch.empty(Q, 2 * nb, dtype=F32, device=dev)
-        self.vis = torch.empty(Q, 1, dtype=F32, device=dev)
+        self.out = torch.empty(Q, self.nout, dtype=F32, device=dev)                # [logits | vis | 0 0 0]
         self.tracks = torch.empty(Q, 2, dtype=F32, device=dev)
 
     def __call__(self, x):
         cfg = self.cfg
         Q, Hh = x.shape[0], cfg.head_hidden
         assert Q <= self.y1.shape[0]
-        y1, y2, lg, vis, tr = self.y1[:Q], self.y2[:Q], self.logits[:Q], self.vis[:Q], self.tracks[:Q]
+        nb2 = 2 * cfg.track_bins
+        y1, y2, out, tr = self.y1[:Q], self.y2[:Q], self.out[:Q], self.tracks[:Q]
         ops.head_linear(x, self.w0, self.b0, y1)
         ops.head_ln_gelu(y1.view(2 * Q, Hh), self.g1, self.be1, cfg.head_eps)
-        ops.head_linear(y1[:, :Hh], self.w3c, self.b3c, y2[:, :Hh])
-        ops.head_linear(y1[:, Hh:], self.w3v, self.b3v, y2[:, Hh:])
+        ops.head_linear(y1, self.w3, self.b3, y2)
         ops.head_ln_gelu(y2.view(2 * Q, Hh), self.g4, self.be4, cfg.head_eps)
-        ops.head_linear(y2[:, :Hh], self.w6c, self.b6c, lg)
-        ops.head_linear(y2[:, Hh:], self.w6v, self.b6v, vis)
+        ops.head_linear(y2, self.w6, self.b6, out)
+        lg = out[:, :nb2]
         ops.soft_argmax(lg, cfg.track_bins, cfg.track_window, cfg.track_temperature, tr)
-        return tr, lg, vis[:, 0]
+        return tr, lg, out[:, nb2]
 
 
 class TapNextPPStep:
@@ -180,8 +188,8 @@ class TapNextPPStep:
         assert self.heads is not None, "TapNextPPStep(heads=...) is needed for tracks"
         out = self.step(frame, queries)
         h = self.heads
-        Q = self.cfg.n_queries
-        return h.tracks[:Q], h.logits[:Q], h.vis[:Q, 0], out[self.cfg.n_img_tok:]
+        Q, nb2 = self.cfg.n_queries, 2 * self.cfg.track_bins
+        return h.tracks[:Q], h.out[:Q, :nb2], h.out[:Q, nb2], out[self.cfg.n_img_tok:]
 
     def _run(self, frame, queries, k, first):
         cfg = self.cfg

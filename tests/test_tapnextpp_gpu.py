@@ -133,6 +133,27 @@ def test_track_heads_against_reference_heads_np():
     assert device_status(clear=True) == 0
 
 
+@pytest.mark.parametrize("x_bf16", [True, False])
+def test_head_linear_ring_kernel_equals_plain_kernel(x_bf16):
+    """vt_head_linear's two kernels give the same fp32 results bit for bit: the cp.async-ring kernel (16-byte
+    aligned rows, N % 4 == 0) and the plain one (taken here by N = 515 on the same rows and pitches) both sum
+    every output over k in order with fp32 FMAs.  A partial row block (M = 77) and a float64 check."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    M, K, N = 77, 768, 516
+    x = torch.randn(M, K, device=DEV, generator=g)
+    x = x.to(BF) if x_bf16 else x
+    w = torch.randn(K, N, device=DEV, generator=g)
+    b = torch.randn(N, device=DEV, generator=g)
+    y_ring = torch.full((M, N), float("nan"), device=DEV)
+    ops.head_linear(x, w, b, y_ring)
+    y_plain = torch.full((M, N), float("nan"), device=DEV)
+    ops.head_linear(x, w[:, :515], b, y_plain[:, :515])
+    torch.cuda.synchronize()
+    assert torch.equal(y_ring[:, :515], y_plain[:, :515])
+    ref = x.double() @ w.double() + b.double()
+    assert torch.allclose(y_ring.double(), ref, rtol=1e-4, atol=1e-3)
+
+
 def test_tapnextpp_track_runs_the_heads_inside_the_step():
     """TapNextPPStep(heads=...).track: the tracks of frames replayed from the CUDA graph equal TrackHeads run on
     the step's own query tokens, and the oracle heads of those tokens (CPU fp32) within 1e-3 px."""
