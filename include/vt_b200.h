@@ -78,6 +78,20 @@ int vt_gemm_fused_ws(cudaStream_t stream, const uint16_t* A, long long lda, cons
                      const float* ln_moments, const float* ln_c, int tiles_T, int tiles_H, int tiles_D, void* ws,
                      long long ws_bytes);
 
+/* vt_gemm_fused_ws whose folded norm takes its row factors straight from the 32-column chunk statistics that
+ * the last writer of the A rows left (a stats_out of an earlier call): ln_stats [M][ln_nchunk] (mean, M2) float
+ * pairs, merged in this GEMM's epilogue as vt_row_moments does (ln_rms != 0: as vt_row_rms does, an RMSNorm
+ * with mean 0), so the separate row-moment pass and its launch go away.  ln_mom_out [M] (may be NULL)
+ * receives the (mean, rstd) pairs for a later kernel.  Every other argument as for vt_gemm_fused_ws.
+ * Replaces: the same pre-norm + linear pairs as vt_gemm_fused with ln_moments (md2fast.py:153-154, 157; the
+ * TAPNext++ block's norms before linear_yx / ffw_up / qkv / fc1, tapnext/npu/step8.py:474-486). */
+int vt_gemm_fused_lnstats(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw,
+                          int M, int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu,
+                          const void* res, long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2,
+                          float* stats_out, const float* ln_stats, int ln_nchunk, float ln_eps, int ln_rms,
+                          const float* ln_c, float* ln_mom_out, int tiles_T, int tiles_H, int tiles_D, void* ws,
+                          long long ws_bytes);
+
 /* Per-token int8 quantisation of the activation rows of a W8A8 GEMM: s[m] = max(max_k |x[m,k]|, 1e-5) / 127
  * and q[m,k] = trunc(x[m,k] / s[m] +- 0.5) (round half away from zero, IEEE fp32 division and addition),
  * from x bf16 [M, K] (pitch ldx elements, 16-byte aligned) into q int8 (pitch ldq bytes, 8-byte aligned);

@@ -22,6 +22,8 @@ SIGNATURES = {
     "vt_gemm_fused": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, P, I, I, I]),
     "vt_gemm_ws_bytes": (LL, [I, I]),
     "vt_gemm_fused_ws": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, P, I, I, I, P, LL]),
+    "vt_gemm_fused_lnstats": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL, P, P, I, F, I, P, P, I, I,
+                                  I, P, LL]),
     "vt_quant_rows": (I, [P, P, LL, I, I, P, LL, P]),
     "vt_layernorm_quant": (I, [P, P, LL, I, P, P, I, I, F, P, LL, P, P, LL]),
     "vt_gemm_i8": (I, [P, P, LL, P, LL, P, P, I, I, I, P, P, LL, I, I, P, LL, I, P, LL]),

@@ -85,7 +85,59 @@ struct Epi {
   // bf16 GEMM's rule)
   const float* i8_sa;
   const float* i8_sw;
+  // The same LayerNorm / RMSNorm fold with the row factors merged here from chunk statistics (ln_stats != null
+  // instead of ln_moments; vt_gemm_fused_lnstats): ln_stats[m * ln_nchunk + j] = (mean, M2) of 32-column chunk
+  // j of row m, merged as vt_row_moments / vt_row_rms do (ln_rms: mean 0, rstd from the mean square); the
+  // tiles of column block 0 also store (mean, rstd) of their rows in ln_mom_out when it is set
+  const float2* ln_stats;
+  int ln_nchunk;
+  float ln_eps;
+  int ln_rms;
+  float2* ln_mom_out;
 };
+
+__host__ __device__ __forceinline__ bool ln_folded(const Epi& ep) { return ep.ln_moments || ep.ln_stats; }
+
+// (mean, rstd) of A row m for a folded norm (left as (0, 1) without one); issued by the epilogue threads before
+// they wait for the tile's accumulator, so the loads overlap the MMAs.  The merge is vt_row_moments' (mean of
+// the chunk means, M2 = sum of chunk M2 + 32 (chunk mean - mean)^2) summed in chunk order by one thread.
+__device__ __forceinline__ void ln_row_factors(const Epi& ep, int m, int M, bool store, float& mu, float& rstd) {
+  if (m >= M) return;
+  if (ep.ln_moments) {
+    const float2 mr = ep.ln_moments[m];
+    mu = mr.x;
+    rstd = mr.y;
+    return;
+  }
+  if (!ep.ln_stats) return;
+  const float2* st = ep.ln_stats + (size_t)m * ep.ln_nchunk;
+  const int n = ep.ln_nchunk;
+  const float inv = 1.f / (32.f * (float)n);
+  if (ep.ln_rms) {
+    float q = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < n; i++) {
+      const float2 v = st[i];
+      q += v.y + 32.f * v.x * v.x;
+    }
+    mu = 0.f;
+    rstd = rsqrtf(q * inv + ep.ln_eps);
+  } else {
+    float sum = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < n; i++) sum += st[i].x;
+    mu = sum / (float)n;
+    float m2 = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < n; i++) {
+      const float2 v = st[i];
+      const float d = v.x - mu;
+      m2 += v.y + 32.f * d * d;
+    }
+    rstd = rsqrtf(m2 * inv + ep.ln_eps);
+  }
+  if (store && ep.ln_mom_out) ep.ln_mom_out[m] = make_float2(mu, rstd);
+}
 
 // Split-K slices of one launch (the workspace holds this many partial planes).
 constexpr int kMaxSplit = 16;
@@ -138,7 +190,7 @@ __device__ __forceinline__ void epilogue_chunk_partial(const uint32_t (&r)[32], 
     for (int j = 0; j < 32; j++)
       if (n0 + j < N) v[j] = __fmul_rn(v[j], ep.i8_sw[n0 + j]);
   }
-  if (ep.ln_moments) {
+  if (ln_folded(ep)) {
     if (full) {
       const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
 #pragma unroll
@@ -320,7 +372,7 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
       v[2 * j + 1] = f2_mul(v[2 * j + 1], f2_pack(sw.z, sw.w));
     }
   }
-  if (ep.ln_moments) {  // rstd * (acc - mean * c) + bias = rstd * acc + (bias - rstd * mean * c)
+  if (ln_folded(ep)) {  // rstd * (acc - mean * c) + bias = rstd * acc + (bias - rstd * mean * c)
     const unsigned long long rs = f2_pack(rstd, rstd), nrm = f2_pack(-rstd * mu, -rstd * mu);
     const float4* c4 = reinterpret_cast<const float4*>(ep.ln_c + n0);
     const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0);
@@ -603,11 +655,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int mt = t / nN, nt = t % nN;
       const int m = mt * BM + row;
       float mu = 0.f, rstd = 1.f, sa = 1.f;
-      if (ep.ln_moments && m < M) {  // issued before the wait: the load overlaps the tile's MMAs
-        const float2 mr = ep.ln_moments[m];
-        mu = mr.x;
-        rstd = mr.y;
-      }
+      ln_row_factors(ep, m, M, nt == 0 && half == 0, mu, rstd);  // before the wait: overlaps the tile's MMAs
       if (I8 && m < M) sa = ep.i8_sa[m];
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
       tc_fence_after();
@@ -887,11 +935,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int mt = t / nN, nt = t % nN;
       const int m = mt * 256 + (int)rank * 128 + row;
       float mu = 0.f, rstd = 1.f, sa = 1.f;
-      if (ep.ln_moments && m < M) {
-        const float2 mr = ep.ln_moments[m];
-        mu = mr.x;
-        rstd = mr.y;
-      }
+      ln_row_factors(ep, m, M, nt == 0 && half == 0, mu, rstd);
       if (I8 && m < M) sa = ep.i8_sa[m];
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * CH * 32);
       const int nbase = nt * BN + half * CH * 32;
@@ -1082,7 +1126,7 @@ static bool pair_mode2_ok(const Epi& ep, int N, int K) {
     return e ? atoi(e) : 1;
   }();
   return enabled && K <= 2048 && ep.res && !ep.res_bf16 && ep.res_period == 0 && ep.out_f32 && !ep.gelu &&
-         ep.pk_T == 0 && !ep.ln_moments && N % 32 == 0 && ep.ldr % 4 == 0 && ep.ldo % 4 == 0 &&
+         ep.pk_T == 0 && !ln_folded(ep) && N % 32 == 0 && ep.ldr % 4 == 0 && ep.ldo % 4 == 0 &&
          (!ep.out2 || ep.ldo2 % 8 == 0);
 }
 
@@ -1237,6 +1281,10 @@ static int launch(cudaStream_t st, const void* A, long long lda, const void* W, 
     return set_error(E_VARIANT, "vt_gemm: row statistics need an fp32 output with N %% 32 == 0");
   if (ep.ln_moments && (!ep.ln_c || !aligned16(ep.ln_c) || (reinterpret_cast<uintptr_t>(ep.ln_moments) & 7)))
     return set_error(E_VARIANT, "vt_gemm: folded LayerNorm needs ln_c (16-byte aligned) and 8-byte aligned moments");
+  if (ep.ln_stats && (ep.ln_moments || !ep.ln_c || !aligned16(ep.ln_c) || ep.ln_nchunk < 1 ||
+                      (reinterpret_cast<uintptr_t>(ep.ln_stats) & 7) || (reinterpret_cast<uintptr_t>(ep.ln_mom_out) & 7)))
+    return set_error(E_VARIANT, "vt_gemm: folded norm from chunk statistics needs ln_c (16-byte aligned), nchunk >= 1, "
+                                "8-byte aligned statistics / moments and no ln_moments");
 
   // 256-wide tiles by default: measured on B200 they beat 192-wide ones on every tower shape, even where
   // 192 divides N exactly (N = 1152, 3456).  VT_GEMM_BN=192 selects the 192-wide tile (tuning switch,
@@ -1364,6 +1412,35 @@ int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const ui
                    tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
                    reinterpret_cast<const float2*>(ln_moments), ln_c, 0};
+  const int rc = vt::gemm::set_workspace(ep, ws, ws_bytes, M, N);
+  if (rc) return rc;
+  return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);
+}
+
+// vt_gemm_fused_ws with the folded norm's row factors merged in the epilogue from the chunk statistics that
+// the last writer of the A rows left (ln_stats [M][ln_nchunk] float pairs; ln_rms selects RMSNorm) instead of
+// a vt_row_moments / vt_row_rms pass; ln_mom_out (may be null) receives the (mean, rstd) pairs.
+int vt_gemm_fused_lnstats(cudaStream_t st, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M,
+                          int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu,
+                          const void* res, long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2,
+                          float* stats_out, const float* ln_stats, int ln_nchunk, float ln_eps, int ln_rms,
+                          const float* ln_c, float* ln_mom_out, int tiles_T, int tiles_H, int tiles_D, void* ws,
+                          long long ws_bytes) {
+  using namespace vt;
+  if (!ln_stats) return set_error(E_SHAPE, "vt_gemm_fused_lnstats: ln_stats is required");
+  if (tiles_T > 0) {
+    if (tiles_H <= 0 || tiles_D <= 0 || tiles_D % 8 || tiles_D > 80 || M % tiles_T || N != 3 * tiles_H * tiles_D ||
+        out_f32 || gelu || res || out2 || stats_out || !aligned16(out))
+      return set_error(E_SHAPE, "vt_gemm_fused_lnstats: attention-tile output needs bf16, N = 3*H*D, M a multiple of T");
+  }
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
+                   tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
+                   tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out), nullptr, ln_c, 0};
+  ep.ln_stats = reinterpret_cast<const float2*>(ln_stats);
+  ep.ln_nchunk = ln_nchunk;
+  ep.ln_eps = ln_eps;
+  ep.ln_rms = ln_rms ? 1 : 0;
+  ep.ln_mom_out = reinterpret_cast<float2*>(ln_mom_out);
   const int rc = vt::gemm::set_workspace(ep, ws, ws_bytes, M, N);
   if (rc) return rc;
   return vt::gemm::launch(st, A, lda, W, ldw, M, N, K, ep);

@@ -53,16 +53,30 @@ def as_gemm_operand(x2):
 
 
 def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=None, out_f32=False, out2=None,
-         stats_out=None, ln=None, tiles=None, ws=None):
+         stats_out=None, ln=None, tiles=None, ws=None, ln_rows=None):
     """out[M, N] = x2 . w^T + bias (+ GELU) (+ res), see vt_gemm_fused in include/vt_b200.h.
     stats_out: [M, N/32, 2] fp32 row-chunk statistics of the (fp32) output; ln: (moments [M, 2], c) of a
-    LayerNorm folded into this GEMM; tiles: (T, H, D) to scatter into the attention-tile buffer `out`;
+    LayerNorm folded into this GEMM; ln_rows: (stats [M, nchunk, 2], eps, rms, c, moments_out or None), the same
+    fold (a LayerNorm, or an RMSNorm when rms) with the row factors merged in the epilogue from the chunk
+    statistics (vt_gemm_fused_lnstats); tiles: (T, H, D) to scatter into the attention-tile buffer `out`;
     ws: a zero-filled workspace (gemm_workspace) that lets small GEMMs split K (vt_gemm_fused_ws)."""
     M = x2.shape[0]
     if out is None:
         out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :N]
     ln_mom, ln_c = ln if ln is not None else (None, None)
     tT, tH, tD = tiles if tiles is not None else (0, 0, 0)
+    if ln_rows is not None:
+        st, eps, rms, c, mom_out = ln_rows
+        assert ln is None and st.shape[0] >= M and st.is_contiguous()
+        rc = lib().vt_gemm_fused_lnstats(
+            _stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias), out.data_ptr(),
+            out.stride(0) if tiles is None else 0, int(tiles is None and out.dtype == torch.float32), int(gelu),
+            _ptr(res), 0 if res is None else res.stride(0), int(res_period), int(res is not None and res.dtype == BF16),
+            _ptr(out2), 0 if out2 is None else out2.stride(0), _ptr(stats_out), st.data_ptr(), st.shape[1],
+            float(eps), int(rms), c.data_ptr(), _ptr(mom_out), tT, tH, tD, _ptr(ws),
+            0 if ws is None else ws.numel() * ws.element_size())
+        check(rc, "vt_gemm_fused_lnstats")
+        return out
     rc = lib().vt_gemm_fused_ws(_stream(), x2.data_ptr(), x2.stride(0), w.data_ptr(), ldw, M, N, K, _ptr(bias),
                                 out.data_ptr(), out.stride(0) if tiles is None else 0,
                                 int(tiles is None and out.dtype == torch.float32), int(gelu), _ptr(res),

@@ -8,15 +8,18 @@ new video.
 
 Per block the kernels are the tower's (vt_gemm_qkv_tiles + vt_attn_tiles_fwd with d = 64, vt_gemm_fused) plus
 the RG-LRU.  With fold_ln=True (default) every norm is folded into the GEMM after it, as in the tower:
-    mom = (mean, rstd) of x             vt_row_moments, from the chunk statistics the last writer of x left
+    (mean, rstd) of x                   from the chunk statistics the last writer of x left (see below)
     qkv = LN1(x) . Wqkv^T + b           folded LN1 (A = bf16 copy of x, W * gamma1), tile scatter
     x  += attn . Wo^T + b               residual epilogue + bf16 copy + chunk statistics
     f   = gelu(LN2(x) . W1^T + b)       folded LN2
     x  += f . W2^T + b                  residual epilogue + bf16 copy + chunk statistics
-    mom = (0, rstd) of x                vt_row_rms
+    (0, rstd) of x                      the same, RMSNorm
     G   = RMSNorm(x) . [Wx; Wa]^T + b   folded RMSNorm (W * gamma), N = 1536, fp32 out
     vt_rglru_fold                       t = bf16(x rstd gamma), gates, recurrence, state, x += h, and the bf16 copy
                                         and chunk statistics of the new x for the next block's LN1
+By default (rows_in_gemm=True) no row-moment pass runs: each folded GEMM merges the chunk statistics into its
+rows' (mean, rstd) in its own epilogue (vt_gemm_fused_lnstats), and the gate GEMM also stores the RMS factors
+that vt_rglru_fold reads; rows_in_gemm=False keeps the vt_row_moments / vt_row_rms passes.
 With fold_ln=False the norms run as vt_layernorm / vt_rmsnorm passes and the gate step as RgLruGate.
 """
 import torch
@@ -51,9 +54,11 @@ class RgLruGate:
 
 
 class TapNextStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, fold_ln=True):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, fold_ln=True,
+                 rows_in_gemm=True):
         self.cfg = cfg
         self.fold_ln = fold_ln
+        self.rows_in_gemm = rows_in_gemm
         self.use_graphs = graphs
         self._graph = None
         self._frame_in = self._q_in = None
@@ -155,24 +160,31 @@ class TapNextStep:
             blk["lru"](self.t, self.state[i], self.x, first)
         ops.layer_norm(self.x, self.fin_w, self.fin_b, cfg.eps, out=self.out)
 
+    def _norm(self, c, rms, keep=False):
+        """gemm keyword arguments of a norm of x folded into the GEMM that follows (c = its rowsum vector):
+        the row factors merged from x's chunk statistics in that GEMM's epilogue (stored in self.mom when keep),
+        or, with rows_in_gemm=False, computed into self.mom by a row-moment pass launched here."""
+        cfg = self.cfg
+        if self.rows_in_gemm:
+            return dict(ln_rows=(self.stats, cfg.eps, rms, c, self.mom if keep else None))
+        (ops.row_rms if rms else ops.row_moments)(self.stats, cfg.eps, self.mom)
+        return dict(ln=(self.mom, c))
+
     def _blocks_folded(self, first):
         cfg = self.cfg
         T, Wd = cfg.ntok, cfg.width
         fold = dict(out2=self.xb, stats_out=self.stats)
         ops.row_stats(self.x, self.stats, self.xb)
         for i, blk in enumerate(self.blocks):
-            ops.row_moments(self.stats, cfg.eps, self.mom)
             ops.gemm(self.xb, blk["qkv_wf"], blk["qkv_ldf"], Wd, 3 * Wd, blk["qkv_bf"], out=self.tiles,
-                     ln=(self.mom, blk["qkv_c"]), tiles=(T, cfg.heads, cfg.head_dim))
+                     tiles=(T, cfg.heads, cfg.head_dim), **self._norm(blk["qkv_c"], False))
             ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
             ops.gemm(self.a, blk["proj_w"], blk["proj_ld"], Wd, Wd, blk["proj_b"], res=self.x, out=self.x, **fold)
-            ops.row_moments(self.stats, cfg.eps, self.mom)
             ops.gemm(self.xb, blk["fc1_wf"], blk["fc1_ldf"], Wd, cfg.ff, blk["fc1_bf"], gelu=True,
-                     out=self.f[:, :cfg.ff], ln=(self.mom, blk["fc1_c"]))
+                     out=self.f[:, :cfg.ff], **self._norm(blk["fc1_c"], False))
             ops.gemm(self.f[:, :cfg.ff], blk["fc2_w"], blk["fc2_ld"], cfg.ff, Wd, blk["fc2_b"], res=self.x, out=self.x,
                      **fold)
-            ops.row_rms(self.stats, cfg.eps, self.mom)
             ops.gemm(self.xb, blk["gate_wf"], blk["gate_ldf"], Wd, 2 * Wd, blk["gate_b"], out=self.G,
-                     ln=(self.mom, blk["gate_c"]))
+                     **self._norm(blk["gate_c"], True, keep=True))
             ops.rglru_fold(self.G, blk["lru"].a_param, self.mom, blk["rms_w"], self.state[i], self.x, self.xb,
                            self.stats, cfg.lru_c, first)

@@ -90,8 +90,10 @@ class TrackHeads:
 
 
 class TapNextPPStep:
-    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, heads=None, fold_ln=True):
+    def __init__(self, weights, cfg: TapNextConfig = TAPNEXT, device="cuda", graphs=True, heads=None, fold_ln=True,
+                 rows_in_gemm=True):
         self.cfg = cfg
+        self.rows_in_gemm = rows_in_gemm
         self.fold_ln = fold_ln
         self.use_graphs = graphs
         self._graphs = {}
@@ -232,10 +234,20 @@ class TapNextPPStep:
             ops.gelu_erf(self.f)
             ops.gemm(self.f, b["fc2_w"], b["fc2_ld"], Fh, Wd, b["fc2_b"], res=self.x, out=self.x)
 
+    def _norm(self, c, rms):
+        """gemm keyword arguments of a norm of x folded into the GEMM that follows (c = its rowsum vector): the row
+        factors merged from x's chunk statistics in that GEMM's epilogue, or, with rows_in_gemm=False, computed
+        into self.mom by a vt_row_rms / vt_row_moments pass launched here."""
+        cfg = self.cfg
+        if self.rows_in_gemm:
+            return dict(ln_rows=(self.stats, cfg.eps, rms, c, None))
+        (ops.row_rms if rms else ops.row_moments)(self.stats, cfg.eps, self.mom)
+        return dict(ln=(self.mom, c))
+
     def _blocks_folded(self, k, first):
         """The same blocks with every norm folded into the GEMM after it: the residual GEMMs (linear_out,
         ffw_down, out_proj, mlp.3) also write the bf16 copy of x and its 32-column chunk statistics, from which
-        vt_row_rms / vt_row_moments give the next norm's row factors."""
+        the next folded GEMM's epilogue takes its rows' norm factors (see _norm)."""
         cfg = self.cfg
         T, Wd, Fh = cfg.ntok, cfg.width, cfg.ff
         fold = dict(out2=self.xb, stats_out=self.stats)
@@ -243,24 +255,20 @@ class TapNextPPStep:
         for i, b in enumerate(self.blocks):
             hist = (self.hist[i, k], self.hist[i, (k + 1) % 3], self.hist[i, (k + 2) % 3])
             # recurrent block (step8.py:474-481)
-            ops.row_rms(self.stats, cfg.eps, self.mom)
-            ops.gemm(self.xb, b["yx_wf"], b["yx_ldf"], Wd, 2 * Wd, b["yx_bf"], out=self.yx, ln=(self.mom, b["yx_c"]))
+            ops.gemm(self.xb, b["yx_wf"], b["yx_ldf"], Wd, 2 * Wd, b["yx_bf"], out=self.yx, **self._norm(b["yx_c"], True))
             ops.ssm_step(self.yx[:, :Wd], self.yx[:, Wd:], hist, self.h[i], b["conv_w"], b["conv_b"],
                          b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first, gelu_y=True)
             ops.gemm(self.z, b["out_w"], b["out_ld"], Wd, Wd, b["out_b"], res=self.x, out=self.x, **fold)
             # gated MLP (step8.py:482-483)
-            ops.row_rms(self.stats, cfg.eps, self.mom)
-            ops.gemm(self.xb, b["up_wf"], b["up_ldf"], Wd, 2 * Fh, b["up_bf"], out=self.G, ln=(self.mom, b["up_c"]))
+            ops.gemm(self.xb, b["up_wf"], b["up_ldf"], Wd, 2 * Fh, b["up_bf"], out=self.G, **self._norm(b["up_c"], True))
             ops.gated_gelu_mul(self.G, self.m)
             ops.gemm(self.m, b["down_w"], b["down_ld"], Fh, Wd, b["down_b"], res=self.x, out=self.x, **fold)
             # ViT block (step8.py:484-486)
-            ops.row_moments(self.stats, cfg.eps, self.mom)
             ops.gemm(self.xb, b["qkv_wf"], b["qkv_ldf"], Wd, 3 * Wd, b["qkv_bf"], out=self.tiles,
-                     ln=(self.mom, b["qkv_c"]), tiles=(T, cfg.heads, cfg.head_dim))
+                     tiles=(T, cfg.heads, cfg.head_dim), **self._norm(b["qkv_c"], False))
             ops.attention_tiles(self.tiles, 1, T, cfg.heads, cfg.head_dim, self.a)
             ops.gemm(self.a, b["proj_w"], b["proj_ld"], Wd, Wd, b["proj_b"], res=self.x, out=self.x, **fold)
-            ops.row_moments(self.stats, cfg.eps, self.mom)
-            ops.gemm(self.xb, b["fc1_wf"], b["fc1_ldf"], Wd, Fh, b["fc1_bf"], out=self.f, ln=(self.mom, b["fc1_c"]))
+            ops.gemm(self.xb, b["fc1_wf"], b["fc1_ldf"], Wd, Fh, b["fc1_bf"], out=self.f, **self._norm(b["fc1_c"], False))
             # the exact GELU as its own pass: in fc1's epilogue (one 256 x 256 tile per CTA pair at 1280 rows, so
             # nothing hides it) it measured 20 us per frame slower
             ops.gelu_erf(self.f)

@@ -126,6 +126,36 @@ def test_gemm_folded_layernorm(gelu):
     assert rel(out, ref) < 8e-3
 
 
+@pytest.mark.parametrize("M,N,rms", [(1280, 2304, False), (1280, 1536, True), (96, 64, False), (37, 768, True)])
+def test_gemm_norm_factors_merged_in_the_epilogue(M, N, rms):
+    """vt_gemm_fused_lnstats (the folded norm's row factors merged from the chunk statistics in the epilogue)
+    against the same GEMM fed by a vt_row_moments / vt_row_rms pass: the factors it stores (ln_mom_out) and its
+    outputs match to fp32 rounding (the chunks are summed in another order); CTA-pair tiles (1280 rows) and
+    single-CTA tiles (few tiles), LayerNorm and RMSNorm, a partial row block."""
+    K = 768
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(M, K, device=DEV, generator=g) * 2 + 0.3
+    w = torch.randn(N, K, device=DEV, generator=g) * 0.02
+    b = torch.randn(N, device=DEV, generator=g) * 0.1
+    gamma = 1 + 0.1 * torch.randn(K, device=DEV, generator=g)
+    beta = torch.zeros(K, device=DEV) if rms else 0.05 * torch.randn(K, device=DEV, generator=g)
+    stats = torch.empty(M, K // 32, 2, device=DEV)
+    xb = torch.empty(M, K, device=DEV, dtype=BF)
+    ops.row_stats(x, stats, xb)
+    wf, c, bf = ops.fold_layernorm(w, b, gamma, beta)
+    wf, c, bf = wf.contiguous(), c.to(DEV), bf.to(DEV)
+    mom_ref = (ops.row_rms if rms else ops.row_moments)(stats, 1e-6, torch.empty(M, 2, device=DEV))
+    out_ref = ops.gemm(xb, wf, K, K, N, bf, out_f32=True, ln=(mom_ref, c))
+    mom = torch.full((M, 2), float("nan"), device=DEV)
+    out = ops.gemm(xb, wf, K, K, N, bf, out_f32=True, ln_rows=(stats, 1e-6, rms, c, mom))
+    torch.cuda.synchronize()
+    assert torch.allclose(mom, mom_ref, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(out, out_ref, rtol=1e-4, atol=1e-4)
+    if not rms:
+        ref = F.linear(F.layer_norm(x, (K,), gamma, beta, 1e-6), w, b)
+        assert rel(out, ref) < 8e-3
+
+
 @pytest.mark.parametrize("bn", ["192", "256"])
 def test_gemm_both_tile_widths_in_a_subprocess(bn):
     """VT_GEMM_BN forces the 192- or 256-wide N tile: both give correct results on the tower shapes."""

@@ -14,15 +14,19 @@ from helpers import assert_tokens_close
 CFG = TapNextConfig()
 
 
-@pytest.mark.parametrize("n_blocks,n_frames,affine,fold_ln", [(12, 16, "zero", True), (3, 16, "random", True),
-                                                             (3, 16, "random", False)])
-def test_tapnext_stream(n_blocks, n_frames, affine, fold_ln):
+NORMS = {"in_gemm": dict(), "row_pass": dict(rows_in_gemm=False), "unfolded": dict(fold_ln=False)}
+
+
+@pytest.mark.parametrize("n_blocks,n_frames,affine,norms", [(12, 16, "zero", "in_gemm"), (3, 16, "random", "in_gemm"),
+                                                           (3, 16, "random", "row_pass"), (3, 16, "random", "unfolded")])
+def test_tapnext_stream(n_blocks, n_frames, affine, norms):
     """Config 3 as BASELINE states it (12 blocks, 16 frames, state carried) and a random-affine stack, with the
-    norms folded into the GEMMs (default) and as separate passes: every frame within the per-token tolerance."""
+    norms folded into the GEMMs and their row factors merged in those GEMMs' epilogues (default), folded with a
+    row-moment pass before each, and as separate norm passes: every frame within the per-token tolerance."""
     device_status(clear=True)
     W = wg.tapnext_weights(CFG, seed=8, n_blocks=n_blocks, affine=affine)
     frames, queries = wg.tapnext_inputs(CFG, n_frames, seed=2)
-    eng = TapNextStep(W, CFG, device="cuda", fold_ln=fold_ln)
+    eng = TapNextStep(W, CFG, device="cuda", **NORMS[norms])
     state = None
     for f in range(n_frames):
         ref, state = tapnext_ref.step(frames[f], queries[f], W, CFG, state, n_blocks)

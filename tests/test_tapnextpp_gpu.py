@@ -73,15 +73,19 @@ def test_gated_gelu_mul_and_gelu_erf():
     assert torch.allclose(x.float(), ref2, rtol=1e-2, atol=1e-3)
 
 
-@pytest.mark.parametrize("n_blocks,n_frames,affine,fold_ln", [(12, 2, "zero", True), (2, 6, "random", True),
-                                                             (2, 6, "random", False)])
-def test_tapnextpp_stream(n_blocks, n_frames, affine, fold_ln):
+NORMS = {"in_gemm": dict(), "row_pass": dict(rows_in_gemm=False), "unfolded": dict(fold_ln=False)}
+
+
+@pytest.mark.parametrize("n_blocks,n_frames,affine,norms", [(12, 2, "zero", "in_gemm"), (2, 6, "random", "in_gemm"),
+                                                           (2, 6, "random", "row_pass"), (2, 6, "random", "unfolded")])
+def test_tapnextpp_stream(n_blocks, n_frames, affine, norms):
     """The full TAPNext++ step against the fp32 restatement, state and conv history carried, with the four norms
-    of a block folded into the GEMMs after them (default) and as separate passes."""
+    of a block folded into the GEMMs after them and their row factors merged in those GEMMs' epilogues
+    (default), folded with a row-moment pass before each, and as separate passes."""
     device_status(clear=True)
     W = wg.tapnextpp_weights(CFG, seed=9, n_blocks=n_blocks, affine=affine)
     frames, queries = wg.tapnext_inputs(CFG, n_frames, seed=2)
-    eng = TapNextPPStep(W, CFG, device=DEV, fold_ln=fold_ln)
+    eng = TapNextPPStep(W, CFG, device=DEV, **NORMS[norms])
     state = None
     for f in range(n_frames):
         ref, state = R.step(frames[f], queries[f], W, CFG, state, n_blocks)
