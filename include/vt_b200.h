@@ -69,9 +69,13 @@ long long vt_gemm_ws_bytes(int M, int N);
  * small M, e.g. the text decoder's 32-token question -- splits K across CTAs: each stores its fp32 partial
  * sum in the workspace and the last to finish a row chunk adds them in slice order and runs the epilogue,
  * so results are deterministic (equal to vt_gemm_fused's up to fp32 summation order).  ws = NULL is
- * vt_gemm_fused.
+ * vt_gemm_fused.  gelu = 2 here (and in vt_gemm_fused_lnstats) is the gated GELU of a gated MLP: W's rows are
+ * [gate | up] pairs interleaved in blocks of 16 (rows 32c .. 32c+15 gate channels 16c .., rows 32c+16 .. the
+ * matching up channels), N % 32 == 0, and the bf16 output has N / 2 columns, out[m][16c + i] =
+ * bf16(bf16(gelu_tanh(gate)) * up) of the bf16-rounded linear outputs (no residual, tiles or statistics).
  * Replaces: the same call sites as vt_gemm_fused (here the question prefill's linears, md2fast.py:192-199);
- * the reference's HIP GEMM has no split-K variant. */
+ * the reference's HIP GEMM has no split-K variant; with gelu = 2, ffw_up followed by the gated GELU product of
+ * the TAPNext++ MLP (tapnext/npu/step8.py:482-483, mm8.cc:937-960). */
 int vt_gemm_fused_ws(cudaStream_t stream, const uint16_t* A, long long lda, const uint16_t* W, long long ldw, int M,
                      int N, int K, const float* bias, void* out, long long ldo, int out_f32, int gelu, const void* res,
                      long long ldr, int res_period, int res_bf16, uint16_t* out2, long long ldo2, float* stats_out,

@@ -161,7 +161,7 @@ __device__ __forceinline__ void ld_words32(const void* p, uint32_t (&w)[32], boo
     }
   }
 }
-template <int NW>  // NW = 16 or 32 words
+template <int NW>  // NW = 8, 16 or 32 words (32-byte aligned when wide)
 __device__ __forceinline__ void st_words(void* p, const uint32_t* w, bool wide) {
   uint32_t* q = reinterpret_cast<uint32_t*>(p);
   if (wide) {
@@ -463,6 +463,21 @@ __device__ __forceinline__ void epilogue_chunk_rw(const uint32_t (&r)[32], const
       f2_unpack(gelu_tanh2(f2_pack(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u))), g0, g1);
       w[j] = pack_bf2(g0, g1);
     }
+  }
+  if (ep.gelu == 3) {
+    // gated: the chunk holds gate columns 16c .. 16c+15 (words 0-7) and the matching up columns (words 8-15) of a
+    // weight whose gate / up rows are interleaved in blocks of 16; out column 16c + i = bf16(bf16(gelu_tanh(gate))
+    // * up), 16 bf16 outputs at n0 / 2
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float g0, g1;
+      f2_unpack(gelu_tanh2(f2_pack(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u))), g0, g1);
+      o[j] = pack_bf2(__fmul_rn(bfround(g0), __uint_as_float(w[8 + j] << 16)),
+                      __fmul_rn(bfround(g1), __uint_as_float(w[8 + j] & 0xffff0000u)));
+    }
+    st_words<8>(reinterpret_cast<uint16_t*>(ep.out) + (long long)m * ep.ldo + n0 / 2, o, ep.wide != 0);
+    return;
   }
   if (ep.pk_T > 0) {
     // attention tiles: the chunk's four 8-column groups each lie in one head (D % 8 == 0); the head and
@@ -1261,15 +1276,19 @@ static int launch(cudaStream_t st, const void* A, long long lda, const void* W, 
   if (lda < K || ldw < K || lda % pal || ldw % pal || !aligned16(A) || !aligned16(W))
     return set_error(E_SHAPE, "vt_gemm: A/W need 16-byte aligned bases and row pitches (lda=%lld ldw=%lld K=%d)", lda,
                      ldw, K);
-  if (ep.pk_T <= 0 && (ep.ldo < N || ep.ldo % 8 || !aligned16(ep.out)))
-    return set_error(E_SHAPE, "vt_gemm: output pitch %lld must be >= N=%d, a multiple of 8, 16-byte aligned", ep.ldo,
-                     N);
+  const int n_out = ep.gelu == 3 ? N / 2 : N;  // the gated GELU writes one column per gate / up pair
+  if (ep.pk_T <= 0 && (ep.ldo < n_out || ep.ldo % 8 || !aligned16(ep.out)))
+    return set_error(E_SHAPE, "vt_gemm: output pitch %lld must be >= %d columns, a multiple of 8, 16-byte aligned",
+                     ep.ldo, n_out);
   if (ep.res && (ep.ldr < N || ep.ldr % 8 || !aligned16(ep.res) || ep.res_period < 0))
     return set_error(E_SHAPE, "vt_gemm: residual pitch %lld / period %d invalid", ep.ldr, ep.res_period);
   if (ep.out2 && (ep.ldo2 < N || ep.ldo2 % 8 || !aligned16(ep.out2)))
     return set_error(E_SHAPE, "vt_gemm: bf16 copy pitch %lld invalid", ep.ldo2);
   if (ep.bias && !aligned16(ep.bias)) return set_error(E_SHAPE, "vt_gemm: bias must be 16-byte aligned");
   if (ep.gelu && ep.out_f32) return set_error(E_VARIANT, "vt_gemm: GELU is only fused for bf16 output");
+  if (ep.gelu == 3 && (N % 32 || ep.res || ep.pk_T > 0 || ep.stats_out || ep.out2 || ep.i8_sw))
+    return set_error(E_VARIANT, "vt_gemm: the gated GELU epilogue needs N %% 32 == 0 and no residual, tiles, "
+                                "statistics or second output");
   {
     auto a32 = [](const void* p, long long ld, int es) {
       return p == nullptr || ((reinterpret_cast<uintptr_t>(p) & 31) == 0 && (ld * es) % 32 == 0);
@@ -1408,8 +1427,8 @@ int vt_gemm_fused_ws(cudaStream_t st, const uint16_t* A, long long lda, const ui
         out_f32 || gelu || res || out2 || stats_out || !aligned16(out))
       return set_error(E_SHAPE, "vt_gemm_fused: attention-tile output needs bf16, N = 3*H*D, M a multiple of T");
   }
-  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
-                   tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu == 2 ? 3 : gelu ? 1 : 0,
+                   out2, ldo2, tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out),
                    reinterpret_cast<const float2*>(ln_moments), ln_c, 0};
   const int rc = vt::gemm::set_workspace(ep, ws, ws_bytes, M, N);
@@ -1433,8 +1452,8 @@ int vt_gemm_fused_lnstats(cudaStream_t st, const uint16_t* A, long long lda, con
         out_f32 || gelu || res || out2 || stats_out || !aligned16(out))
       return set_error(E_SHAPE, "vt_gemm_fused_lnstats: attention-tile output needs bf16, N = 3*H*D, M a multiple of T");
   }
-  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu ? 1 : 0, out2, ldo2,
-                   tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
+  vt::gemm::Epi ep{bias, out, ldo, res, ldr, res_period, res_bf16 ? 1 : 0, out_f32 ? 1 : 0, gelu == 2 ? 3 : gelu ? 1 : 0,
+                   out2, ldo2, tiles_T > 0 ? tiles_T : 0, tiles_H, tiles_D, tiles_D <= 64 ? 8 : 10,
                    tiles_T > 0 ? (tiles_T + 127) / 128 : 0, reinterpret_cast<float2*>(stats_out), nullptr, ln_c, 0};
   ep.ln_stats = reinterpret_cast<const float2*>(ln_stats);
   ep.ln_nchunk = ln_nchunk;

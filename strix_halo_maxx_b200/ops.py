@@ -59,10 +59,14 @@ def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=No
     LayerNorm folded into this GEMM; ln_rows: (stats [M, nchunk, 2], eps, rms, c, moments_out or None), the same
     fold (a LayerNorm, or an RMSNorm when rms) with the row factors merged in the epilogue from the chunk
     statistics (vt_gemm_fused_lnstats); tiles: (T, H, D) to scatter into the attention-tile buffer `out`;
-    ws: a zero-filled workspace (gemm_workspace) that lets small GEMMs split K (vt_gemm_fused_ws)."""
+    ws: a zero-filled workspace (gemm_workspace) that lets small GEMMs split K (vt_gemm_fused_ws);
+    gelu="gated": w holds [gate | up] rows interleaved in blocks of 16 (gate_up_interleave) and out [M, N/2]
+    receives bf16(gelu_tanh(gate)) * up."""
     M = x2.shape[0]
+    gelu = 2 if gelu == "gated" else int(gelu)
     if out is None:
-        out = torch.empty(M, _pad8(N), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :N]
+        No = N // 2 if gelu == 2 else N
+        out = torch.empty(M, _pad8(No), dtype=torch.float32 if out_f32 else BF16, device=x2.device)[:, :No]
     ln_mom, ln_c = ln if ln is not None else (None, None)
     tT, tH, tD = tiles if tiles is not None else (0, 0, 0)
     if ln_rows is not None:
@@ -86,6 +90,14 @@ def gemm(x2, w, ldw, K, N, bias=None, gelu=False, res=None, res_period=0, out=No
                                 tT, tH, tD, _ptr(ws), 0 if ws is None else ws.numel() * ws.element_size())
     check(rc, "vt_gemm_fused_ws")
     return out
+
+
+def gate_up_interleave(t, F):
+    """Rows (or entries) [gate 0..F) | up 0..F) of a gated MLP's up projection, reordered into blocks of 16
+    gate rows followed by the matching 16 up rows (the layout gemm(gelu="gated") reads)."""
+    assert t.shape[0] == 2 * F and F % 16 == 0
+    g, u = t[:F], t[F:]
+    return torch.stack([g.reshape(F // 16, 16, *t.shape[1:]), u.reshape(F // 16, 16, *t.shape[1:])], 1).reshape(t.shape)
 
 
 def _pad16(n):

@@ -131,6 +131,8 @@ class TapNextPPStep:
                                  ("up", 1.0 + torch.as_tensor(W[p + "rms1_scale"]).float(), zero),
                                  ("qkv", W[p + "ln1_w"], W[p + "ln1_b"]), ("fc1", W[p + "ln2_w"], W[p + "ln2_b"])):
                     wf, c, bf = ops.fold_layernorm(W[p + n + "_w"], W[p + n + "_b"], g, be)
+                    if n == "up":  # gate / up rows interleaved by 16: the GEMM epilogue forms gelu(gate) * up
+                        wf, c, bf = (ops.gate_up_interleave(torch.as_tensor(t), Fh) for t in (wf, c, bf))
                     b[n + "_wf"], b[n + "_ldf"] = _dev_mat(wf, dev)
                     b[n + "_c"] = _dev_vec(c, dev)
                     b[n + "_bf"] = _dev_vec(bf, dev)
@@ -260,8 +262,8 @@ class TapNextPPStep:
                          b["softplus_a"], b["gx_w"], b["gx_b"], b["ga_w"], b["ga_b"], self.z, first, gelu_y=True)
             ops.gemm(self.z, b["out_w"], b["out_ld"], Wd, Wd, b["out_b"], res=self.x, out=self.x, **fold)
             # gated MLP (step8.py:482-483)
-            ops.gemm(self.xb, b["up_wf"], b["up_ldf"], Wd, 2 * Fh, b["up_bf"], out=self.G, **self._norm(b["up_c"], True))
-            ops.gated_gelu_mul(self.G, self.m)
+            ops.gemm(self.xb, b["up_wf"], b["up_ldf"], Wd, 2 * Fh, b["up_bf"], out=self.m, gelu="gated",
+                     **self._norm(b["up_c"], True))
             ops.gemm(self.m, b["down_w"], b["down_ld"], Fh, Wd, b["down_b"], res=self.x, out=self.x, **fold)
             # ViT block (step8.py:484-486)
             ops.gemm(self.xb, b["qkv_wf"], b["qkv_ldf"], Wd, 3 * Wd, b["qkv_bf"], out=self.tiles,

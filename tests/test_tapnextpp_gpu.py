@@ -73,6 +73,29 @@ def test_gated_gelu_mul_and_gelu_erf():
     assert torch.allclose(x.float(), ref2, rtol=1e-2, atol=1e-3)
 
 
+@pytest.mark.parametrize("M", [1280, 77])
+def test_gemm_gated_gelu_epilogue_against_gemm_then_gated_gelu_mul(M):
+    """gemm(gelu="gated") over gate / up weight rows interleaved by 16 against the same GEMM with a bf16 output
+    followed by vt_gated_gelu_mul: the linear outputs are the same, so the results differ only where the two
+    GELU-tanh formulas round to neighbouring bf16 values (a bf16 step or two of the product).  CTA-pair tiles
+    (1280 rows) and single-CTA tiles (77 rows)."""
+    K, Fh = 768, 3072
+    g = torch.Generator(device=DEV).manual_seed(12)
+    x = torch.randn(M, K, device=DEV, generator=g).to(BF)
+    w = (torch.randn(2 * Fh, K, device=DEV, generator=g) * 0.05).to(BF)
+    b = torch.randn(2 * Fh, device=DEV, generator=g) * 0.1
+    G = ops.gemm(x, w, K, K, 2 * Fh, b)
+    ref = torch.empty(M, Fh, dtype=BF, device=DEV)
+    ops.gated_gelu_mul(G, ref)
+    wi, bi = ops.gate_up_interleave(w, Fh).contiguous(), ops.gate_up_interleave(b, Fh).contiguous()
+    out = ops.gemm(x, wi, K, K, 2 * Fh, bi, gelu="gated")
+    torch.cuda.synchronize()
+    assert out.shape == (M, Fh)
+    d = (out.float() - ref.float()).abs()
+    assert float((d > 0).float().mean()) < 5e-2
+    assert torch.all(d <= ref.float().abs() * 2 ** -6 + 1e-6)
+
+
 NORMS = {"in_gemm": dict(), "row_pass": dict(rows_in_gemm=False), "unfolded": dict(fold_ln=False)}
 
 
