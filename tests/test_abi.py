@@ -70,3 +70,24 @@ def test_int8_entry_points_validate_on_the_host():
     # empty problems are no-ops
     assert L.vt_quant_rows(None, 16, 16, 0, 16, 16, 16, 16) == 0
     assert L.vt_gemm_i8(None, 16, 64, 16, 64, None, None, 0, 8, 64, None, 16, 8, 0, 0, None, 0, 0, None, 0) == 0
+
+
+def test_fused_gemm_and_head_entry_points_validate_on_the_host():
+    """vt_gemm_fused_lnstats, the gated GELU mode of vt_gemm_fused_ws and vt_head_linear reject bad arguments
+    before any CUDA call (fake 16-byte aligned addresses, never dereferenced)."""
+    L = _lib.lib()
+    A = W = O = S = 4096
+    common = (None, A, 64, W, 64, 4, 64, 64, None, O, 64, 0)   # stream .. out_f32 (M 4, N 64, K 64)
+    tail = (None, 0, 0, 0, None, 0, None)                      # res, ldr, res_period, res_bf16, out2, ldo2, stats_out
+    # no chunk statistics
+    assert L.vt_gemm_fused_lnstats(*common, 0, *tail, None, 2, 1e-6, 0, S, None, 0, 0, 0, None, 0) == -2
+    assert b"ln_stats is required" in L.vt_last_error_string()
+    # statistics without the rowsum vector ln_c
+    assert L.vt_gemm_fused_lnstats(*common, 0, *tail, S, 2, 1e-6, 0, None, None, 0, 0, 0, None, 0) == -1
+    assert b"chunk statistics" in L.vt_last_error_string()
+    # the gated GELU needs N % 32 == 0 (N = 48 here) and a bf16 output
+    gated = (None, A, 64, W, 64, 4, 48, 64, None, O, 64, 0, 2)
+    assert L.vt_gemm_fused_ws(*gated, *tail, None, None, 0, 0, 0, None, 0) == -1
+    assert b"gated GELU" in L.vt_last_error_string()
+    # head GEMM: K = 0
+    assert L.vt_head_linear(None, A, 64, 1, W, 64, None, O, 64, 4, 64, 0) == -2
