@@ -11,7 +11,9 @@
 // allocation and never written there).  The tower's QKV GEMM writes this layout from its epilogue;
 // vt_attn_pack builds it from any strided Q/K/V.
 //
-// CTA = one 128-query tile of one (crop, head), 2 CTAs per SM; 6 warps:
+// CTA = one 128-query tile of one (crop, head), or one 64-query half of it (QR = 64, M = 64 MMAs, for grids of
+// fewer than two 128-query CTAs per SM: the accumulator rows then sit in lanes 0-15 of each TMEM lane quarter,
+// lanes 16-31 of every warp carry no row), 2 CTAs per SM; 6 warps:
 //   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, KVS-stage rings);
 //   warp 5 lane 0: tcgen05.mma  S_j = Q K_j^T (M 128, N 64, K DP) into one of two TMEM S buffers, then
 //                  O += P_j V_j (M 128, N DP, K 64; P read from TMEM, V an MN-major B operand in shared
@@ -65,7 +67,7 @@ struct Args {
 //                into the first 32 columns of S buffer j%2 (tcgen05.st), arrive.  The MMA reads P_j from tensor
 //                memory (A operand); S_(j+2), the next writer of that buffer, is issued after PV_j and the
 //                tensor core runs them in order.
-template <int NC>
+template <int NC, int QR>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   using L = Smem<NC>;
   constexpr int DP = NC * 8;
@@ -85,7 +87,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tt = blockIdx.x, h = blockIdx.y, b = a.b0 + blockIdx.z;
+  const int tt = QR == 128 ? blockIdx.x : blockIdx.x >> 1, hq = QR == 128 ? 0 : blockIdx.x & 1;
+  const int h = blockIdx.y, b = a.b0 + blockIdx.z;
   const int T = a.T, H = a.H, Tt = a.Tt;
   const int nkv = (T + BKV - 1) / BKV;
   const size_t tile_elems = (size_t)NC * 1024;  // one 128-row tile of one operand
@@ -150,8 +153,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   } else if (warp == 5) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV);
-      constexpr uint32_t IDESC_O = idesc_bf16(BQ, DP) | (1u << 16);  // B (= V) MN-major
+      constexpr uint32_t IDESC_S = idesc_bf16(QR, BKV);
+      constexpr uint32_t IDESC_O = idesc_bf16(QR, DP) | (1u << 16);  // B (= V) MN-major
       const uint32_t sq = smem_u32(sm + L::Q), sk = smem_u32(sm + L::K), sv = smem_u32(sm + L::V);
       // S_j = Q K_j^T into S buffer j%2; k_ready: K_j is known to have landed (checked off the S chain)
       auto issue_s = [&](int j, bool k_ready) -> bool {
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         const uint32_t kb = sk + ks * L::KT;
 #pragma unroll
         for (int k = 0; k < NC / 2; k++)  // K = 16 per MMA: Q chunks 2k, 2k+1 (2048 B apart), K chunks (1024 B apart)
-          umma_f16(tmem + s * BKV, sdesc_noswz(sq + k * 4096, 2048, 128), sdesc_noswz(kb + k * 2048, 1024, 128),
+          umma_f16(tmem + s * BKV, sdesc_noswz(sq + hq * 1024 + k * 4096, 2048, 128), sdesc_noswz(kb + k * 2048, 1024, 128),
                    IDESC_S, k > 0 ? 1u : 0u);
         umma_commit(&s_full[s]);  // first: the softmax warps wait on this one
         umma_commit(&k_empty[ks]);
@@ -196,7 +199,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
     }
   } else {
     // ---------------- softmax warps 0-3: thread = query row
-    const int row = warp * 32 + lane;
+    const bool has_row = QR == 128 || lane < 16;  // M = 64: rows 16w .. 16w+15 in lanes 0-15 of quarter w
+    const int row = QR == 128 ? warp * 32 + lane : warp * 16 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       if (j == 0) {
         m_used = mx;
       } else {
-        const bool need = mx > m_used + kRescaleThreshold;
+        const bool need = has_row && mx > m_used + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {  // O round trip through registers (warp-collective), rare
           // O must hold every P.V up to j-1: wait for PV_(j-1) on its V stage's barrier.  S_j is complete, so
           // PV_(j-2) and everything before it are too, and PV_(j-1+KVS), the next arrival on that barrier, needs P_j
@@ -294,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
     }
     if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
       tc_fence_after();
-      const int t = tt * BQ + row;
+      const int t = tt * BQ + hq * QR + row;
       const float inv = 1.f / l;
       uint16_t* orow = a.o + (size_t)b * a.so_b + (size_t)t * a.so_t + (size_t)h * a.so_h;
 #pragma unroll
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
         uint32_t r[16];
         tmem_ld16(t_o + lane_off + c * 16, r);
         tmem_ld_wait();
-        if (t < T) {
+        if (has_row && t < T) {
 #pragma unroll
           for (int half = 0; half < 2; half++) {
             const int d0 = c * 16 + half * 8;
@@ -364,11 +368,14 @@ int prepare_device() {
   if (dev < 0 || dev >= 64) return set_error(E_LAUNCH, "attention: device %d out of range", dev);
   std::call_once(once[dev], [dev] {
     // two CTAs per SM need (almost) the whole 228 KB as shared memory
-    cudaError_t r = cudaFuncSetAttribute(attn_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<8>::BYTES);
-    if (r == cudaSuccess) r = cudaFuncSetAttribute(attn_tc_kernel<8>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (r == cudaSuccess)
-      r = cudaFuncSetAttribute(attn_tc_kernel<10>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<10>::BYTES);
-    if (r == cudaSuccess) r = cudaFuncSetAttribute(attn_tc_kernel<10>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    auto set = [](auto kernel, int bytes) {
+      cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      return r == cudaSuccess ? cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) : r;
+    };
+    cudaError_t r = set(attn_tc_kernel<8, 128>, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<8, 64>, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 128>, Smem<10>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 64>, Smem<10>::BYTES);
     status[dev] = r;
   });
   if (status[dev] != cudaSuccess)
@@ -376,14 +383,14 @@ int prepare_device() {
   return OK;
 }
 
-template <int NC>
+template <int NC, int QR>
 static int launch_nc(cudaStream_t st, Args a, int B) {
   int rc = prepare_device();
   if (rc) return rc;
   for (int b0 = 0; b0 < B; b0 += 65535) {
     a.b0 = b0;
     const int nb = (B - b0) < 65535 ? (B - b0) : 65535;
-    launch_k(attn_tc_kernel<NC>, dim3(a.Tt, a.H, nb), THREADS, Smem<NC>::BYTES, st, a);
+    launch_k(attn_tc_kernel<NC, QR>, dim3(a.Tt * (128 / QR), a.H, nb), THREADS, Smem<NC>::BYTES, st, a);
     rc = check_launch("vt_attn_tiles_fwd");
     if (rc) return rc;
   }
@@ -440,8 +447,11 @@ int vt_attn_tiles_fwd(cudaStream_t st, const uint16_t* tiles, uint16_t* O, int B
   if (!tiles || !O || !aligned16(tiles) || !aligned16(O) || (so_b | so_t | so_h) % 8)
     return set_error(E_SHAPE, "vt_attn_tiles_fwd: pointers / strides not 16-byte aligned");
   attn_tc::Args a{tiles, O, T, H, D, (T + 127) / 128, so_b, so_t, so_h, scale * 1.4426950408889634f, 0};
-  if (attn_tc::dp_chunks(D) == 8) return attn_tc::launch_nc<8>(st, a, B);
-  return attn_tc::launch_nc<10>(st, a, B);
+  // fewer 128-query CTAs than two per SM (one TAPNext frame: 10 tiles x 12 heads): 64-query CTAs (M = 64 MMAs),
+  // so that two share each SM and hide each other's MMA chain (config 3 1.220 -> 1.211 ms per frame)
+  const bool half = (long long)a.Tt * H * B < 2LL * sm_count();
+  if (attn_tc::dp_chunks(D) == 8) return half ? attn_tc::launch_nc<8, 64>(st, a, B) : attn_tc::launch_nc<8, 128>(st, a, B);
+  return half ? attn_tc::launch_nc<10, 64>(st, a, B) : attn_tc::launch_nc<10, 128>(st, a, B);
 }
 
 }  // extern "C"
