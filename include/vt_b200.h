@@ -3,7 +3,7 @@
  * Conventions (the reference's, moondream/gpu/hgemm.py:21-36, hattn.py:5-16):
  *   - every function takes the CUDA stream to launch on first (torch's current stream in the Python host)
  *     and raw device pointers; the caller owns every buffer; nothing is allocated, nothing synchronises
- *     (except vt_device_status), so the calls can be captured in CUDA graphs;
+ *     (except vt_device_status);
  *   - bf16 tensors are passed as uint16_t*; pitches / strides are in elements;
  *   - return 0 on success, negative on error (-1 unknown variant, -2 shape or alignment, -3 CUDA launch
  *     error, -4 layout mismatch, -5 tensor-map encode failure), the message in vt_last_error_string().
@@ -173,7 +173,7 @@ int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, i
  * more than 16 MiB of tiles (vt_attn_tiles_bytes) return -2.  Every call shares the array, which keeps the
  * last call's contents; each call writes the zeros its pad rows and lanes need, and calls that overlap on
  * the GPU race on the array.  The first call on a device does the set-up (the array's device address and
- * the attention kernels' attributes) with that device current: make it before any stream capture.
+ * the attention kernels' attributes) with that device current.
  * No counterpart in the reference (its attention always takes a caller-allocated V^T buffer). */
 int vt_attn_fwd_noalloc(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
                         int B, int T, int H, int D, long long sq_b, long long sq_t, long long sq_h, long long sk_b,

@@ -24,7 +24,6 @@
 //     host threads -- race on the array;
 //   * the first call on a device does its set-up with that device current: it looks up the array's
 //     device address (cudaGetSymbolAddress) and sets the attention kernels' shared-memory attributes.
-//     Make that first call before any stream capture.
 #include <mutex>
 
 #include "vt_common.cuh"
