@@ -126,12 +126,14 @@ def test_gemm_folded_layernorm(gelu):
     assert rel(out, ref) < 8e-3
 
 
-@pytest.mark.parametrize("M,N,rms", [(1280, 2304, False), (1280, 1536, True), (96, 64, False), (37, 768, True)])
-def test_gemm_norm_factors_merged_in_the_epilogue(M, N, rms):
+@pytest.mark.parametrize("M,N,rms,split", [(1280, 2304, False, False), (1280, 1536, True, False),
+                                           (96, 64, False, False), (37, 768, True, False), (37, 768, False, True)])
+def test_gemm_norm_factors_merged_in_the_epilogue(M, N, rms, split):
     """vt_gemm_fused_lnstats (the folded norm's row factors merged from the chunk statistics in the epilogue)
     against the same GEMM fed by a vt_row_moments / vt_row_rms pass: the factors it stores (ln_mom_out) and its
     outputs match to fp32 rounding (the chunks are summed in another order); CTA-pair tiles (1280 rows) and
-    single-CTA tiles (few tiles), LayerNorm and RMSNorm, a partial row block."""
+    single-CTA tiles (few tiles), LayerNorm and RMSNorm, a partial row block, and K split across CTAs (a
+    workspace: every slice merges the factors, the last one runs the epilogue)."""
     K = 768
     g = torch.Generator(device=DEV).manual_seed(9)
     x = torch.randn(M, K, device=DEV, generator=g) * 2 + 0.3
@@ -147,7 +149,8 @@ def test_gemm_norm_factors_merged_in_the_epilogue(M, N, rms):
     mom_ref = (ops.row_rms if rms else ops.row_moments)(stats, 1e-6, torch.empty(M, 2, device=DEV))
     out_ref = ops.gemm(xb, wf, K, K, N, bf, out_f32=True, ln=(mom_ref, c))
     mom = torch.full((M, 2), float("nan"), device=DEV)
-    out = ops.gemm(xb, wf, K, K, N, bf, out_f32=True, ln_rows=(stats, 1e-6, rms, c, mom))
+    ws = ops.gemm_workspace(M, N, DEV) if split else None
+    out = ops.gemm(xb, wf, K, K, N, bf, out_f32=True, ln_rows=(stats, 1e-6, rms, c, mom), ws=ws)
     torch.cuda.synchronize()
     assert torch.allclose(mom, mom_ref, rtol=1e-5, atol=1e-6)
     assert torch.allclose(out, out_ref, rtol=1e-4, atol=1e-4)
