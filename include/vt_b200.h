@@ -214,17 +214,18 @@ int vt_row_rms(cudaStream_t stream, const float* stats, int M, int nchunk, float
  * whose A was the bf16 copy of x and whose weights carry the RMSNorm gamma; the recurrence's input
  * t = bf16(x * rstd * gamma) is formed here from the fp32 stream x and rms_moments [M][2] (vt_row_rms).
  * Updates state and x (x += h) in place and writes the bf16 copy xb of the new x and its per-32-column chunk
- * statistics stats [M][W/32][2] (mean, M2) for the next block's folded LayerNorm.  W % 32 == 0.
+ * statistics stats [M][W/32][2] (mean, M2) for the next block's folded LayerNorm.  W % 32 == 0.  softplus_a [W]:
+ * softplus(a_param) per channel, as vt_ssm_step takes it (the caller computes it once per block).
  * Replaces: the RG-LRU step of tapnext/npu/r9/cpuemu.py:33-47 with its pre-norm (step8.py:474-479). */
-int vt_rglru_fold(cudaStream_t stream, const float* G, long long ldg, const float* a_param, const float* rms_moments,
+int vt_rglru_fold(cudaStream_t stream, const float* G, long long ldg, const float* softplus_a, const float* rms_moments,
                   const float* rms_gamma, float* state, long long lds, float* x, long long ldx, uint16_t* xb,
                   long long ldxb, float* stats, int M, int W, float c, int first);
 
 /* RG-LRU recurrence step over M tokens of width W on the bf16 input u (the normalised stream):
  * G = [gx_pre | ga_pre] fp32; state and the residual stream x fp32, updated in place (state <- h,
- * x <- x + h); first != 0 starts a sequence.
+ * x <- x + h); first != 0 starts a sequence; softplus_a [W] = softplus(a_param) per channel.
  * Replaces: the RG-LRU forward restated in tapnext/npu/r9/cpuemu.py:33-47 (the NPU's EW SSM op). */
-int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* a_param, const uint16_t* u,
+int vt_rglru(cudaStream_t stream, const float* G, long long ldg, const float* softplus_a, const uint16_t* u,
              long long ldu, float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first);
 
 /* One recurrent step of the full TAPNext++ block's temporal mixing for R tokens of width W (W % 64 == 0,

@@ -310,12 +310,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* f, long lo
 }
 
 // RG-LRU step (tapnext/npu/r9/cpuemu.py:33-47) on the normalised input u, per element (m, n < W):
-//   gx = sigmoid(G[m, n]), ga = sigmoid(G[m, W + n]), log_a = -c * ga * softplus(a_param[n])
+//   gx = sigmoid(G[m, n]), ga = sigmoid(G[m, W + n]), log_a = -c * ga * softplus_a[n]  (softplus(a_param))
 //   h  = u * gx                                              (first frame)
 //   h  = exp(log_a) * h0 + (u * gx) * sqrt(-expm1(2 log_a))   (later frames)
 //   state <- h, x <- x + h     (u bf16; state and the residual stream x fp32, updated in place)
 
-__global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* a_param,
+__global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ldg, const float* softplus_a,
                                                     const uint16_t* u, long long ldu, float* state, long long lds,
                                                     float* x, long long ldx, int M, int W, float c, int first) {
   griddep_wait();  // programmatic dependent launch: the previous kernel has completed
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
     const int n = (int)(i % nv) * 4;
     const float4 gx4 = *reinterpret_cast<const float4*>(G + m * ldg + n);
     const float4 ga4 = *reinterpret_cast<const float4*>(G + m * ldg + W + n);
-    const float4 ap4 = *reinterpret_cast<const float4*>(a_param + n);
+    const float4 ap4 = *reinterpret_cast<const float4*>(softplus_a + n);
     float4 x4 = *reinterpret_cast<const float4*>(x + m * ldx + n);
     const uint2 u2 = *reinterpret_cast<const uint2*>(u + m * ldu + n);
     const float uv[4] = {__uint_as_float(u2.x << 16), __uint_as_float(u2.x & 0xffff0000u), __uint_as_float(u2.y << 16),
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(256) rglru_kernel(const float* G, long long ld
 // per-32-column (mean, M2) statistics, the inputs of the next block's folded LayerNorm.  Thread = 4 columns;
 // the 8 threads of a 32-column chunk are consecutive lanes (W % 32 == 0), so a chunk's statistics are a
 // shuffle reduction over 8 lanes, and every lane of a warp runs the same number of iterations.
-__global__ void __launch_bounds__(256) rglru_fold_kernel(const float* G, long long ldg, const float* a_param,
+__global__ void __launch_bounds__(256) rglru_fold_kernel(const float* G, long long ldg, const float* softplus_a,
                                                          const float2* __restrict__ mom, const float* __restrict__ rms_g,
                                                          float* state, long long lds, float* x, long long ldx,
                                                          uint16_t* __restrict__ xb, long long ldxb,
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(256) rglru_fold_kernel(const float* G, long lo
       n = (int)(i % nv) * 4;
       const float4 gx4 = *reinterpret_cast<const float4*>(G + m * ldg + n);
       const float4 ga4 = *reinterpret_cast<const float4*>(G + m * ldg + W + n);
-      const float4 ap4 = *reinterpret_cast<const float4*>(a_param + n);
+      const float4 ap4 = *reinterpret_cast<const float4*>(softplus_a + n);
       const float4 rg4 = *reinterpret_cast<const float4*>(rms_g + n);
       const float4 x4 = *reinterpret_cast<const float4*>(x + m * ldx + n);
       const float4 h4 = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(state + m * lds + n);
@@ -704,35 +704,35 @@ int vt_row_rms(cudaStream_t st, const float* stats, int M, int nchunk, float eps
   return check_launch("vt_row_rms");
 }
 
-int vt_rglru_fold(cudaStream_t st, const float* G, long long ldg, const float* a_param, const float* rms_moments,
+int vt_rglru_fold(cudaStream_t st, const float* G, long long ldg, const float* softplus_a, const float* rms_moments,
                   const float* rms_gamma, float* state, long long lds, float* x, long long ldx, uint16_t* xb,
                   long long ldxb, float* stats, int M, int W, float c, int first) {
   using namespace vt;
   if (M < 0 || W <= 0 || W % 32) return set_error(E_SHAPE, "vt_rglru_fold: W must be a positive multiple of 32");
   if (M == 0) return OK;
-  if (!G || !a_param || !rms_moments || !rms_gamma || !state || !x || !xb || !stats)
+  if (!G || !softplus_a || !rms_moments || !rms_gamma || !state || !x || !xb || !stats)
     return set_error(E_SHAPE, "vt_rglru_fold: null pointer");
   if (ldg < 2LL * W || lds < W || ldx < W || ldxb < W || ldg % 4 || lds % 4 || ldx % 4 || ldxb % 4 || !aligned16(G) ||
-      !aligned16(a_param) || !aligned16(rms_gamma) || !aligned16(state) || !aligned16(x) ||
+      !aligned16(softplus_a) || !aligned16(rms_gamma) || !aligned16(state) || !aligned16(x) ||
       (reinterpret_cast<uintptr_t>(xb) & 7) || (reinterpret_cast<uintptr_t>(rms_moments) & 7) ||
       (reinterpret_cast<uintptr_t>(stats) & 7))
     return set_error(E_SHAPE, "vt_rglru_fold: pitches / alignment invalid");
-  launch_k(ew::rglru_fold_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, a_param,
+  launch_k(ew::rglru_fold_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, softplus_a,
            reinterpret_cast<const float2*>(rms_moments), rms_gamma, state, lds, x, ldx, xb, ldxb,
            reinterpret_cast<float2*>(stats), M, W, c, first);
   return check_launch("vt_rglru_fold");
 }
 
-int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* a_param, const uint16_t* u, long long ldu,
+int vt_rglru(cudaStream_t st, const float* G, long long ldg, const float* softplus_a, const uint16_t* u, long long ldu,
              float* state, long long lds, float* x, long long ldx, int M, int W, float c, int first) {
   using namespace vt;
   if (M < 0 || W <= 0 || W % 4) return set_error(E_SHAPE, "vt_rglru: bad shape");
   if (M == 0) return OK;
-  if (!G || !a_param || !u || !state || !x || ldg < 2LL * W || ldu < W || lds < W || ldx < W || ldg % 4 || ldu % 4 ||
-      lds % 4 || ldx % 4 || !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(a_param) ||
+  if (!G || !softplus_a || !u || !state || !x || ldg < 2LL * W || ldu < W || lds < W || ldx < W || ldg % 4 || ldu % 4 ||
+      lds % 4 || ldx % 4 || !aligned16(G) || !aligned16(state) || !aligned16(x) || !aligned16(softplus_a) ||
       (reinterpret_cast<uintptr_t>(u) & 7))
     return set_error(E_SHAPE, "vt_rglru: pitches / alignment invalid");
-  launch_k(ew::rglru_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, a_param, u, ldu, state, lds, x,
+  launch_k(ew::rglru_kernel, ew::grid_for((long long)M * (W / 4), 256), 256, 0, st, G, ldg, softplus_a, u, ldu, state, lds, x,
                                                                              ldx, M, W, c, first);
   return check_launch("vt_rglru");
 }

@@ -127,18 +127,18 @@ __device__ __forceinline__ float gelu_sigmoid(float x) {
   return x * r;
 }
 
-// RG-LRU element step (tapnext/npu/r9/cpuemu.py:33-47) in fp32 with CUDA's transcendentals: u the normed
-// input, gx_pre / ga_pre the gate pre-activations, ap the softplus argument (a = sigmoid(-ap)^(c ga)), h0 the
-// state (unused when first).  h = u sigmoid(gx) on a sequence's first frame, else a h0 + u sigmoid(gx)
-// sqrt(1 - a^2) with log a = -c sigmoid(ga) softplus(ap).  Shared by vt_rglru, vt_rglru_fold and the gate
-// GEMM's RG-LRU epilogue, so all three give the same numbers.
-__device__ __forceinline__ float rglru_elem(float u, float gx_pre, float ga_pre, float ap, float h0, float c,
+// RG-LRU element step (tapnext/npu/r9/cpuemu.py:33-47) in fp32: u the normed input, gx_pre / ga_pre the gate
+// pre-activations, sp = softplus(a_param) of the channel (computed once per channel by the caller), h0 the state
+// (unused when first).  h = u sigmoid(gx) on a sequence's first frame, else a h0 + u sigmoid(gx) sqrt(1 - a^2)
+// with log a = -c sigmoid(ga) sp.  The sigmoids and a = exp(log a) take the hardware exponential and division
+// (__expf, __fdividef: a few ulp, far inside the RG-LRU's tolerances); 1 - a^2 keeps expm1f, which a near 1
+// needs.  Shared by vt_rglru and vt_rglru_fold, so both give the same numbers.
+__device__ __forceinline__ float rglru_elem(float u, float gx_pre, float ga_pre, float sp, float h0, float c,
                                             bool first) {
-  const float gated = u * (1.0f / (1.0f + expf(-gx_pre)));
+  const float gated = u * __fdividef(1.0f, 1.0f + __expf(-gx_pre));
   if (first) return gated;
-  const float sp = ap > 20.f ? ap : log1pf(expf(ap));
-  const float log_a = -c * (1.0f / (1.0f + expf(-ga_pre))) * sp;
-  return expf(log_a) * h0 + gated * sqrtf(-expm1f(2.0f * log_a));
+  const float log_a = -c * __fdividef(1.0f, 1.0f + __expf(-ga_pre)) * sp;
+  return __expf(log_a) * h0 + gated * sqrtf(-expm1f(2.0f * log_a));
 }
 
 // Attention-tile layout: offset (bf16 elements) of row t, 8-element d chunk c of operand w (0 q, 1 k, 2 v)

@@ -217,11 +217,11 @@ def row_rms(stats, eps, out):
     return out
 
 
-def rglru_fold(G, a_param, rms_moments, rms_gamma, state, x, xb, stats, c, first):
+def rglru_fold(G, softplus_a, rms_moments, rms_gamma, state, x, xb, stats, c, first):
     """RG-LRU step with its RMSNorm folded into the gate GEMM (vt_rglru_fold): state, x updated in place; xb and
-    stats receive the bf16 copy and chunk statistics of the new x."""
+    stats receive the bf16 copy and chunk statistics of the new x.  softplus_a [W] = softplus(a_param)."""
     M, W = x.shape
-    rc = lib().vt_rglru_fold(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), rms_moments.data_ptr(),
+    rc = lib().vt_rglru_fold(_stream(), G.data_ptr(), G.stride(0), softplus_a.data_ptr(), rms_moments.data_ptr(),
                              rms_gamma.data_ptr(), state.data_ptr(), state.stride(0), x.data_ptr(), x.stride(0),
                              xb.data_ptr(), xb.stride(0), stats.data_ptr(), M, W, float(c), int(bool(first)))
     check(rc, "vt_rglru_fold")
@@ -370,10 +370,11 @@ def crop_combine(feats, out):
     return out
 
 
-def rglru(G, a_param, u, state, x, c, first):
-    """RG-LRU step on the bf16 input u [M, W]: state [M, W] and x [M, W] fp32 updated in place."""
+def rglru(G, softplus_a, u, state, x, c, first):
+    """RG-LRU step on the bf16 input u [M, W]: state [M, W] and x [M, W] fp32 updated in place; softplus_a [W] =
+    softplus(a_param) per channel."""
     M, W = x.shape
-    rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), a_param.data_ptr(), u.data_ptr(), u.stride(0),
+    rc = lib().vt_rglru(_stream(), G.data_ptr(), G.stride(0), softplus_a.data_ptr(), u.data_ptr(), u.stride(0),
                         state.data_ptr(), state.stride(0), x.data_ptr(), x.stride(0), M, W, float(c), int(bool(first)))
     check(rc, "vt_rglru")
 

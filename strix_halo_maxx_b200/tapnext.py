@@ -36,21 +36,22 @@ class RgLruGate:
     """The RG-LRU temporal update of one block (tapnext/npu/r9/cpuemu.py:33-47) on the device:
     G = t . [Wx; Wa]^T + [bx; ba] (one GEMM, fp32 out), then vt_rglru: gates, recurrence, state and x += h.
     gx_w / ga_w are [768 out, 768 in] (dense; the reference's block-diagonal gates are the special case that
-    tests/golden/rglru_ref_cases.npz pins), a_param [768]; G an fp32 [rows >= M, 2 * 768] buffer."""
+    tests/golden/rglru_ref_cases.npz pins), a_param [768] (kept on the device as softplus(a_param), computed once in
+    float64 and rounded to fp32); G an fp32 [rows >= M, 2 * 768] buffer."""
 
     def __init__(self, gx_w, gx_b, ga_w, ga_b, a_param, c, dev, G):
         g = torch.cat([torch.as_tensor(gx_w), torch.as_tensor(ga_w)], 0)
         self.W = g.shape[1]
         self.w, self.ld = _dev_mat(g, dev)
         self.b = _dev_vec(torch.cat([torch.as_tensor(gx_b), torch.as_tensor(ga_b)]), dev)
-        self.a_param = _dev_vec(a_param, dev)
+        self.softplus_a = _dev_vec(torch.nn.functional.softplus(torch.as_tensor(a_param).double()).float(), dev)
         self.c = c
         self.G = G  # fp32 [rows, 2 W] scratch for the gate pre-activations, shareable between blocks
 
     def __call__(self, t, state, x, first):
         """t [M, W] bf16 (the normed input), state [M, W] fp32 and x [M, W] fp32 updated in place."""
         ops.gemm(t, self.w, self.ld, self.W, 2 * self.W, self.b, out=self.G[:t.shape[0]])
-        ops.rglru(self.G[:t.shape[0]], self.a_param, t, state, x, self.c, first)
+        ops.rglru(self.G[:t.shape[0]], self.softplus_a, t, state, x, self.c, first)
 
 
 class TapNextStep:
@@ -186,5 +187,5 @@ class TapNextStep:
                      **fold)
             ops.gemm(self.xb, blk["gate_wf"], blk["gate_ldf"], Wd, 2 * Wd, blk["gate_b"], out=self.G,
                      **self._norm(blk["gate_c"], True, keep=True))
-            ops.rglru_fold(self.G, blk["lru"].a_param, self.mom, blk["rms_w"], self.state[i], self.x, self.xb,
+            ops.rglru_fold(self.G, blk["lru"].softplus_a, self.mom, blk["rms_w"], self.state[i], self.x, self.xb,
                            self.stats, cfg.lru_c, first)

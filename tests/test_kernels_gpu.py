@@ -428,6 +428,7 @@ def test_rglru(first):
                    F.linear(uf, Wd["blocks.0.ga_w"], Wd["blocks.0.ga_b"])], 1).to(DEV)
     ref = rglru_ref(uf, Wd, "blocks.0.", None if first else h0.cpu(), 8.0)
     state, xx = h0.clone(), x.clone()
-    ops.rglru(G, Wd["blocks.0.a_param"].to(DEV), u, state, xx, 8.0, first)
+    sp = F.softplus(Wd["blocks.0.a_param"].double()).float().to(DEV)
+    ops.rglru(G, sp, u, state, xx, 8.0, first)
     assert rel(state, ref) < 1e-5
     assert rel(xx, x + ref.to(DEV)) < 1e-5
