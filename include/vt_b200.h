@@ -27,6 +27,14 @@ const char* vt_last_error_string(void);
  * (the kernel then unwinds instead of hanging).  Synchronises the device; clear != 0 resets the word. */
 int vt_device_status(int clear, unsigned int* status);
 
+/* Failure detection without a GPU fault: one CTA runs the kernels' bounded-wait protocol on two mbarriers that
+ * nothing completes.  Its thread 0 gives up after `cycles` SM cycles (1000 <= cycles <= 1e9), sets the CTA's
+ * abort flag and status bit 8; its thread 32, waiting with the kernels' own ~2 s limit, must leave on the abort
+ * flag.  result (2 ints, device memory) = what the two waits returned (0: gave up).
+ * Replaces: nothing in the reference (its kernels have no bounded waits); checks the mechanism behind
+ * vt_device_status. */
+int vt_wait_selftest(cudaStream_t stream, long long cycles, int* result);
+
 /* C[M,N] (bf16, pitch ldc) = A[M,K] . W[N,K]^T + bias (fp32, may be NULL), optional GELU-tanh applied
  * after rounding to bf16.  A, W bf16 K-contiguous, pitches multiples of 8, bases 16-byte aligned.
  * tcgen05/TMEM tiles fed by TMA.

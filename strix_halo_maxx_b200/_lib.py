@@ -16,6 +16,7 @@ SIGNATURES = {
     "vt_abi_version": (I, []),
     "vt_last_error_string": (ctypes.c_char_p, []),
     "vt_device_status": (I, [I, ctypes.POINTER(U)]),
+    "vt_wait_selftest": (I, [P, LL, P]),
     "vt_gemm_bf16": (I, [P, P, LL, P, LL, P, P, LL, I, I, I, I]),
     "vt_gemm_ex": (I, [P, P, LL, P, LL, I, I, I, P, P, LL, I, I, P, LL, I, I, P, LL]),
     "vt_gemm_qkv_tiles": (I, [P, P, LL, P, LL, P, P, I, I, I, I, I]),

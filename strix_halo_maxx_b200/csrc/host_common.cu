@@ -161,3 +161,37 @@ int vt_device_status(int clear, unsigned int* status) {
 int vt_abi_version(void) { return 1; }
 
 }  // extern "C"
+
+namespace vt {
+// The bounded-wait protocol every kernel uses, run on two barriers that nothing completes: thread 0 waits with
+// `cycles` as its limit and gives up (abort flag and status bit set), thread 32 waits with the kernels' own
+// limit (kSpinCycles, ~2 s) and must leave as soon as it sees the abort flag.  result[0 / 1] = what the two
+// waits returned (0: gave up).
+__global__ void wait_selftest_kernel(long long cycles, int* result) {
+  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) result[0] = mbar_wait_for(&bar[0], 0, &abort_flag, ST_SELFTEST, cycles) ? 1 : 0;
+  if (threadIdx.x == 32) result[1] = mbar_wait(&bar[1], 0, &abort_flag, ST_SELFTEST) ? 1 : 0;
+}
+}  // namespace vt
+
+extern "C" {
+
+// Failure detection without a fault: runs the bounded-wait protocol on barriers nothing completes (see
+// wait_selftest_kernel).  result: 2 ints of device memory.  1000 <= cycles <= 1e9.
+int vt_wait_selftest(cudaStream_t st, long long cycles, int* result) {
+  using namespace vt;
+  if (!result || cycles < 1000 || cycles > 1000000000LL)
+    return set_error(E_SHAPE, "vt_wait_selftest: result must be non-null and 1000 <= cycles <= 1e9");
+  wait_selftest_kernel<<<1, 64, 0, st>>>(cycles, result);
+  return check_launch("vt_wait_selftest");
+}
+
+}  // extern "C"

@@ -22,6 +22,7 @@ enum : unsigned int {
   ST_ATTN_MMA = 1u << 5,
   ST_ATTN_SOFTMAX = 1u << 6,
   ST_SSM_MMA = 1u << 7,
+  ST_SELFTEST = 1u << 8,  // vt_wait_selftest
 };
 // A wait gives up after this many SM clock cycles (~2 s at 1.9 GHz); legitimate waits are microseconds.
 constexpr long long kSpinCycles = 4000000000LL;
@@ -187,17 +188,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase of `parity` to complete.  Returns false if another role of this CTA has
-// aborted (flag set) or if the wait outlives kSpinCycles, in which case it sets the flag and
-// records `site` in g_status.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int site) {
+// aborted (flag set) or if the wait outlives `limit` cycles (kSpinCycles for mbar_wait), in which case
+// it sets the flag and records `site` in g_status.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              unsigned int site, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++n & 255u) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > kSpinCycles) {
+      if (clock64() - t0 > limit) {
         *abort_flag = 1;
         atomicOr(&g_status, site);
         return false;
@@ -205,6 +206,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int site) {
+  return mbar_wait_for(bar, parity, abort_flag, site, kSpinCycles);
 }
 // Bounded wait used while unwinding: ignores the abort flag, gives up after `cycles`.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, long long cycles) {
