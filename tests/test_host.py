@@ -66,3 +66,50 @@ def test_two_rank_all_gather_over_gloo():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+def _rank_leaving(rank, world, port, q):
+    """Rank 1 leaves between steps, before the first all-gather (a host-side injected failure); rank 0 must get
+    an error from its collective instead of waiting for good."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the message is sent before the process goes
+        os._exit(3)
+    try:
+        n_total, mb, T, W = 16, 2, 3, 4
+        ids = local_crop_ids(n_total, world, rank, mb)
+        pix = torch.tensor(ids, dtype=torch.float32)
+        feats = torch.empty(n_total, T, W)
+        local = torch.empty(len(ids), T, W)
+        encode_sharded(lambda p, out: out.copy_(p[:, None, None].expand(-1, T, W)), pix, feats, local, mb)
+        q.put((rank, "completed"))
+    except Exception as e:  # the collective's error: the peer is gone
+        q.put((rank, "error " + type(e).__name__))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_a_rank_leaving_before_the_all_gather_ends_the_other_ranks_collective_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_rank_leaving, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("error"), res[0]
+    assert procs[1].exitcode == 3
