@@ -216,7 +216,7 @@ def run_vt(a):
     from strix_halo_maxx_b200.config import TOWER
     from strix_halo_maxx_b200.weights import tower_weights, crop_pixels
     from strix_halo_maxx_b200.tower import VisionTower
-    from strix_halo_maxx_b200.multigpu import local_crop_ids, encode_sharded, HostPipeline
+    from strix_halo_maxx_b200.multigpu import local_crop_ids, encode_sharded, HostPipeline, ShardedFrame
     from strix_halo_maxx_b200 import ops
     from strix_halo_maxx_b200._lib import device_status
 
@@ -313,19 +313,27 @@ def run_vt(a):
         e2e, e2e_ok = run_e2e(a, tower, n_local, mb, pix_host, feats_all, local_out, dev, world, barrier,
                               max_over_ranks)
     # ---------------- config 2 latency: one 13-crop frame (tower + combine + projection)
-    frame_ms = None
+    # one 13-crop frame's latency on the N GPUs of the run: at N = 1 the whole frame on this GPU; at N > 1 its
+    # crops sharded over the ranks (ShardedFrame: ceil(13 / N) crops each, one NCCL all-gather of the features,
+    # combine + projection on every rank), max over ranks; the sharded output is checked against one GPU's
+    frame_ms = frame_ok = None
     if not a.no_frame:
-        crops = pix_dev[:13] if n_local >= 13 else pix_dev[:1].expand(13, -1, -1, -1).contiguous()
+        crops = torch.from_numpy(crop_pixels(13, cfg, seed=1, first=0)).to(torch.bfloat16).to(dev)
+        sf = ShardedFrame(tower, 13, cfg.ntok, cfg.width, dev)
         for _ in range(3):
-            tower.frame(crops)
+            sf(crops)
         torch.cuda.synchronize()
+        barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
         for _ in range(10):
-            tower.frame(crops)
+            sf(crops)
         g1.record()
         torch.cuda.synchronize()
-        frame_ms = g0.elapsed_time(g1) / 10
+        frame_ms = max_over_ranks(g0.elapsed_time(g1) / 10)
+        if world > 1:
+            frame_ok = bool(torch.equal(sf(crops), tower.frame(crops)))
+            frame_ok = max_over_ranks(0.0 if frame_ok else 1.0) == 0.0
 
     tap = txt = fin = None
     if world == 1 and not a.no_tapnext:
@@ -353,6 +361,10 @@ def run_vt(a):
             "allgather_exposed_ms_per_step": ag_exposed,
             "ms_per_frame_13crop_throughput": 13 * 1000.0 / value,
             "ms_per_frame_13crop_latency": frame_ms,
+            "frame_latency_mode": ("one GPU" if world == 1 else
+                                   f"13 crops sharded over {world} GPUs ({-(-13 // world)} per rank), NCCL all-gather "
+                                   "of the features, combine + projection on every rank; max over ranks"),
+            "frame_sharded_matches_one_gpu": frame_ok,
             "tapnext_ms_per_frame": tap,
             "text_decoder": txt,
             "frame_input": fin,

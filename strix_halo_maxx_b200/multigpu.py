@@ -6,6 +6,10 @@ Crop order: the batch is cut into chunks of world * mb crops; in chunk j, rank r
 [j*world*mb + r*mb, j*world*mb + (r+1)*mb).  So after chunk j every rank has a contiguous slice of
 the global output and one all_gather_into_tensor fills rows [j*world*mb, (j+1)*world*mb) in crop
 order.  The collective of chunk j is asynchronous and runs while chunk j+1 is computed.
+
+One frame's latency (BASELINE config 2 on N GPUs, ShardedFrame): the frame's 13 crops are cut the same way
+(ceil(13 / N) consecutive crops per rank), one all-gather puts every crop's features on every rank in crop
+order, and every rank runs the combine and the projection, so each ends with the whole frame's output.
 """
 import torch
 import torch.distributed as dist
@@ -110,3 +114,37 @@ class HostPipeline:
         main.wait_stream(self.s_out)
         main.wait_stream(self.s_in)
         return out_host
+
+
+def frame_crop_slice(n_crops, world, rank):
+    """(lo, hi, per_rank): the crops [lo, hi) of one n_crops-crop frame that `rank` computes when the frame is
+    sharded over `world` ranks, ceil(n_crops / world) consecutive crops each (the last ranks fewer, maybe none)."""
+    per = -(-n_crops // world)
+    lo = min(rank * per, n_crops)
+    return lo, min(lo + per, n_crops), per
+
+
+class ShardedFrame:
+    """One multi-crop frame with its crops sharded over the ranks, for latency: rank r runs
+    the tower on crops frame_crop_slice(n, world, r), the [per_rank, T, W] features of every rank are
+    all-gathered (rank-major, so rows 0..n-1 are the crops in order; a rank with fewer crops pads its block,
+    and the padding rows land after row n-1), and every rank combines and projects the frame
+    (tower.frame_from_features).  Per-crop features do not depend on which crops share a launch, so the
+    result equals tower.frame on one GPU.  `tower` needs forward(pix, out=) and frame_from_features(feats)."""
+
+    def __init__(self, tower, n_crops, T, W, device, group=None, dtype=torch.bfloat16):
+        self.tower, self.n, self.group = tower, n_crops, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.lo, self.hi, per = frame_crop_slice(n_crops, self.world, rank)
+        self.local = torch.zeros(per, T, W, dtype=dtype, device=device)
+        self.gathered = torch.empty(self.world * per, T, W, dtype=dtype, device=device)
+
+    def __call__(self, crops):
+        """crops [n_crops, ...]: the whole frame (each rank reads only its own slice) -> the frame's output."""
+        if self.world == 1:
+            return self.tower.frame_from_features(self.tower.forward(crops))
+        if self.hi > self.lo:
+            self.tower.forward(crops[self.lo:self.hi], out=self.local[:self.hi - self.lo])
+        dist.all_gather_into_tensor(self.gathered, self.local, group=self.group)
+        return self.tower.frame_from_features(self.gathered[:self.n])

@@ -215,10 +215,14 @@ class VisionTower:
 
     def frame(self, crops):
         """Config 2: 1 global + n local crops [1+n, 3, 378, 378] -> projected frame features [729, proj_out]."""
+        return self.frame_from_features(self.forward(crops))
+
+    def frame_from_features(self, feats):
+        """The frame's tail: crop features [1+n, 729, width] bf16 (global crop first) -> combined [729, 2 width]
+        (global features, then the per-token mean of the local crops) -> projection [729, proj_out]."""
         assert self.p1_k == 2 * self.cfg.width, "the multi-crop frame needs the unfolded [hidden, 2 width] fc1"
-        f = self.forward(crops)
         comb = torch.empty(self.cfg.ntok, 2 * self.cfg.width, dtype=BF16, device=self.dev)
-        ops.crop_combine(f, comb)
+        ops.crop_combine(feats, comb)
         return self.project(comb)
 
 

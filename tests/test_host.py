@@ -10,7 +10,7 @@ import torch.multiprocessing as mp
 
 from strix_halo_maxx_b200.config import TowerConfig, TapNextConfig
 from strix_halo_maxx_b200 import weights as wg
-from strix_halo_maxx_b200.multigpu import local_crop_ids, encode_sharded
+from strix_halo_maxx_b200.multigpu import local_crop_ids, encode_sharded, frame_crop_slice, ShardedFrame
 
 
 def test_weights_are_deterministic_and_independent():
@@ -113,3 +113,61 @@ def test_a_rank_leaving_before_the_all_gather_ends_the_other_ranks_collective_wi
     assert res[1] == "left"
     assert res[0].startswith("error"), res[0]
     assert procs[1].exitcode == 3
+
+
+@pytest.mark.parametrize("n,world", [(13, 1), (13, 2), (13, 4), (13, 8), (3, 4), (1, 2)])
+def test_frame_crop_slices_cover_the_frame_once_in_order(n, world):
+    got = []
+    for r in range(world):
+        lo, hi, per = frame_crop_slice(n, world, r)
+        assert 0 <= hi - lo <= per and (hi == lo or lo == r * per)
+        got.extend(range(lo, hi))
+    assert got == list(range(n))
+
+
+class _FakeTower:
+    """Stand-in for VisionTower on the CPU: the features of crop i are the value i; the frame's output lists the
+    first feature of every crop it was given, in order."""
+    T, W = 3, 4
+
+    def forward(self, p, out=None):
+        out = torch.empty(p.shape[0], self.T, self.W) if out is None else out
+        out.copy_(p[:, None, None].expand(-1, self.T, self.W))
+        return out
+
+    def frame_from_features(self, feats):
+        return feats[:, 0, 0].clone()
+
+
+def _rank_frame(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        res = []
+        for n in (13, 3, 1):
+            sf = ShardedFrame(_FakeTower(), n, _FakeTower.T, _FakeTower.W, "cpu", dtype=torch.float32)
+            crops = torch.arange(n, dtype=torch.float32) + 100
+            res.append(bool(torch.equal(sf(crops), crops)))
+        q.put((rank, all(res)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_frame_gathers_every_crop_in_order_on_every_rank(world):
+    """ShardedFrame over gloo ranks: every rank ends with the features of all crops of the frame, in crop order,
+    also when the crops do not divide evenly and some ranks hold fewer (or none: 1 crop over 2 or 3 ranks)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 31500 + world * 10 + (os.getpid() % 500)
+    procs = [ctx.Process(target=_rank_frame, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res == {r: True for r in range(world)}
