@@ -67,7 +67,13 @@ struct Args {
 //                into the first 32 columns of S buffer j%2 (tcgen05.st), arrive.  The MMA reads P_j from tensor
 //                memory (A operand); S_(j+2), the next writer of that buffer, is issued after PV_j and the
 //                tensor core runs them in order.
-template <int NC, int QR>
+//
+// KS = 2 (grids of fewer than two query-tile CTAs per SM and 16 or more key tiles: a TAPNext frame): the keys
+// of a query tile are split over a cluster of two CTAs, each running the pipeline above on its half of the key
+// tiles, so a CTA's chain of key tiles is half as long.  At the end rank 1 sends its unnormalised O rows with
+// their row max and row sum into rank 0's shared memory (over its then idle K / V ring) and rank 0 merges the
+// two halves (flash-decoding's rescale by 2^(m_i - max m)) and stores the output.
+template <int NC, int QR, int KS>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   using L = Smem<NC>;
   constexpr int DP = NC * 8;
@@ -87,10 +93,14 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tt = QR == 128 ? blockIdx.x : blockIdx.x >> 1, hq = QR == 128 ? 0 : blockIdx.x & 1;
+  static_assert(KS == 1 || QR == 128, "the key split runs 128-query tiles");
+  const int tt = (QR == 128 && KS == 1) ? blockIdx.x : blockIdx.x >> 1, hq = QR == 128 ? 0 : blockIdx.x & 1;
+  const int ks = KS == 2 ? (int)(blockIdx.x & 1) : 0;  // the cluster rank: blockIdx.x pairs form the clusters
   const int h = blockIdx.y, b = a.b0 + blockIdx.z;
   const int T = a.T, H = a.H, Tt = a.Tt;
-  const int nkv = (T + BKV - 1) / BKV;
+  const int nkv_all = (T + BKV - 1) / BKV;
+  const int kt0 = nkv_all * ks / KS;                    // this CTA's key tiles: [kt0, kt0 + nkv)
+  const int nkv = nkv_all * (ks + 1) / KS - kt0;
   const size_t tile_elems = (size_t)NC * 1024;  // one 128-row tile of one operand
   const uint16_t* q_src = a.tiles + ((((size_t)b * 3 + 0) * H + h) * Tt + tt) * tile_elems;
   const uint16_t* k_base = a.tiles + ((((size_t)b * 3 + 1) * H + h) * Tt) * tile_elems;
@@ -114,6 +124,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   const uint32_t t_o = tmem + 128;
   griddep_wait();  // programmatic dependent launch: the tiles' producer has completed
   griddep_launch();
+  float m_used = -INFINITY, l = 0.f;  // softmax threads: the row's running max (log2 units) and sum
+  bool have_o = false;                // (KS = 2) softmax threads: O complete
 
   if (warp == 4) {
     if (lane == 0) {
@@ -124,7 +136,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       bool ok = true;
       int last_k = 0, last_v = -1;  // last key tiles whose K / V copies were issued
       auto load_kv = [&](uint64_t* full, const uint16_t* base, int j, int off) {
-        const uint16_t* src = base + (size_t)(j >> 1) * tile_elems + (size_t)(j & 1) * NC * 512;
+        const int g = kt0 + j;  // the key tile's index in the head
+        const uint16_t* src = base + (size_t)(g >> 1) * tile_elems + (size_t)(g & 1) * NC * 512;
         mbar_arrive_expect_tx(full, L::KT);
         bulk_load(sm + off + (j % KVS) * L::KT, src, L::KT, full);
       };
@@ -202,14 +215,13 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
     const bool has_row = QR == 128 || lane < 16;  // M = 64: rows 16w .. 16w+15 in lanes 0-15 of quarter w
     const int row = QR == 128 ? warp * 32 + lane : warp * 16 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; j++) {
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, ST_ATTN_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
       const uint32_t t_s = tmem + s * BKV + lane_off;
-      const int kbase = j * BKV;
+      const int kbase = (kt0 + j) * BKV;
       const bool tail = kbase + BKV > T;  // only the last key tile has keys past T (zero rows, masked)
       uint32_t r0[32], r1[32];
       tmem_ld32(t_s, r0);
@@ -296,7 +308,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[s]);
     }
-    if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
+    if (KS == 2) {
+      have_o = __all_sync(0xffffffffu, ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX));
+      if (have_o) tc_fence_after();
+    } else if (ok && mbar_wait(o_full, 0, abort_flag, ST_ATTN_SOFTMAX)) {
       tc_fence_after();
       const int t = tt * BQ + hq * QR + row;
       const float inv = 1.f / l;
@@ -316,6 +331,64 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
                              pack_bf2(__uint_as_float(r[8 * half + 2]) * inv, __uint_as_float(r[8 * half + 3]) * inv),
                              pack_bf2(__uint_as_float(r[8 * half + 4]) * inv, __uint_as_float(r[8 * half + 5]) * inv),
                              pack_bf2(__uint_as_float(r[8 * half + 6]) * inv, __uint_as_float(r[8 * half + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+  if constexpr (KS == 2) {
+    // every MMA of both CTAs is complete and every load has landed: rank 0's K / V ring takes rank 1's rows
+    // (row i: DP floats of O, then m, l, a valid flag) while rank 0 still holds its own O in tensor memory
+    constexpr int RS = DP + 4;  // floats per row
+    static_assert(128 * RS * 4 <= L::BAR - L::K, "the merge buffer must fit in the K / V ring");
+    const uint32_t rx = smem_u32(sm + L::K);
+    const int row = warp * 32 + lane;
+    const uint32_t t_row = t_o + ((uint32_t)(warp * 32) << 16);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp < 4 && ks == 1) {
+      const uint32_t dst = mapa_shared(rx + (uint32_t)(row * RS * 4), 0);
+      if (have_o) {
+#pragma unroll
+        for (int c = 0; c < DP / 16; c++) {
+          uint32_t r[16];
+          tmem_ld16(t_row + c * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e += 4) st_cluster_v4(dst + (uint32_t)((c * 16 + e) * 4), r[e], r[e + 1], r[e + 2], r[e + 3]);
+        }
+      }
+      st_cluster_v4(dst + DP * 4, __float_as_uint(m_used), __float_as_uint(l), have_o ? 1u : 0u, 0u);
+    }
+    __syncwarp();
+    cluster_sync();  // release / acquire: rank 1's rows are visible in rank 0's shared memory
+    if (warp < 4 && ks == 0) {
+      const float* prow = reinterpret_cast<const float*>(sm + L::K) + row * RS;
+      const int t = tt * BQ + row;
+      const float m1 = prow[DP], l1 = prow[DP + 1];
+      const bool both = have_o && __float_as_uint(prow[DP + 2]) == 1u;
+      const float mx = fmaxf(m_used, m1);
+      const float a0 = exp2f(m_used - mx), a1 = exp2f(m1 - mx);
+      const float inv = 1.f / (l * a0 + l1 * a1);
+      const float s0 = a0 * inv, s1 = a1 * inv;
+      uint16_t* orow = a.o + (size_t)b * a.so_b + (size_t)t * a.so_t + (size_t)h * a.so_h;
+#pragma unroll
+      for (int c = 0; c < DP / 16; c++) {
+        uint32_t r[16];
+        tmem_ld16(t_row + c * 16, r);
+        tmem_ld_wait();
+        if (both && t < T) {
+#pragma unroll
+          for (int half = 0; half < 2; half++) {
+            const int d0 = c * 16 + half * 8;
+            if (d0 < a.D) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; e++) v[e] = __uint_as_float(r[8 * half + e]) * s0 + prow[d0 + e] * s1;
+              *reinterpret_cast<uint4*>(orow + d0) = make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]),
+                                                                pack_bf2(v[4], v[5]), pack_bf2(v[6], v[7]));
+            }
           }
         }
       }
@@ -372,10 +445,12 @@ int prepare_device() {
       cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
       return r == cudaSuccess ? cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) : r;
     };
-    cudaError_t r = set(attn_tc_kernel<8, 128>, Smem<8>::BYTES);
-    if (r == cudaSuccess) r = set(attn_tc_kernel<8, 64>, Smem<8>::BYTES);
-    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 128>, Smem<10>::BYTES);
-    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 64>, Smem<10>::BYTES);
+    cudaError_t r = set(attn_tc_kernel<8, 128, 1>, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<8, 64, 1>, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<8, 128, 2>, Smem<8>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 128, 1>, Smem<10>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 64, 1>, Smem<10>::BYTES);
+    if (r == cudaSuccess) r = set(attn_tc_kernel<10, 128, 2>, Smem<10>::BYTES);
     status[dev] = r;
   });
   if (status[dev] != cudaSuccess)
@@ -383,14 +458,37 @@ int prepare_device() {
   return OK;
 }
 
-template <int NC, int QR>
+// launch_k with clusters of two CTAs along x (the key split)
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pairs(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
+template <int NC, int QR, int KS>
 static int launch_nc(cudaStream_t st, Args a, int B) {
   int rc = prepare_device();
   if (rc) return rc;
   for (int b0 = 0; b0 < B; b0 += 65535) {
     a.b0 = b0;
     const int nb = (B - b0) < 65535 ? (B - b0) : 65535;
-    launch_k(attn_tc_kernel<NC, QR>, dim3(a.Tt * (128 / QR), a.H, nb), THREADS, Smem<NC>::BYTES, st, a);
+    const dim3 grid(a.Tt * (128 / QR) * KS, a.H, nb);
+    if (KS == 2) launch_pairs(attn_tc_kernel<NC, QR, KS>, grid, THREADS, Smem<NC>::BYTES, st, a);
+    else launch_k(attn_tc_kernel<NC, QR, KS>, grid, THREADS, Smem<NC>::BYTES, st, a);
     rc = check_launch("vt_attn_tiles_fwd");
     if (rc) return rc;
   }
@@ -447,11 +545,23 @@ int vt_attn_tiles_fwd(cudaStream_t st, const uint16_t* tiles, uint16_t* O, int B
   if (!tiles || !O || !aligned16(tiles) || !aligned16(O) || (so_b | so_t | so_h) % 8)
     return set_error(E_SHAPE, "vt_attn_tiles_fwd: pointers / strides not 16-byte aligned");
   attn_tc::Args a{tiles, O, T, H, D, (T + 127) / 128, so_b, so_t, so_h, scale * 1.4426950408889634f, 0};
-  // fewer 128-query CTAs than two per SM (one TAPNext frame: 10 tiles x 12 heads): 64-query CTAs (M = 64 MMAs),
-  // so that two share each SM and hide each other's MMA chain (config 3 1.220 -> 1.211 ms per frame)
-  const bool half = (long long)a.Tt * H * B < 2LL * sm_count();
-  if (attn_tc::dp_chunks(D) == 8) return half ? attn_tc::launch_nc<8, 64>(st, a, B) : attn_tc::launch_nc<8, 128>(st, a, B);
-  return half ? attn_tc::launch_nc<10, 64>(st, a, B) : attn_tc::launch_nc<10, 128>(st, a, B);
+  // Fewer 128-query CTAs than two per SM: with 16 or more key tiles (a TAPNext frame: 10 query tiles x 12 heads,
+  // 20 key tiles) the keys of each query tile split over a cluster of two CTAs (16.0 against 19.8 us per
+  // launch; config 3 1.19 -> 1.15 ms per frame); with fewer (one or two tower crops, 12 key tiles: the merge
+  // costs more than the shorter chain saves, 15.4 against 13.5 us for one crop) or with VT_ATTN_KSPLIT=0 (A/B
+  // switch), 64-query CTAs (M = 64 MMAs), so that two share each SM (config 3 1.220 -> 1.211 ms per frame against
+  // 128-query CTAs)
+  static const int ksplit = [] {
+    const char* e = getenv("VT_ATTN_KSPLIT");
+    return e ? atoi(e) : 1;
+  }();
+  const bool few = (long long)a.Tt * H * B < 2LL * sm_count();
+  const bool split = few && ksplit && (T + 63) / 64 >= 16;
+  if (attn_tc::dp_chunks(D) == 8)
+    return split ? attn_tc::launch_nc<8, 128, 2>(st, a, B)
+                 : few ? attn_tc::launch_nc<8, 64, 1>(st, a, B) : attn_tc::launch_nc<8, 128, 1>(st, a, B);
+  return split ? attn_tc::launch_nc<10, 128, 2>(st, a, B)
+               : few ? attn_tc::launch_nc<10, 64, 1>(st, a, B) : attn_tc::launch_nc<10, 128, 1>(st, a, B);
 }
 
 }  // extern "C"

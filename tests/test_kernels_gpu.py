@@ -322,6 +322,27 @@ def test_attention_many_items_each_within_tolerance(B, H, T, D):
     assert float((e / r).max()) < 1e-2
 
 
+@pytest.mark.parametrize("B,H,T,D,scale", [(1, 12, 1280, 64, 1.0), (1, 4, 1100, 72, 6.0), (2, 2, 1025, 64, 1.0),
+                                           (1, 3, 1500, 80, 3.0)])
+def test_attention_key_split_each_item_within_tolerance(B, H, T, D, scale):
+    """Grids of fewer than two query-tile CTAs per SM with 16 or more key tiles: the keys of each query tile are
+    split over a cluster of two CTAs and rank 0 merges the halves (each half's unnormalised O rescaled by
+    2^(m_half - m)).  Even and odd key-tile counts, a partial last key tile (T = 1025: one key), head_dim 64 / 72 /
+    80, and scaled logits whose row maxima differ between the halves; the error is checked per (crop, head,
+    query tile)."""
+    qkv = (torch.randn(B, T, 3 * H * D, device=DEV) * scale).to(BF)
+    q, k, v = [t.view(B, T, H, D).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
+    out = ops.VtAttn(H, T, D)(q, k, v).float().view(B, T, H, D)
+    ref = _attn_ref(q, k, v).transpose(1, 2).float()
+    Tt = (T + 127) // 128
+    pad = Tt * 128 - T
+    e = F.pad((out - ref).transpose(1, 2), (0, 0, 0, pad)).reshape(B, H, Tt, 128 * D).norm(dim=-1)
+    r = F.pad(ref.transpose(1, 2), (0, 0, 0, pad)).reshape(B, H, Tt, 128 * D).norm(dim=-1)
+    assert B * H * Tt < 2 * torch.cuda.get_device_properties(0).multi_processor_count and (T + 63) // 64 >= 16
+    assert torch.isfinite(out).all()
+    assert float((e / r).max()) < 1e-2
+
+
 def test_attention_fused_qkv_tiles_match_pack_path():
     """QKV GEMM writing attention tiles == separate GEMM + pack (bit-exact: same GEMM rows)."""
     B, H, T, D, K = 2, 16, 729, 72, 1152
