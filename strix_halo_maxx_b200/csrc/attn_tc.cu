@@ -338,9 +338,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
   }
   if constexpr (KS == 2) {
     // every MMA of both CTAs is complete and every load has landed: rank 0's K / V ring takes rank 1's rows
-    // (row i: DP floats of O, then m, l, a valid flag) while rank 0 still holds its own O in tensor memory
-    constexpr int RS = DP + 4;  // floats per row
-    static_assert(128 * RS * 4 <= L::BAR - L::K, "the merge buffer must fit in the K / V ring");
+    // while rank 0 still holds its own O in tensor memory.  16-byte chunk q of row i (O columns 4q .. 4q+3; chunk
+    // DP/4 = m, l, a valid flag) sits at (q * 128 + i) * 16 bytes, so a warp's 32 rows fill 512 consecutive bytes
+    // (no bank conflicts on either side)
+    constexpr int NQ = DP / 4 + 1;  // 16-byte chunks per row
+    static_assert(NQ * 128 * 16 <= L::BAR - L::K, "the merge buffer must fit in the K / V ring");
     const uint32_t rx = smem_u32(sm + L::K);
     const int row = warp * 32 + lane;
     const uint32_t t_row = t_o + ((uint32_t)(warp * 32) << 16);
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
     __syncthreads();
     cluster_sync();
     if (warp < 4 && ks == 1) {
-      const uint32_t dst = mapa_shared(rx + (uint32_t)(row * RS * 4), 0);
+      const uint32_t dst = mapa_shared(rx + (uint32_t)(row * 16), 0);
       if (have_o) {
 #pragma unroll
         for (int c = 0; c < DP / 16; c++) {
@@ -356,18 +358,20 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           tmem_ld16(t_row + c * 16, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; e += 4) st_cluster_v4(dst + (uint32_t)((c * 16 + e) * 4), r[e], r[e + 1], r[e + 2], r[e + 3]);
+          for (int e = 0; e < 16; e += 4)
+            st_cluster_v4(dst + (uint32_t)((c * 4 + e / 4) * 2048), r[e], r[e + 1], r[e + 2], r[e + 3]);
         }
       }
-      st_cluster_v4(dst + DP * 4, __float_as_uint(m_used), __float_as_uint(l), have_o ? 1u : 0u, 0u);
+      st_cluster_v4(dst + (uint32_t)((NQ - 1) * 2048), __float_as_uint(m_used), __float_as_uint(l), have_o ? 1u : 0u, 0u);
     }
     __syncwarp();
     cluster_sync();  // release / acquire: rank 1's rows are visible in rank 0's shared memory
     if (warp < 4 && ks == 0) {
-      const float* prow = reinterpret_cast<const float*>(sm + L::K) + row * RS;
+      const float4* prow = reinterpret_cast<const float4*>(sm + L::K) + row;  // chunk q at prow[q * 128]
       const int t = tt * BQ + row;
-      const float m1 = prow[DP], l1 = prow[DP + 1];
-      const bool both = have_o && __float_as_uint(prow[DP + 2]) == 1u;
+      const float4 ml = prow[(NQ - 1) * 128];
+      const float m1 = ml.x, l1 = ml.y;
+      const bool both = have_o && __float_as_uint(ml.z) == 1u;
       const float mx = fmaxf(m_used, m1);
       const float a0 = exp2f(m_used - mx), a1 = exp2f(m1 - mx);
       const float inv = 1.f / (l * a0 + l1 * a1);
@@ -383,9 +387,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(Args a) {
           for (int half = 0; half < 2; half++) {
             const int d0 = c * 16 + half * 8;
             if (d0 < a.D) {
+              const float4 p0 = prow[(d0 / 4) * 128], p1 = prow[(d0 / 4 + 1) * 128];
+              const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
               float v[8];
 #pragma unroll
-              for (int e = 0; e < 8; e++) v[e] = __uint_as_float(r[8 * half + e]) * s0 + prow[d0 + e] * s1;
+              for (int e = 0; e < 8; e++) v[e] = __uint_as_float(r[8 * half + e]) * s0 + pv[e] * s1;
               *reinterpret_cast<uint4*>(orow + d0) = make_uint4(pack_bf2(v[0], v[1]), pack_bf2(v[2], v[3]),
                                                                 pack_bf2(v[4], v[5]), pack_bf2(v[6], v[7]));
             }
@@ -546,11 +552,12 @@ int vt_attn_tiles_fwd(cudaStream_t st, const uint16_t* tiles, uint16_t* O, int B
     return set_error(E_SHAPE, "vt_attn_tiles_fwd: pointers / strides not 16-byte aligned");
   attn_tc::Args a{tiles, O, T, H, D, (T + 127) / 128, so_b, so_t, so_h, scale * 1.4426950408889634f, 0};
   // Fewer 128-query CTAs than two per SM: with 16 or more key tiles (a TAPNext frame: 10 query tiles x 12 heads,
-  // 20 key tiles) the keys of each query tile split over a cluster of two CTAs (16.0 against 19.8 us per
-  // launch; config 3 1.19 -> 1.15 ms per frame); with fewer (one or two tower crops, 12 key tiles: the merge
-  // costs more than the shorter chain saves, 15.4 against 13.5 us for one crop) or with VT_ATTN_KSPLIT=0 (A/B
-  // switch), 64-query CTAs (M = 64 MMAs), so that two share each SM (config 3 1.220 -> 1.211 ms per frame against
-  // 128-query CTAs)
+  // 20 key tiles) the keys of each query tile split over a cluster of two CTAs (14.3 against 19.7 us per launch);
+  // else, or with VT_ATTN_KSPLIT=0 (A/B switch), 64-query CTAs (M = 64 MMAs), so that two share each SM (config 3
+  // 1.220 -> 1.211 ms per frame against 128-query CTAs).  The split would also be faster for one or two tower crops
+  // (13.2 / 21.3 against 13.6 / 23.5 us) and the text prefill (18.9 against 22.0 us), but it sums a row in another
+  // order than the unsplit kernel, and tower crops (12 key tiles) must give the same bits whatever batch they run
+  // in (a 130-crop chunk, a 13-crop frame, a frame sharded over GPUs), so the choice never splits them
   static const int ksplit = [] {
     const char* e = getenv("VT_ATTN_KSPLIT");
     return e ? atoi(e) : 1;
