@@ -1145,15 +1145,6 @@ static bool pair_mode2_ok(const Epi& ep, int N, int K) {
          (!ep.out2 || ep.ldo2 % 8 == 0);
 }
 
-template <int MODE, bool I8, int PBN>
-static void pair_attr(int dev) {
-  static bool done[64] = {false};
-  if (dev >= 0 && dev < 64 && !done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<MODE, I8, PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         PairCfg<MODE, PBN>::SMEM_BYTES);
-    done[dev] = true;
-  }
-}
 
 // K-major operand tensor maps: bf16 with 64-element boxes, or int8 with 128-element ones (128 bytes either way).
 static int make_tmap_op(CUtensorMap* m, const void* p, int K, int rows, long long ld, int box_rows, bool i8) {
@@ -1165,9 +1156,9 @@ template <int MODE, bool I8, int PBN>
 static void launch_pair_mode(cudaStream_t st, int clusters, const CUtensorMap& ta, const CUtensorMap& tb,
                              const CUtensorMap& tr, const CUtensorMap& to, const CUtensorMap& to2, int M, int N, int K,
                              const Epi& ep) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  pair_attr<MODE, I8, PBN>(dev);
+  // a failure here leaves the kernel's default shared-memory limit, so the launch below fails and check_launch
+  // reports it
+  smem_attr_once((const void*)gemm_bf16_tc_pair_kernel<MODE, I8, PBN>, PairCfg<MODE, PBN>::SMEM_BYTES, "vt_gemm");
   launch_k(gemm_bf16_tc_pair_kernel<MODE, I8, PBN>, 2 * clusters, THREADS, PairCfg<MODE, PBN>::SMEM_BYTES, st, ta, tb,
            tr, to, to2, M, N, K, ep);
 }
@@ -1248,14 +1239,8 @@ static int launch_bn(cudaStream_t st, const void* A, long long lda, const void* 
   if (rc) return rc;
   rc = make_tmap_op(&tb, W, K, N, ldw, BN, I8);
   if (rc) return rc;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Cfg<BN>::SMEM_BYTES);
-    attr_done[dev] = true;
-  }
+  rc = smem_attr_once((const void*)gemm_bf16_tc_kernel<BN, I8>, Cfg<BN>::SMEM_BYTES, "vt_gemm");
+  if (rc) return rc;
   const long long ntiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   ep.ksplit = (BN == 64 && ep.sk_ws) ? split_k(ntiles, K, I8 ? 2 * BK : BK) : 1;  // <= kMaxSplit
   const long long units = ntiles * ep.ksplit;

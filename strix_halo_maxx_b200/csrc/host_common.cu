@@ -4,7 +4,10 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "vt_common.cuh"
 #include "vt_host.h"
@@ -28,16 +31,33 @@ int check_launch(const char* what) {
 }
 
 int sm_count() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];  // zero-initialised (static storage); 0 = not looked up yet
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
+  int c = cache[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    c = n > 0 ? n : 148;
+    cache[dev].store(c, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return c;
+}
+
+int smem_attr_once(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(E_LAUNCH, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return set_error(E_LAUNCH, "%s: setting %d bytes of dynamic shared memory: %s", what, bytes, cudaGetErrorString(e));
+  done.insert({kernel, dev});
+  return OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -198,14 +198,9 @@ int vt_attn_causal(cudaStream_t st, const uint16_t* q, const uint16_t* kc, const
     return set_error(E_SHAPE, "vt_attn_causal: null pointer, pitch or alignment invalid");
   if (H > 65535 || (n + text::QG - 1) / text::QG > 65535)
     return set_error(E_SHAPE, "vt_attn_causal: grid too large (H=%d, n=%d)", H, n);
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(text::attn_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         text::causal_smem_floats(text::MAX_CTX) * 4);
-    attr_done[dev] = true;
-  }
+  const int arc = smem_attr_once((const void*)text::attn_causal_kernel, text::causal_smem_floats(text::MAX_CTX) * 4,
+                                 "vt_attn_causal");
+  if (arc) return arc;
   const int nkp = (pos0 + n + 3) & ~3;  // row pitch of the score rows (floats), 16-byte multiple
   launch_k(text::attn_causal_kernel, dim3(H, (n + text::QG - 1) / text::QG), text::CT, text::causal_smem_floats(nkp) * 4, st, 
       q, kc, vc, n, H, pos0, ctx, nkp, scale, out, ldo);

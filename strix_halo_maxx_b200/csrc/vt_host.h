@@ -33,6 +33,9 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
 }
 int check_launch(const char* what);              // maps cudaGetLastError() to E_LAUNCH
+// Sets a kernel's maximum dynamic shared memory on the current device the first time (kernel, device) is seen;
+// safe to call from several host threads at once; E_LAUNCH with the CUDA error's message if it fails.
+int smem_attr_once(const void* kernel, int bytes, const char* what);
 int sm_count();                                  // SMs of the current device (cached per device)
 bool aligned16(const void* p);
 
