@@ -672,6 +672,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       float mu = 0.f, rstd = 1.f, sa = 1.f;
       ln_row_factors(ep, m, M, nt == 0 && half == 0, mu, rstd);  // before the wait: overlaps the tile's MMAs
       if (I8 && m < M) sa = ep.i8_sa[m];
+      // 64-wide tiles without split K (one 32-column chunk per warp and tile; the small-M GEMMs, often one tile
+      // per CTA): the chunk's residual is loaded before the accumulator wait, so its latency overlaps the MMAs
+      // instead of following them
+      const bool pre = CH == 1 && ks_n == 1;
+      uint32_t rw[32];
+      if (pre) res_load(rw, m, nt * BN + half * 32, M, N, ep);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ST_GEMM_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -732,7 +738,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           *cnt = 0;
         }
         if constexpr (I8) i8_row_scale(r, sa);
-        epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
+        if (pre) epilogue_chunk_rw<true>(r, rw, m, M, n0, N, ep, mu, rstd);
+        else epilogue_chunk(r, m, M, n0, N, ep, mu, rstd);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
