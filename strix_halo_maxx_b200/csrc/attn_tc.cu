@@ -12,8 +12,9 @@
 // vt_attn_pack builds it from any strided Q/K/V.
 //
 // CTA = one 128-query tile of one (crop, head), or one 64-query half of it (QR = 64, M = 64 MMAs, for grids of
-// fewer than two 128-query CTAs per SM: the accumulator rows then sit in lanes 0-15 of each TMEM lane quarter,
-// lanes 16-31 of every warp carry no row), 2 CTAs per SM; 6 warps:
+// fewer than two 128-query CTAs per SM and fewer than 16 key tiles: the accumulator rows then sit in lanes 0-15
+// of each TMEM lane quarter, lanes 16-31 of every warp carry no row; with 16 or more key tiles such grids split
+// the keys instead, KS = 2 below), 2 CTAs per SM; 6 warps:
 //   warp 4 lane 0: bulk loads (Q once, then K_j and V_j per 64-key tile, KVS-stage rings);
 //   warp 5 lane 0: tcgen05.mma  S_j = Q K_j^T (M 128, N 64, K DP) into one of two TMEM S buffers, then
 //                  O += P_j V_j (M 128, N DP, K 64; P read from TMEM, V an MN-major B operand in shared
