@@ -168,7 +168,9 @@ int vt_attn_pack(cudaStream_t stream, const uint16_t* Q, const uint16_t* K, cons
                  long long sk_t, long long sk_h, long long sv_b, long long sv_t, long long sv_h);
 
 /* tcgen05 flash attention from attention tiles: O[b,t,h,:D] = softmax(Q K^T * scale) V, S, P and O in TMEM;
- * O element (b,t,h,d) at O + b*so_b + t*so_t + h*so_h + d (strides multiples of 8).
+ * O element (b,t,h,d) at O + b*so_b + t*so_t + h*so_h + d (strides multiples of 8).  Grids of fewer than two
+ * 128-query tiles per SM with T > 960 split each query tile's keys over a cluster of two CTAs (results equal
+ * within rounding, deterministic); for T <= 960 a row's result does not depend on B.
  * Replaces: attn_fwd2, moondream/gpu/hip/attn.hip:442 (hattn.Attn.__call__, hattn.py:26-37). */
 int vt_attn_tiles_fwd(cudaStream_t stream, const uint16_t* tiles, uint16_t* O, int B, int T, int H, int D,
                       long long so_b, long long so_t, long long so_h, float scale);
